@@ -1,0 +1,151 @@
+"""The reference's own FP32 CPU path: Hugging Face ``LlamaForCausalLM`` eager.
+
+TEST INFRASTRUCTURE ONLY -- used by ``tests/`` to build seeded models, by
+``__graft_entry__.smoke()`` and by ``bench.py``'s ``cpu_baseline`` and
+``--impl reference`` legs as the timed CPU baseline.  Never imported by the
+product.
+
+Flux's FP32 reference path is the transformers eager model loaded by
+``flux/model/smollm2.py:25-36`` and driven as ``benchmarks/benchmark_flux.py:
+533-564`` (``model(input_ids=tok, past_key_values=cache, use_cache=True,
+logits_to_keep=1)``).  The real SmolLM2 checkpoint is not available offline, so
+the models here use the same architecture with seeded random init (HF default
+N(0, 0.02) linear/embedding init, unit norms), tied embeddings and RoPE theta
+1e5, as the benchmark configuration specifies.
+"""
+
+from __future__ import annotations
+
+import os
+import time
+
+import numpy as np
+import torch
+from transformers import DynamicCache, LlamaConfig, LlamaForCausalLM
+
+from oracle import smollm2
+
+
+def smollm2_config(vocab_size: int = 49152, max_positions: int = 8320, layers: int = 30) -> LlamaConfig:
+    """SmolLM2-135M geometry (30 x 576, MLP 1536, 9/3 heads x 64, tied)."""
+    config = LlamaConfig(
+        hidden_size=576, intermediate_size=1536, num_hidden_layers=layers,
+        num_attention_heads=9, num_key_value_heads=3, head_dim=64,
+        vocab_size=vocab_size, max_position_embeddings=max_positions,
+        rms_norm_eps=1e-5, rope_theta=1.0e5, tie_word_embeddings=True,
+        attention_bias=False, attention_dropout=0.0, mlp_bias=False,
+    )
+    config._attn_implementation = "eager"
+    return config
+
+
+def reference_runtime_config() -> LlamaConfig:
+    """The full-geometry, vocab-128 configuration of the reference's runtime
+    tests (``tests/test_system.py:318-335``): untied, default RoPE theta."""
+    config = LlamaConfig(
+        hidden_size=576, intermediate_size=1536, num_hidden_layers=30,
+        num_attention_heads=9, num_key_value_heads=3, head_dim=64,
+        vocab_size=128, max_position_embeddings=8192, rms_norm_eps=1e-5,
+        attention_bias=False, attention_dropout=0.0, mlp_bias=False,
+    )
+    config._attn_implementation = "eager"
+    return config
+
+
+def build_model(config: LlamaConfig, seed: int) -> LlamaForCausalLM:
+    """Seeded CPU FP32 model in eval mode (``torch.manual_seed`` then HF init)."""
+    torch.manual_seed(seed)
+    return LlamaForCausalLM(config).float().eval()
+
+
+def numpy_state(model: torch.nn.Module) -> dict[str, np.ndarray]:
+    return {k: v.detach().cpu().numpy() for k, v in model.state_dict().items()}
+
+
+def oracle_weights(model: torch.nn.Module) -> smollm2.ModelWeights:
+    layer = model.model.layers[0]
+    return smollm2.weights_from_state_dict(
+        numpy_state(model), eps=float(layer.input_layernorm.variance_epsilon),
+        scale=float(layer.self_attn.scaling))
+
+
+def rope_tables(model: torch.nn.Module, positions: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin ``[positions, 64]`` from the model's own ``rotary_emb`` exactly as
+    the reference runtime owner builds them (``flux/runtime/native_smollm2.py:
+    131-138``), on the model's device."""
+    device = model.model.embed_tokens.weight.device
+    ids = torch.arange(positions, dtype=torch.long, device=device).unsqueeze(0)
+    seed = model.model.embed_tokens.weight[:1].view(1, 1, -1)
+    with torch.inference_mode():
+        cos, sin = model.model.rotary_emb(seed, ids)
+    return cos.reshape(positions, -1).contiguous(), sin.reshape(positions, -1).contiguous()
+
+
+def synthetic_cache(config: LlamaConfig, length: int, seed: int, std: float = 1.0):
+    """Per-layer K/V ``[1, 3, length, 64]`` drawn from N(0, std^2), seeded."""
+    generator = torch.Generator().manual_seed(seed)
+    keys, values = [], []
+    for _ in range(config.num_hidden_layers):
+        keys.append(torch.randn((1, config.num_key_value_heads, length, config.head_dim), generator=generator) * std)
+        values.append(torch.randn((1, config.num_key_value_heads, length, config.head_dim), generator=generator) * std)
+    return keys, values
+
+
+def dynamic_cache(config: LlamaConfig, keys, values) -> DynamicCache:
+    cache = DynamicCache(config=config)
+    for layer, (k, v) in enumerate(zip(keys, values)):
+        cache.update(k.clone(), v.clone(), layer)
+    return cache
+
+
+def decode_step(model, token: int, cache) -> torch.Tensor:
+    """One HF eager decode step, the way the reference benchmark drives it."""
+    with torch.inference_mode():
+        out = model(input_ids=torch.tensor([[int(token)]], dtype=torch.long), past_key_values=cache,
+                    use_cache=True, logits_to_keep=1)
+    return out.logits[0, -1]
+
+
+def time_cpu_decode(model, config: LlamaConfig, context: int, steps: int, seed: int = 0,
+                    threads: int | None = None, budget_s: float = 20.0) -> dict:
+    """Time HF eager FP32 decode on the host cores at a given context.
+
+    The bounded sample: the cache is filled with ``context`` seeded synthetic
+    K/V rows per layer (a decode step's cost does not depend on the values),
+    then up to ``steps`` greedy steps are timed one by one (wall clock), stopping
+    early once ``budget_s`` is spent.  Returns ms/token (median) and the sample
+    description.
+    """
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    keys, values = synthetic_cache(config, context, seed)
+    cache = dynamic_cache(config, keys, values)
+    token = int(seed) % config.vocab_size
+    # one untimed warm-up step
+    logits = decode_step(model, token, cache)
+    token = int(torch.argmax(logits))
+    times = []
+    start_all = time.perf_counter()
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        logits = decode_step(model, token, cache)
+        token = int(torch.argmax(logits))
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - start_all > budget_s:
+            break
+    times.sort()
+    median = times[len(times) // 2]
+    return {
+        "ms_per_token": median * 1e3,
+        "steps": len(times),
+        "context": context,
+        "threads": threads,
+        "total_s": time.perf_counter() - start_all,
+    }
+
+
+__all__ = [
+    "build_model", "decode_step", "dynamic_cache", "numpy_state", "oracle_weights",
+    "reference_runtime_config", "rope_tables", "smollm2_config", "synthetic_cache",
+    "time_cpu_decode",
+]
