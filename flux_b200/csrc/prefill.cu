@@ -1,0 +1,436 @@
+// Native prompt prefill that fills the decode runtime's compact cache.
+//
+// Built only as far as the decode loop needs it (reference:
+// csrc/native_prefill_runtime/native_prefill_runtime_cuda.cu:553-665):
+// embedding gather -> 30 x (RMSNorm, QKV GEMM, RoPE + cache fill, causal
+// online-softmax attention, o_proj GEMM + residual, RMSNorm, gate/up GEMM,
+// SwiGLU, down GEMM + residual) -> final RMSNorm of the last row -> LM head
+// -> greedy token -> decode state handoff (position = prompt length,
+// generated[0] = token, step = 1).  Projections use an FP32 SIMT GEMM
+// (exact FP32 products, unlike TF32 tensor cores); the attention keeps one
+// query row per thread with the K/V tile in shared memory.
+#include "common.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <new>
+#include <string>
+
+namespace fx {
+namespace {
+
+constexpr int kGemmBM = 128, kGemmBN = 128, kGemmBK = 16, kGemmThreads = 256;
+
+// C[M, N] = A[M, K] . B[N, K]^T (+ R[M, N] when R is set).  Row-major, K % 4 == 0,
+// 16-byte aligned A and B.  128 x 128 tile, 8 x 8 outputs per thread.
+__global__ void __launch_bounds__(kGemmThreads) gemm_nt_kernel(const float* __restrict__ A,
+                                                               const float* __restrict__ B, float* __restrict__ C,
+                                                               const float* __restrict__ R, int64_t M, int64_t N,
+                                                               int64_t K) {
+    __shared__ __align__(16) float As[2][kGemmBK][kGemmBM + 4];
+    __shared__ __align__(16) float Bs[2][kGemmBK][kGemmBN + 4];
+    const int tid = threadIdx.x;
+    const int tx = tid % 16, ty = tid / 16;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kGemmBM;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kGemmBN;
+    // Loader mapping: 512 float4 per operand tile -> 2 per thread.
+    // float4 f: row = f / 4 (0..127), k4 = f % 4.
+    float4 ra[2], rb[2];
+    auto load_tiles = [&](int64_t k0) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int f = tid + i * kGemmThreads;
+            const int row = f >> 2, k4 = f & 3;
+            const int64_t kk = k0 + 4 * k4;
+            const int64_t am = m0 + row, bn = n0 + row;
+            ra[i] = (am < M && kk < K) ? __ldg(reinterpret_cast<const float4*>(A + am * K + kk))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+            rb[i] = (bn < N && kk < K) ? __ldg(reinterpret_cast<const float4*>(B + bn * K + kk))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    auto store_tiles = [&](int buf) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int f = tid + i * kGemmThreads;
+            const int row = f >> 2, k4 = f & 3;
+            As[buf][4 * k4 + 0][row] = ra[i].x;
+            As[buf][4 * k4 + 1][row] = ra[i].y;
+            As[buf][4 * k4 + 2][row] = ra[i].z;
+            As[buf][4 * k4 + 3][row] = ra[i].w;
+            Bs[buf][4 * k4 + 0][row] = rb[i].x;
+            Bs[buf][4 * k4 + 1][row] = rb[i].y;
+            Bs[buf][4 * k4 + 2][row] = rb[i].z;
+            Bs[buf][4 * k4 + 3][row] = rb[i].w;
+        }
+    };
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+    load_tiles(0);
+    store_tiles(0);
+    __syncthreads();
+    int buf = 0;
+    for (int64_t k0 = 0; k0 < K; k0 += kGemmBK) {
+        const bool more = k0 + kGemmBK < K;
+        if (more) load_tiles(k0 + kGemmBK);
+#pragma unroll
+        for (int kk = 0; kk < kGemmBK; ++kk) {
+            float a[8], b[8];
+            const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + ty * 4]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + tx * 4]);
+            a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
+            a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
+            b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
+            b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        if (more) {
+            store_tiles(buf ^ 1);
+            __syncthreads();
+            buf ^= 1;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int64_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int64_t n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+            if (n >= N) continue;
+            float v = acc[i][j];
+            if (R != nullptr) v = v + R[m * N + n];
+            C[m * N + n] = v;
+        }
+    }
+}
+
+// Fallback for K % 4 != 0 or unaligned operands: one thread per output.
+__global__ void gemm_nt_simple_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C,
+                                      const float* __restrict__ R, int64_t M, int64_t N, int64_t K) {
+    const int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (t >= M * N) return;
+    const int64_t m = t / N, n = t % N;
+    float acc = 0.0f;
+    for (int64_t k = 0; k < K; ++k) acc = fmaf(A[m * K + k], B[n * K + k], acc);
+    C[t] = R != nullptr ? acc + R[t] : acc;
+}
+
+__global__ void embedding_gather_kernel(const int64_t* __restrict__ ids, const float* __restrict__ embedding,
+                                        float* __restrict__ out, int64_t rows, int64_t vocab) {
+    const int64_t total = rows * kHidden;
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = t / kHidden, c = t % kHidden;
+        const int64_t tok = ids[r];
+        out[t] = (tok >= 0 && tok < vocab) ? embedding[tok * kHidden + c] : 0.0f;
+    }
+}
+
+// Rows [0, S) of packed QKV -> q [9, S, 64] (RoPE), K (RoPE) / V into the
+// cache rows [0, S) (native_prefill_runtime_cuda.cu:124-163).
+__global__ void prefill_rope_cache_kernel(const float* __restrict__ packed, const float* __restrict__ cos,
+                                          const float* __restrict__ sin, float* __restrict__ q,
+                                          float* __restrict__ key_cache, float* __restrict__ value_cache,
+                                          int64_t rows, int64_t capacity) {
+    const int64_t total = rows * kQKV;
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = t / kQKV;
+        const int col = static_cast<int>(t % kQKV);
+        const float* prow = packed + r * kQKV;
+        if (col < kHidden + kKVHeads * kHeadDim) {
+            const int base = (col / kHeadDim) * kHeadDim, d = col % kHeadDim;
+            const int partner = d < kHeadDim / 2 ? d + kHeadDim / 2 : d - kHeadDim / 2;
+            const float v = rope_value(prow[base + d], prow[base + partner], cos[r * kHeadDim + d],
+                                       sin[r * kHeadDim + d], d < kHeadDim / 2);
+            if (col < kHidden) {
+                q[(static_cast<int64_t>(col / kHeadDim) * rows + r) * kHeadDim + d] = v;
+            } else {
+                const int h = (col - kHidden) / kHeadDim;
+                key_cache[(static_cast<int64_t>(h) * capacity + r) * kHeadDim + d] = v;
+            }
+        } else {
+            const int u = col - kHidden - kKVHeads * kHeadDim;
+            value_cache[(static_cast<int64_t>(u / kHeadDim) * capacity + r) * kHeadDim + u % kHeadDim] = prow[col];
+        }
+    }
+}
+
+constexpr int kAttnRows = 128;  // query rows per CTA (one per thread)
+constexpr int kAttnKeys = 64;   // keys per shared-memory tile
+constexpr int kAttnSub = 16;    // keys per online-softmax update
+
+// Causal attention over the cache rows [0, S): grid (ceil(S/128), 9).
+// out is row-major [S, 576] (head h at columns [64 h, 64 h + 64)).
+__global__ void __launch_bounds__(kAttnRows) prefill_attention_kernel(const float* __restrict__ q,
+                                                                      const float* __restrict__ key_cache,
+                                                                      const float* __restrict__ value_cache,
+                                                                      float* __restrict__ out, int64_t rows,
+                                                                      int64_t capacity, float scale) {
+    __shared__ __align__(16) float ks[kAttnKeys][kHeadDim];
+    __shared__ __align__(16) float vs[kAttnKeys][kHeadDim];
+    const int h = blockIdx.y, g = h / kGroup;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kAttnRows;
+    const int64_t r = r0 + threadIdx.x;
+    const bool valid = r < rows;
+    float qv[kHeadDim], o[kHeadDim];
+    {
+        const float4* q4 = reinterpret_cast<const float4*>(q + (static_cast<int64_t>(h) * rows + (valid ? r : 0)) * kHeadDim);
+#pragma unroll
+        for (int j = 0; j < kHeadDim / 4; ++j) {
+            const float4 v = q4[j];
+            qv[4 * j] = v.x; qv[4 * j + 1] = v.y; qv[4 * j + 2] = v.z; qv[4 * j + 3] = v.w;
+        }
+    }
+#pragma unroll
+    for (int d = 0; d < kHeadDim; ++d) o[d] = 0.0f;
+    float m = -INFINITY, l = 0.0f;
+    const int64_t last_key = std::min<int64_t>(rows, r0 + kAttnRows);  // exclusive
+    const float* kb = key_cache + static_cast<int64_t>(g) * capacity * kHeadDim;
+    const float* vb = value_cache + static_cast<int64_t>(g) * capacity * kHeadDim;
+    for (int64_t t0 = 0; t0 < last_key; t0 += kAttnKeys) {
+        __syncthreads();
+        for (int f = threadIdx.x; f < kAttnKeys * kHeadDim / 4; f += kAttnRows) {
+            const int key = f / (kHeadDim / 4), c4 = f % (kHeadDim / 4);
+            const bool in = t0 + key < last_key;
+            const float4 kv = in ? __ldg(reinterpret_cast<const float4*>(kb + (t0 + key) * kHeadDim) + c4)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 vv = in ? __ldg(reinterpret_cast<const float4*>(vb + (t0 + key) * kHeadDim) + c4)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(&ks[key][4 * c4]) = kv;
+            *reinterpret_cast<float4*>(&vs[key][4 * c4]) = vv;
+        }
+        __syncthreads();
+        for (int j0 = 0; j0 < kAttnKeys; j0 += kAttnSub) {
+            if (t0 + j0 > r) break;  // every key of this sub-block is in the future
+            float s[kAttnSub];
+            float smax = -INFINITY;
+#pragma unroll
+            for (int jj = 0; jj < kAttnSub; ++jj) {
+                const int key = j0 + jj;
+                float dot = 0.0f;
+#pragma unroll
+                for (int d = 0; d < kHeadDim; d += 4) {
+                    const float4 k4 = *reinterpret_cast<const float4*>(&ks[key][d]);
+                    dot = fmaf(qv[d], k4.x, dot);
+                    dot = fmaf(qv[d + 1], k4.y, dot);
+                    dot = fmaf(qv[d + 2], k4.z, dot);
+                    dot = fmaf(qv[d + 3], k4.w, dot);
+                }
+                s[jj] = (t0 + key <= r) ? dot * scale : -INFINITY;
+                smax = fmaxf(smax, s[jj]);
+            }
+            const float m_new = fmaxf(m, smax);
+            const float corr = expf(m - m_new);
+            l *= corr;
+#pragma unroll
+            for (int d = 0; d < kHeadDim; ++d) o[d] *= corr;
+#pragma unroll
+            for (int jj = 0; jj < kAttnSub; ++jj) {
+                const float p = expf(s[jj] - m_new);
+                l += p;
+#pragma unroll
+                for (int d = 0; d < kHeadDim; d += 4) {
+                    const float4 v4 = *reinterpret_cast<const float4*>(&vs[j0 + jj][d]);
+                    o[d] = fmaf(p, v4.x, o[d]);
+                    o[d + 1] = fmaf(p, v4.y, o[d + 1]);
+                    o[d + 2] = fmaf(p, v4.z, o[d + 2]);
+                    o[d + 3] = fmaf(p, v4.w, o[d + 3]);
+                }
+            }
+            m = m_new;
+        }
+    }
+    if (!valid) return;
+    float4* o4 = reinterpret_cast<float4*>(out + r * kHidden + h * kHeadDim);
+    const float inv = 1.0f / l;
+#pragma unroll
+    for (int j = 0; j < kHeadDim / 4; ++j) o4[j] = make_float4(o[4 * j] * inv, o[4 * j + 1] * inv, o[4 * j + 2] * inv, o[4 * j + 3] * inv);
+}
+
+unsigned blocks_for(int64_t work) {
+    return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 148 * 32)));
+}
+
+}  // namespace
+
+fx_status launch_gemm_nt_residual(const float* a, const float* b, float* c, const float* residual, int64_t m,
+                                  int64_t n, int64_t k, cudaStream_t stream) {
+    const bool aligned = k % 4 == 0 && reinterpret_cast<uintptr_t>(a) % 16 == 0 &&
+                         reinterpret_cast<uintptr_t>(b) % 16 == 0;
+    if (aligned) {
+        const dim3 grid(static_cast<unsigned>((n + kGemmBN - 1) / kGemmBN), static_cast<unsigned>((m + kGemmBM - 1) / kGemmBM));
+        gemm_nt_kernel<<<grid, kGemmThreads, 0, stream>>>(a, b, c, residual, m, n, k);
+    } else {
+        gemm_nt_simple_kernel<<<static_cast<unsigned>((m * n + 255) / 256), 256, 0, stream>>>(a, b, c, residual, m, n, k);
+    }
+    FX_CUDA_TRY(cudaGetLastError(), "launching GEMM");
+    return FX_OK;
+}
+
+fx_status launch_gemm_nt(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
+                         cudaStream_t stream) {
+    return launch_gemm_nt_residual(a, b, c, nullptr, m, n, k, stream);
+}
+
+}  // namespace fx
+
+using namespace fx;
+
+struct fx_prefill {
+    fx_model_desc model{};
+    int64_t rows = 0;
+    fx_decode* decode = nullptr;
+    float* buffer = nullptr;
+    size_t buffer_bytes = 0;
+    float* logits = nullptr;
+    int64_t* initial_token = nullptr;
+    float *h_a, *h_b, *norm, *residual, *qkv, *q, *attn, *gate_up, *swiglu_out, *final_hidden;
+};
+
+namespace fx {
+namespace {
+
+fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
+    const fx_model_desc& m = p->model;
+    fx_decode_buffers db{};
+    fx_status st = fx_decode_get_buffers(p->decode, &db);
+    if (st != FX_OK) return st;
+    st = fx_decode_wait(p->decode, s);
+    if (st != FX_OK) return st;
+    const int64_t S = p->rows;
+    const int64_t cap = m.capacity;
+    const size_t layer_stride = static_cast<size_t>(kKVHeads) * cap * kHeadDim;
+    embedding_gather_kernel<<<blocks_for(S * kHidden), 256, 0, s>>>(ids, m.embedding, p->h_a, S, m.vocab);
+    FX_CUDA_TRY(cudaGetLastError(), "launching embedding gather");
+    for (int l = 0; l < kLayers; ++l) {
+        float* in = l % 2 == 0 ? p->h_a : p->h_b;
+        float* out = l % 2 == 0 ? p->h_b : p->h_a;
+        float* kc = db.key_cache + l * layer_stride;
+        float* vc = db.value_cache + l * layer_stride;
+        if ((st = fx_rmsnorm_f32(in, m.input_norm[l], p->norm, S, kHidden, m.epsilon, s)) != FX_OK) return st;
+        if ((st = launch_gemm_nt(p->norm, m.packed_qkv[l], p->qkv, S, kQKV, kHidden, s)) != FX_OK) return st;
+        prefill_rope_cache_kernel<<<blocks_for(S * kQKV), 256, 0, s>>>(p->qkv, m.rope_cos, m.rope_sin, p->q, kc, vc,
+                                                                       S, cap);
+        FX_CUDA_TRY(cudaGetLastError(), "launching prefill RoPE/cache fill");
+        const dim3 agrid(static_cast<unsigned>((S + kAttnRows - 1) / kAttnRows), kQHeads);
+        prefill_attention_kernel<<<agrid, kAttnRows, 0, s>>>(p->q, kc, vc, p->attn, S, cap, m.attention_scale[l]);
+        FX_CUDA_TRY(cudaGetLastError(), "launching prefill attention");
+        // residual = attn . Wo^T + in; norm = rmsnorm(residual)
+        if ((st = launch_gemm_nt_residual(p->attn, m.o_proj[l], p->residual, in, S, kHidden, kHidden, s)) != FX_OK)
+            return st;
+        if ((st = fx_rmsnorm_f32(p->residual, m.post_norm[l], p->norm, S, kHidden, m.epsilon, s)) != FX_OK) return st;
+        if ((st = launch_gemm_nt(p->norm, m.gate_up[l], p->gate_up, S, kGateUp, kHidden, s)) != FX_OK) return st;
+        if ((st = fx_packed_swiglu_f32(p->gate_up, p->swiglu_out, S, kInter, s)) != FX_OK) return st;
+        if ((st = launch_gemm_nt_residual(p->swiglu_out, m.down[l], out, p->residual, S, kHidden, kInter, s)) != FX_OK)
+            return st;
+    }
+    const float* last = p->h_a + (S - 1) * kHidden;  // 30 layers end in h_a
+    if ((st = fx_rmsnorm_f32(last, m.final_norm, p->final_hidden, 1, kHidden, m.epsilon, s)) != FX_OK) return st;
+    if ((st = fx_linear_f32(p->final_hidden, m.lm_head, p->logits, 1, kHidden, m.vocab, s)) != FX_OK) return st;
+    if ((st = fx_greedy_argmax_f32(p->logits, m.vocab, p->initial_token, s)) != FX_OK) return st;
+    return fx_decode_install_prefill(p->decode, p->initial_token, S, s);
+}
+
+void prefill_release(fx_prefill* p) {
+    if (p == nullptr) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(p->model.device);
+    if (p->decode != nullptr) fx_decode_destroy(p->decode);  // waits for pending work
+    cudaFree(p->buffer);
+    cudaFree(p->logits);
+    cudaFree(p->initial_token);
+    if (prev >= 0) cudaSetDevice(prev);
+    delete p;
+}
+
+fx_status prefill_create_impl(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
+    const int64_t S = p->rows;
+    const size_t counts[] = {static_cast<size_t>(S) * kHidden, static_cast<size_t>(S) * kHidden,
+                             static_cast<size_t>(S) * kHidden, static_cast<size_t>(S) * kHidden,
+                             static_cast<size_t>(S) * kQKV,    static_cast<size_t>(S) * kHidden,
+                             static_cast<size_t>(S) * kHidden, static_cast<size_t>(S) * kGateUp,
+                             static_cast<size_t>(S) * kInter,  static_cast<size_t>(kHidden)};
+    size_t total = 0;
+    for (size_t c : counts) total += (c + 63) / 64 * 64;
+    p->buffer_bytes = total * sizeof(float);
+    FX_CUDA_TRY(cudaMalloc(&p->buffer, p->buffer_bytes), "allocating prefill workspace");
+    FX_CUDA_TRY(cudaMalloc(&p->logits, p->model.vocab * sizeof(float)), "allocating prefill logits");
+    FX_CUDA_TRY(cudaMalloc(&p->initial_token, sizeof(int64_t)), "allocating prefill token");
+    float** views[] = {&p->h_a, &p->h_b, &p->norm, &p->residual, &p->qkv, &p->q, &p->attn, &p->gate_up,
+                       &p->swiglu_out, &p->final_hidden};
+    float* cursor = p->buffer;
+    for (int i = 0; i < 10; ++i) {
+        *views[i] = cursor;
+        cursor += (counts[i] + 63) / 64 * 64;
+    }
+    FX_CUDA_TRY(cudaMemsetAsync(p->initial_token, 0, sizeof(int64_t), s), "initializing decode token");
+    fx_status st = fx_decode_create(&p->model, p->initial_token, nullptr, nullptr, 0, 0, s, &p->decode);
+    if (st != FX_OK) return st;
+    return prefill_run(p, ids, s);
+}
+
+}  // namespace
+}  // namespace fx
+
+extern "C" fx_status fx_prefill_create(const fx_model_desc* model, const int64_t* input_ids, int64_t prompt_length,
+                                       void* stream, fx_prefill** out) {
+    FX_REQUIRE(out != nullptr && model != nullptr && input_ids != nullptr, "fx_prefill_create: null pointer");
+    *out = nullptr;
+    FX_REQUIRE(prompt_length >= 1 && prompt_length <= model->capacity,
+               "flux native prefill: prompt length must be in [1, capacity]");
+    fx_prefill* p = new (std::nothrow) fx_prefill();
+    FX_REQUIRE(p != nullptr, "flux native prefill: out of host memory");
+    p->model = *model;
+    p->rows = prompt_length;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(model->device);
+    const fx_status st = prefill_create_impl(p, input_ids, as_stream(stream));
+    if (prev >= 0) cudaSetDevice(prev);
+    if (st != FX_OK) {
+        const std::string message = fx_last_error();
+        prefill_release(p);
+        set_error(message);
+        return st;
+    }
+    *out = p;
+    return FX_OK;
+}
+
+extern "C" fx_status fx_prefill_run(fx_prefill* p, const int64_t* input_ids, void* stream) {
+    FX_REQUIRE(p != nullptr && input_ids != nullptr, "fx_prefill_run: null pointer");
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(p->model.device);
+    const fx_status st = prefill_run(p, input_ids, as_stream(stream));
+    if (prev >= 0) cudaSetDevice(prev);
+    return st;
+}
+
+extern "C" fx_decode* fx_prefill_decode(fx_prefill* p) { return p == nullptr ? nullptr : p->decode; }
+
+extern "C" fx_status fx_prefill_get_buffers(const fx_prefill* p, fx_prefill_buffers* out) {
+    FX_REQUIRE(p != nullptr && out != nullptr, "fx_prefill_get_buffers: null pointer");
+    out->prefill_logits = p->logits;
+    out->workspace = p->buffer;
+    out->workspace_bytes = static_cast<int64_t>(p->buffer_bytes);
+    out->attention_output = p->attn;
+    out->final_hidden = p->final_hidden;
+    out->initial_token = p->initial_token;
+    return FX_OK;
+}
+
+extern "C" int64_t fx_prefill_prompt_length(const fx_prefill* p) { return p == nullptr ? 0 : p->rows; }
+
+extern "C" void fx_prefill_destroy(fx_prefill* p) { prefill_release(p); }

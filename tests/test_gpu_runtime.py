@@ -1,0 +1,219 @@
+"""GPU parity of the native decode / prefill runtimes against the reference's
+FP32 path (goldens) and the numpy oracle (behaviour spec: the reference's
+``tests/test_system.py:318-497`` and ``csrc/tests/test_native_runtimes.cu``)."""
+
+from __future__ import annotations
+
+import copy
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import hf_reference as hf
+from oracle import smollm2 as o
+from tests.golden import inputs as gi
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 2e-4, 2e-5  # tests/test_system.py:30-31
+LOGIT_TOL = 1e-4         # the 1e-4 abs / rel logits bar for the benchmark geometry
+
+
+def np32(t):
+    return t.detach().reshape(-1).cpu().numpy().astype(np.float32)
+
+
+def flux_model(cpu_model):
+    from flux_b200.integration import FINAL_FLUX_OPERATOR_CATEGORIES, enable_flux_ops
+    model = copy.deepcopy(cpu_model).to("cuda")
+    return enable_flux_ops(model, operators=FINAL_FLUX_OPERATOR_CATEGORIES)
+
+
+@pytest.fixture(scope="module")
+def tiny_flux(tiny30_model):
+    return flux_model(tiny30_model)
+
+
+@pytest.fixture(scope="module")
+def smollm2_flux(smollm2_model):
+    return flux_model(smollm2_model)
+
+
+def test_prefill_decode_matches_reference_and_caches(tiny_flux, tiny30_golden):
+    from flux_b200.runtime import NativeSmolLM2Prefill
+    g = tiny30_golden
+    ids = gi.tiny30_ids(17).cuda()
+    with torch.inference_mode():
+        native = NativeSmolLM2Prefill.capture(tiny_flux, ids, max_decode_steps=3)
+    np.testing.assert_allclose(np32(native.logits), g["prefill17_logits"], rtol=RTOL, atol=ATOL)
+    assert native.prompt_length == native.cache_position == native.cache_length == 17
+    assert native.key_cache.shape == native.value_cache.shape == (30, 1, 3, 20, 64)
+    token = int(torch.argmax(native.logits))
+    assert token == g["steps3_tokens"][0]
+    for step in range(3):
+        logits = native.replay(torch.tensor([[token]], device="cuda"))
+        np.testing.assert_allclose(np32(logits), g["steps3_logits"][step], rtol=RTOL, atol=ATOL)
+        token = int(torch.argmax(logits))
+        assert token == g["steps3_tokens"][step + 1]
+        assert native.cache_position == native.cache_length == 18 + step
+    keys = native.key_cache[:, 0].double()
+    values = native.value_cache[:, 0].double()
+    np.testing.assert_allclose(keys.sum(dim=(1, 2, 3)).cpu().numpy(), g["cache20_key_sums"], rtol=1e-4, atol=1e-3)
+    np.testing.assert_allclose(values.sum(dim=(1, 2, 3)).cpu().numpy(), g["cache20_value_sums"], rtol=1e-4, atol=1e-3)
+    np.testing.assert_allclose(native.key_cache[0, 0].cpu().numpy(), g["cache20_key_l0"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(native.value_cache[29, 0].cpu().numpy(), g["cache20_value_l29"], rtol=RTOL, atol=ATOL)
+    with pytest.raises(RuntimeError, match="exhausted"):
+        native.replay(torch.tensor([[token]], device="cuda"))
+
+
+def test_greedy_generation_matches_reference_exactly(tiny_flux, tiny30_golden):
+    from flux_b200.runtime import NativeSmolLM2Prefill, native_smollm2_greedy_generate
+    expected = torch.from_numpy(tiny30_golden["generate7_8"]).view(1, -1)
+    ids = gi.tiny30_ids(7).cuda()
+    with torch.inference_mode():
+        native = NativeSmolLM2Prefill.capture(tiny_flux, ids, max_decode_steps=7)
+        addresses = native.stable_addresses()
+        generated = native.generate_greedy(8)
+        actual = torch.cat((ids, generated), dim=-1).cpu()
+    assert actual.shape == (1, 15)
+    assert torch.equal(actual, expected)
+    assert torch.equal(generated[:, :1].cpu(), torch.argmax(native.prefill_logits, dim=-1).cpu())
+    assert native.cache_position == native.cache_length == 7 + 7
+    assert native.generation_step == 8
+    assert native.stable_addresses() == addresses
+    with pytest.raises(RuntimeError, match="prefill or reset"):
+        native.generate_greedy(1)
+    with torch.inference_mode():
+        native.prefill(ids)
+        repeated = native.generate_greedy(8).clone().cpu()
+    assert torch.equal(repeated, expected[:, 7:])
+    assert native.stable_addresses() == addresses
+    with torch.inference_mode():
+        full = native_smollm2_greedy_generate(tiny_flux, ids, max_new_tokens=8).cpu()
+    assert torch.equal(full, expected)
+
+
+def test_eager_flux_path_and_decode_capture(tiny30_model, tiny_flux, tiny30_golden):
+    """Eager Flux ops (HF forward with torch.ops.flux.*) then the native decode
+    captured from that eager prefill (``NativeSmolLM2Decode.capture``)."""
+    from flux_b200.runtime import NativeSmolLM2Decode
+    g = tiny30_golden
+    ids = gi.tiny30_ids(17).cuda()
+    with torch.inference_mode():
+        out = tiny_flux(input_ids=ids, use_cache=True, logits_to_keep=1)
+    np.testing.assert_allclose(np32(out.logits), g["prefill17_logits"], rtol=RTOL, atol=ATOL)
+    with torch.inference_mode():
+        decode = NativeSmolLM2Decode.capture(tiny_flux, ids, max_decode_steps=3)
+    np.testing.assert_allclose(np32(decode.prefill_logits), g["prefill17_logits"], rtol=RTOL, atol=ATOL)
+    token = torch.argmax(decode.prefill_logits, dim=-1).view(1, 1)
+    for step in range(3):
+        logits = decode.replay(token)
+        np.testing.assert_allclose(np32(logits), g["steps3_logits"][step], rtol=RTOL, atol=ATOL)
+        token = torch.argmax(logits, dim=-1).view(1, 1)
+    token = torch.argmax(decode.prefill_logits, dim=-1).view(1, 1)
+    decode.reset(token, decode._source_key_caches, decode._source_value_caches, cache_position=17)
+    assert decode.cache_position == decode.cache_length == 17
+    np.testing.assert_allclose(np32(decode.replay(token)), g["steps3_logits"][0], rtol=RTOL, atol=ATOL)
+    with pytest.raises(RuntimeError, match="one K/V tensor per layer"):
+        decode.reset(token, decode._source_key_caches[:-1], decode._source_value_caches, cache_position=17)
+
+
+def test_prefill_reuse_and_input_errors(tiny_flux):
+    from flux_b200.runtime import NativeSmolLM2Prefill
+    first = gi.tiny30_ids(9).cuda()
+    second = (first + 7) % 128
+    native = NativeSmolLM2Prefill.capture(tiny_flux, first, max_decode_steps=1)
+    with torch.inference_mode():
+        actual = native.prefill(second).clone()
+        expected = tiny_flux(input_ids=second, use_cache=True, logits_to_keep=1)
+    np.testing.assert_allclose(np32(actual), np32(expected.logits), rtol=RTOL, atol=ATOL)
+    for layer, cache in enumerate(expected.past_key_values.layers):
+        np.testing.assert_allclose(native.key_cache[layer, ..., :9, :].cpu().numpy(), cache.keys.cpu().numpy(),
+                                   rtol=RTOL, atol=ATOL)
+    ids = gi.tiny30_ids(5).cuda()
+    with pytest.raises(ValueError, match="non-negative"):
+        NativeSmolLM2Prefill.capture(tiny_flux, ids, max_decode_steps=-1)
+    with pytest.raises(ValueError, match="batch of one"):
+        NativeSmolLM2Prefill.capture(tiny_flux, ids.expand(2, -1))
+    with pytest.raises(ValueError, match="vocabulary"):
+        NativeSmolLM2Prefill.capture(tiny_flux, torch.full_like(ids, 128))
+    native = NativeSmolLM2Prefill.capture(tiny_flux, ids)
+    with pytest.raises(ValueError, match="prompt shape"):
+        native.prefill(ids[:, :-1])
+
+
+def test_benchmark_geometry_teacher_forced(smollm2_flux, smollm2_golden):
+    """Vocab 49152, tied head: logits within 1e-4 abs/rel of the reference FP32
+    path for the prefill and four teacher-forced steps."""
+    from flux_b200.runtime import NativeSmolLM2Prefill
+    g = smollm2_golden
+    prompt = gi.uniform_prompt(128).cuda()
+    native = NativeSmolLM2Prefill.capture(smollm2_flux, prompt, max_decode_steps=4)
+    np.testing.assert_allclose(np32(native.logits), g["prompt128_forced4_logits"][0], rtol=LOGIT_TOL, atol=LOGIT_TOL)
+    for step, token in enumerate(g["forced4_tokens"]):
+        logits = native.replay(torch.tensor([[int(token)]], device="cuda"))
+        np.testing.assert_allclose(np32(logits), g["prompt128_forced4_logits"][step + 1], rtol=LOGIT_TOL,
+                                   atol=LOGIT_TOL)
+
+
+def test_synthetic_cache_decode_matches_reference(smollm2_model, smollm2_flux, smollm2_golden):
+    from flux_b200.runtime import NativeSmolLM2Decode
+    config = hf.smollm2_config()
+    keys, values = hf.synthetic_cache(config, 1000, seed=5)
+    token = torch.tensor([[17]], device="cuda")
+    decode = NativeSmolLM2Decode.capture_from_state(smollm2_flux, token, [k.cuda() for k in keys],
+                                                    [v.cuda() for v in values], cache_position=1000,
+                                                    cache_capacity=1002)
+    for step in range(2):
+        logits = decode.replay(token)
+        np.testing.assert_allclose(np32(logits), smollm2_golden["synth1000_logits"][step], rtol=LOGIT_TOL,
+                                   atol=LOGIT_TOL)
+        token = torch.argmax(logits, dim=-1).view(1, 1)
+
+
+@pytest.mark.parametrize("context", [1, 129, 2048, 8192])
+def test_long_context_decode_vs_oracle(smollm2_model, smollm2_flux, context):
+    """Decode over ``context`` synthetic rows (split-K chunking at every size up
+    to the benchmark's 8192 -> 8194) against the numpy oracle, teacher-forced."""
+    from flux_b200.runtime import NativeSmolLM2Decode
+    config = hf.smollm2_config()
+    keys, values = hf.synthetic_cache(config, context, seed=context, std=0.5)
+    capacity = context + 3
+    tokens = gi.uniform_prompt(3, seed=context)[0].tolist()
+    decode = NativeSmolLM2Decode.capture_from_state(
+        smollm2_flux, torch.tensor([[tokens[0]]], device="cuda"), [k.cuda() for k in keys],
+        [v.cuda() for v in values], cache_position=context, cache_capacity=capacity)
+    cos, sin = hf.rope_tables(smollm2_model, capacity)
+    oracle = o.Decoder(hf.oracle_weights(smollm2_model), capacity, cos.numpy(), sin.numpy())
+    oracle.load_cache([k.numpy()[0] for k in keys], [v.numpy()[0] for v in values], context)
+    for token in tokens:
+        logits = np32(decode.replay(torch.tensor([[token]], device="cuda")))
+        expected = oracle.step(token)
+        np.testing.assert_allclose(logits, expected, rtol=LOGIT_TOL, atol=LOGIT_TOL)
+        assert int(np.argmax(logits)) == o.greedy_argmax(expected)
+    assert decode.cache_position == capacity
+    # the three new cache rows match the oracle's
+    np.testing.assert_allclose(decode.key_cache[:, 0, :, context:capacity].cpu().numpy(),
+                               oracle.key_cache[:, :, context:capacity], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(decode.value_cache[:, 0, :, context:capacity].cpu().numpy(),
+                               oracle.value_cache[:, :, context:capacity], rtol=1e-4, atol=1e-5)
+
+
+def test_replay_on_non_default_stream_and_memory(tiny_flux):
+    """Replays enqueue on the caller's current stream (``test_native_runtimes.cu``
+    non-default stream case) and the memory report adds up."""
+    from flux_b200.runtime import NativeSmolLM2Prefill
+    ids = gi.tiny30_ids(5).cuda()
+    native = NativeSmolLM2Prefill.capture(tiny_flux, ids, max_decode_steps=4)
+    reference = NativeSmolLM2Prefill.capture(tiny_flux, ids, max_decode_steps=4)
+    stream = torch.cuda.Stream()
+    token = torch.argmax(native.logits, dim=-1).view(1, 1)
+    with torch.cuda.stream(stream):
+        a = native.replay(token).clone()
+    stream.synchronize()
+    b = reference.replay(token)
+    torch.testing.assert_close(a, b, rtol=0, atol=0)
+    memory = native.memory
+    assert memory.cache_bytes == 2 * 30 * 3 * 9 * 64 * 4
+    assert memory.owned_tensor_bytes > memory.cache_bytes
