@@ -149,6 +149,9 @@ def build_models(context: int, steps_total: int, seed: int):
 def run_native(args) -> dict | None:
     import torch.distributed as dist
 
+    from oracle.host import limit_threads
+    limit_threads()
+
     from flux_b200.integration import FINAL_FLUX_OPERATOR_CATEGORIES, enable_flux_ops
     from flux_b200.runtime import NativeSmolLM2Prefill
     from tests.golden.inputs import uniform_prompt
@@ -271,7 +274,8 @@ def run_native(args) -> dict | None:
 
 def cpu_baseline(cpu_model, config, ctx: int, budget_s: float = 15.0) -> dict:
     from oracle import hf_reference as hf
-    threads = os.cpu_count() or 1
+    from oracle.host import usable_cpus
+    threads = usable_cpus()
     result = hf.time_cpu_decode(cpu_model, config, ctx, steps=64, threads=threads, budget_s=budget_s)
     return {"value": round(result["ms_per_token"], 3), "unit": "ms/token", "cores": threads, "kind": "reference",
             "sample": (f"transformers LlamaForCausalLM eager FP32 decode (the reference's CPU path), "
@@ -284,8 +288,8 @@ def run_reference(args) -> dict | None:
     if rank != 0:
         return None
     from oracle import hf_reference as hf
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
+    from oracle.host import limit_threads
+    threads = limit_threads()
     K, W, ctx = args.steps, args.warmup, args.context
     config, cpu_model = build_models(ctx, W + K, args.seed)
     keys, values = hf.synthetic_cache(config, ctx, seed=args.seed)

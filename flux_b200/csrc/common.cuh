@@ -71,6 +71,17 @@ __device__ __forceinline__ float group_sum(float v) {
     return v;
 }
 
+// Sum within the aligned 8-lane group of the calling lane.  Only that group's
+// lanes need to be active (the mask names exactly them), so row groups of a
+// warp may diverge.
+__device__ __forceinline__ float group8_sum(float v) {
+    const unsigned mask = 0xFFu << ((threadIdx.x & 31) & 24);
+    v += __shfl_xor_sync(mask, v, 4);
+    v += __shfl_xor_sync(mask, v, 2);
+    v += __shfl_xor_sync(mask, v, 1);
+    return v;
+}
+
 // Block-wide sum; every thread gets the result.  `scratch` holds >= 32 floats.
 __device__ __forceinline__ float block_sum(float v, float* scratch) {
     const int lane = threadIdx.x & 31;

@@ -28,9 +28,11 @@
 // 16 lanes x 9 float4) so one warp covers a RoPE pair (d, d + 32) and the
 // rotation happens in registers.
 #include "common.cuh"
+#include "step_kernel.cuh"
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <string>
@@ -214,7 +216,7 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a) {
                 d = fmaf(q1[h].y, k1.y, d);
                 d = fmaf(q1[h].z, k1.z, d);
                 d = fmaf(q1[h].w, k1.w, d);
-                d = group_sum<8>(d);
+                d = group8_sum(d);  // row groups of a warp diverge on the chunk tail
                 if (l8 == 0) scores[h * a.chunk_max + p] = d * a.scale;
             }
         }
@@ -493,6 +495,9 @@ struct DeviceGuard {
 };
 
 }  // namespace
+
+fx_status prepare_step_kernel(int device, int* grid);
+
 }  // namespace fx
 
 using namespace fx;
@@ -503,6 +508,8 @@ struct fx_decode {
     int64_t start_position = 0, replay_count = 0;
     bool pending = false, generation_started = false, capture_active = false;
     int sms = 0, nch = 0, chunk_max = 0, lm_blocks = 0;
+    bool persistent = true;       // one cooperative launch per step (else 151 kernels)
+    int step_grid = 0;
     cudaStream_t capture_stream = nullptr;
     cudaEvent_t done = nullptr;
     cudaGraph_t graph = nullptr;
@@ -512,10 +519,11 @@ struct fx_decode {
     float* logits = nullptr;
     float* key_cache = nullptr;
     float* value_cache = nullptr;
+    float* down_t = nullptr;      // [30, 1536, 576] transposed down projections (persistent step)
     char* workspace = nullptr;
     size_t workspace_bytes = 0;
     // workspace views
-    float *h_a, *h_b, *h_mid, *q, *attn, *swiglu_out, *final_norm_out, *partials, *cand_value;
+    float *h_a, *h_b, *h_mid, *q, *attn, *swiglu_out, *final_norm_out, *partials, *cand_value, *accum;
     long long* cand_index;
     unsigned* counters;           // [3] attention + [1] lm head
     int* error;
@@ -567,6 +575,9 @@ fx_status allocate(fx_decode* r) {
     FX_CUDA_TRY(cudaMalloc(&r->logits, r->vocab * sizeof(float)), "allocating logits");
     FX_CUDA_TRY(cudaMalloc(&r->key_cache, cache * sizeof(float)), "allocating K cache");
     FX_CUDA_TRY(cudaMalloc(&r->value_cache, cache * sizeof(float)), "allocating V cache");
+    if (r->persistent)
+        FX_CUDA_TRY(cudaMalloc(&r->down_t, static_cast<size_t>(kLayers) * kInter * kHidden * sizeof(float)),
+                    "allocating transposed down projections");
     // Lay the workspace out once with a null base to size it, then for real.
     for (int pass = 0; pass < 2; ++pass) {
         char* cursor = pass == 0 ? nullptr : r->workspace;
@@ -578,6 +589,7 @@ fx_status allocate(fx_decode* r) {
         r->swiglu_out = carve<float>(cursor, kInter);
         r->final_norm_out = carve<float>(cursor, kHidden);
         r->partials = carve<float>(cursor, static_cast<size_t>(kKVHeads) * kGroup * r->nch * kPartialStride);
+        r->accum = carve<float>(cursor, static_cast<size_t>(2) * kStepReplicas * kHidden);
         r->cand_value = carve<float>(cursor, r->lm_blocks);
         r->cand_index = carve<long long>(cursor, r->lm_blocks);
         r->counters = carve<unsigned>(cursor, 8);
@@ -616,12 +628,48 @@ fx_status initialize_state(fx_decode* r, const int64_t* token, const float* cons
     set_state_kernel<<<1, 32, 0, stream>>>(r->token(), token, r->position(), r->length(), r->step(), r->generated(),
                                            position, 0, false);
     FX_CUDA_TRY(cudaGetLastError(), "initializing decode state");
+    if (r->persistent) return launch_transpose_down(r->model.down, r->down_t, stream);
     return FX_OK;
 }
 
-// Enqueue one decode step (151 kernels) on `stream`.
+// Enqueue one decode step on `stream`: one cooperative launch, or 151 kernels.
 fx_status run_body(fx_decode* r, cudaStream_t stream) {
     const fx_model_desc& m = r->model;
+    if (r->persistent) {
+        StepArgs a{};
+        for (int l = 0; l < kLayers; ++l) {
+            a.layer[l] = StepLayer{m.input_norm[l], m.packed_qkv[l], m.o_proj[l], m.post_norm[l], m.gate_up[l],
+                                   r->down_t + static_cast<size_t>(l) * kInter * kHidden, m.attention_scale[l]};
+        }
+        a.embedding = m.embedding;
+        a.final_norm = m.final_norm;
+        a.lm_head = m.lm_head;
+        a.cos_table = m.rope_cos;
+        a.sin_table = m.rope_sin;
+        a.vocab = r->vocab;
+        a.capacity = r->capacity;
+        a.eps = m.epsilon;
+        a.key_cache = r->key_cache;
+        a.value_cache = r->value_cache;
+        a.token = r->token();
+        a.position = r->position();
+        a.length = r->length();
+        a.step = r->step();
+        a.generated = r->generated();
+        a.logits = r->logits;
+        a.q = r->q;
+        a.attn = r->attn;
+        a.hidden_mid = r->h_mid;
+        a.accum = r->accum;
+        a.partials = r->partials;
+        a.final_norm_out = r->final_norm_out;
+        a.cand_value = r->cand_value;
+        a.cand_index = r->cand_index;
+        a.sync = r->counters;
+        a.error = r->error;
+        a.nch = r->nch;
+        return launch_step_kernel(a, r->step_grid, stream);
+    }
     const size_t attn_smem = static_cast<size_t>(kGroup) * r->chunk_max * sizeof(float);
     for (int l = 0; l < kLayers; ++l) {
         float* h_in = (l % 2 == 0) ? r->h_a : r->h_b;
@@ -698,6 +746,7 @@ void release(fx_decode* r) {
     cudaFree(r->logits);
     cudaFree(r->key_cache);
     cudaFree(r->value_cache);
+    cudaFree(r->down_t);
     cudaFree(r->workspace);
     delete r;
 }
@@ -710,6 +759,14 @@ fx_status create_impl(fx_decode* r, const int64_t* token, const float* const* ks
     int64_t chunk = (r->capacity + r->nch - 1) / r->nch;
     r->chunk_max = static_cast<int>(((chunk + 31) / 32) * 32);
     r->lm_blocks = std::max(1, 2 * r->sms);
+    const char* mode = std::getenv("FLUX_B200_DECODE_STEP");
+    r->persistent = !(mode != nullptr && std::strcmp(mode, "kernels") == 0);
+    if (r->persistent) {
+        const fx_status prep = prepare_step_kernel(r->model.device, &r->step_grid);
+        if (prep != FX_OK) return prep;
+        FX_REQUIRE(r->step_grid >= 60 && r->step_grid <= r->lm_blocks,
+                   "flux native decode: the persistent step needs 60 or more SMs");
+    }
     const size_t attn_smem = static_cast<size_t>(kGroup) * r->chunk_max * sizeof(float);
     if (attn_smem > 48 * 1024)
         FX_CUDA_TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -868,6 +925,10 @@ extern "C" fx_status fx_decode_install_prefill(fx_decode* r, const int64_t* toke
     set_state_kernel<<<1, 32, 0, s>>>(r->token(), token, r->position(), r->length(), r->step(), r->generated(),
                                       position, 1, true);
     FX_CUDA_TRY(cudaGetLastError(), "installing prefill state");
+    if (r->persistent) {
+        const fx_status st = launch_transpose_down(r->model.down, r->down_t, s);
+        if (st != FX_OK) return st;
+    }
     FX_CUDA_TRY(cudaEventRecord(r->done, s), "recording prefill completion");
     r->start_position = position;
     r->replay_count = 0;
@@ -927,7 +988,7 @@ extern "C" fx_status fx_decode_get_info(const fx_decode* r, fx_decode_info* out)
     out->vocab = r->vocab;
     out->start_position = r->start_position;
     out->replay_count = r->replay_count;
-    out->kernels_per_step = 5 * kLayers + 1;
+    out->kernels_per_step = r->persistent ? 1 : 5 * kLayers + 1;
     return FX_OK;
 }
 

@@ -116,8 +116,8 @@ def time_cpu_decode(model, config: LlamaConfig, context: int, steps: int, seed: 
     early once ``budget_s`` is spent.  Returns ms/token (median) and the sample
     description.
     """
-    threads = threads or os.cpu_count() or 1
-    torch.set_num_threads(threads)
+    from oracle.host import limit_threads
+    threads = limit_threads(threads)
     keys, values = synthetic_cache(config, context, seed)
     cache = dynamic_cache(config, keys, values)
     token = int(seed) % config.vocab_size

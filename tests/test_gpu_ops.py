@@ -239,9 +239,11 @@ def test_linear_c_abi_shapes(m, n, k):
     from flux_b200 import _native
     g = torch.Generator().manual_seed(m * 7 + n)
     x, w = torch.randn((m, k), generator=g), torch.randn((n, k), generator=g)
+    xd, wd = cuda(x), cuda(w)  # keep the device copies alive until the kernel has run
     out = torch.empty((m, n), device="cuda")
-    _native.check(_native.load().fx_linear_f32(cuda(x).data_ptr(), cuda(w).data_ptr(), out.data_ptr(), m, k, n,
+    _native.check(_native.load().fx_linear_f32(xd.data_ptr(), wd.data_ptr(), out.data_ptr(), m, k, n,
                                                torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
     np.testing.assert_allclose(np32(out), o.linear(x.numpy(), w.numpy()), rtol=1e-4, atol=2e-4)
 
 
