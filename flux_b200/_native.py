@@ -77,6 +77,9 @@ class DecodeBuffers(ctypes.Structure):
         ("final_norm_output", _p),
         ("attention_workspace", _p),
         ("stable_buffer_bytes", _i64),
+        ("timeline", _p),
+        ("timeline_ctas", _i64),
+        ("timeline_events", _i64),
     ]
 
 

@@ -520,6 +520,7 @@ struct fx_decode {
     float* key_cache = nullptr;
     float* value_cache = nullptr;
     float* down_t = nullptr;      // [30, 1536, 576] transposed down projections (persistent step)
+    unsigned long long* timeline = nullptr;  // optional per-CTA phase stamps (persistent step)
     char* workspace = nullptr;
     size_t workspace_bytes = 0;
     // workspace views
@@ -575,9 +576,16 @@ fx_status allocate(fx_decode* r) {
     FX_CUDA_TRY(cudaMalloc(&r->logits, r->vocab * sizeof(float)), "allocating logits");
     FX_CUDA_TRY(cudaMalloc(&r->key_cache, cache * sizeof(float)), "allocating K cache");
     FX_CUDA_TRY(cudaMalloc(&r->value_cache, cache * sizeof(float)), "allocating V cache");
-    if (r->persistent)
+    if (r->persistent) {
         FX_CUDA_TRY(cudaMalloc(&r->down_t, static_cast<size_t>(kLayers) * kInter * kHidden * sizeof(float)),
                     "allocating transposed down projections");
+        const char* timeline = std::getenv("FLUX_B200_TIMELINE");
+        if (timeline != nullptr && std::strcmp(timeline, "1") == 0) {
+            const size_t bytes = static_cast<size_t>(r->step_grid) * kStepTimelineEvents * sizeof(unsigned long long);
+            FX_CUDA_TRY(cudaMalloc(&r->timeline, bytes), "allocating the step timeline");
+            FX_CUDA_TRY(cudaMemset(r->timeline, 0, bytes), "clearing the step timeline");
+        }
+    }
     // Lay the workspace out once with a null base to size it, then for real.
     for (int pass = 0; pass < 2; ++pass) {
         char* cursor = pass == 0 ? nullptr : r->workspace;
@@ -668,6 +676,7 @@ fx_status run_body(fx_decode* r, cudaStream_t stream) {
         a.sync = r->counters;
         a.error = r->error;
         a.nch = r->nch;
+        a.timeline = r->timeline;
         return launch_step_kernel(a, r->step_grid, stream);
     }
     const size_t attn_smem = static_cast<size_t>(kGroup) * r->chunk_max * sizeof(float);
@@ -747,6 +756,7 @@ void release(fx_decode* r) {
     cudaFree(r->key_cache);
     cudaFree(r->value_cache);
     cudaFree(r->down_t);
+    cudaFree(r->timeline);
     cudaFree(r->workspace);
     delete r;
 }
@@ -961,6 +971,9 @@ extern "C" fx_status fx_decode_get_buffers(const fx_decode* r, fx_decode_buffers
     out->final_norm_output = r->final_norm_out;
     out->attention_workspace = r->partials;
     out->stable_buffer_bytes = static_cast<int64_t>((4 + r->capacity) * sizeof(int64_t) + r->vocab * sizeof(float));
+    out->timeline = reinterpret_cast<uint64_t*>(r->timeline);
+    out->timeline_ctas = r->timeline != nullptr ? r->step_grid : 0;
+    out->timeline_events = r->timeline != nullptr ? kStepTimelineEvents : 0;
     return FX_OK;
 }
 

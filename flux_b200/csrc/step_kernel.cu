@@ -49,6 +49,13 @@ __device__ __forceinline__ unsigned long long global_timer() {
     return t;
 }
 
+// Optional timeline stamp by thread 0 of each CTA.
+#define STEP_MARK(event)                                                                        \
+    do {                                                                                      \
+        if (a.timeline != nullptr && threadIdx.x == 0)                                         \
+            a.timeline[static_cast<size_t>(blockIdx.x) * kStepTimelineEvents + (event)] = global_timer(); \
+    } while (0)
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
@@ -446,6 +453,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         if (cta == 0) *a.length = s.pos + 1;
     }
     __syncthreads();
+    STEP_MARK(0);
     if (tid == 0) pump(a, s, sh, ring);
 
     int tile = 0;
@@ -492,7 +500,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             }
             release(a, s, sh, ring, tile++);
         }
+        STEP_MARK(1 + 8 * l);
         if (!grid_sync(a, s, sh, ring, barrier++)) goto abort;
+        STEP_MARK(2 + 8 * l);
 
         // -------------------------------------------------------- phase B
         if (s.g >= 0) {
@@ -610,7 +620,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 if (tid == 0) a.sync[1 + s.g] = 0u;
             }
         }
+        STEP_MARK(3 + 8 * l);
         if (!grid_sync(a, s, sh, ring, barrier++)) goto abort;
+        STEP_MARK(4 + 8 * l);
 
         // -------------------------------------------------------- phase C
         for (int i = tid; i < kHidden; i += kStepThreads) sh.xs[i] = __ldcg(a.attn + i);
@@ -630,7 +642,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             }
             release(a, s, sh, ring, tile++);
         }
+        STEP_MARK(5 + 8 * l);
         if (!grid_sync(a, s, sh, ring, barrier++)) goto abort;
+        STEP_MARK(6 + 8 * l);
 
         // -------------------------------------------------------- phase D
         norm_into(sh, [&](int i) { return __ldcg(a.hidden_mid + i); }, L.post_norm, a.eps);
@@ -660,11 +674,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             }
             release(a, s, sh, ring, tile++);
         }
+        STEP_MARK(7 + 8 * l);
         if (!grid_sync(a, s, sh, ring, barrier++)) goto abort;
+        STEP_MARK(8 + 8 * l);
     }
 
     // ------------------------------------------------------------ LM head
     {
+        STEP_MARK(1 + 8 * kLayers);
         norm_into(sh, [&](int i) { return hidden_in(a, s, kLayers, i); }, a.final_norm, a.eps);
         if (cta == 0)
             for (int i = tid; i < kHidden; i += kStepThreads) a.final_norm_out[i] = sh.xs[i];
@@ -694,6 +711,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             sh.ci[warp] = bi;
         }
         __syncthreads();
+        STEP_MARK(2 + 8 * kLayers);
         if (tid == 0) {
             for (int w = 1; w < kWarps; ++w) argmax_take(bv, bi, sh.cv[w], sh.ci[w]);
             a.cand_value[cta] = bv;

@@ -53,7 +53,13 @@ struct StepArgs {
     unsigned* sync;           // [0] grid barrier, [1..3] kv-group merge, [4] LM head
     int* error;               // bit 1: position outside capacity, bit 2: a bounded wait gave up
     int nch;                  // attention chunks per kv head
+    unsigned long long* timeline;  // optional [grid][kStepTimelineEvents] %globaltimer stamps
 };
+
+// Timeline events per CTA: 0 = start, then per layer 8 stamps (phase A done,
+// barrier 1 passed, B done, barrier 2 passed, C done, barrier 3 passed, D
+// done, barrier 4 passed), then LM-head start and end.
+constexpr int kStepTimelineEvents = 1 + 8 * kLayers + 2;
 
 // Enqueue one decode step as a single cooperative launch of `grid` CTAs.
 fx_status launch_step_kernel(const StepArgs& args, int grid, cudaStream_t stream);

@@ -194,6 +194,10 @@ typedef struct fx_decode_buffers {
     float* final_norm_output;    /* [576] */
     float* attention_workspace;  /* split-K partials */
     int64_t stable_buffer_bytes; /* token + logits + generated + step + position + length */
+    uint64_t* timeline;          /* per-CTA %globaltimer stamps of the last step, or NULL
+                                    (enabled by FLUX_B200_TIMELINE=1 at create) */
+    int64_t timeline_ctas;
+    int64_t timeline_events;     /* stamps per CTA */
 } fx_decode_buffers;
 
 /* Build the runtime, install the initial state and capture the step graph.
