@@ -122,6 +122,9 @@ SIGNATURES: dict[str, tuple] = {
     "fx_gqa_decode_attention_workspace_floats": (_i64, [_i64, _i64, _i64, _i64]),
     "fx_gqa_decode_attention_f32": (_st, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _f32,
                                           _i64, _i64, _i64, _i64, _i64, _p]),
+    "fx_gqa_decode_attention_static_scratch_floats": (_i64, []),
+    "fx_gqa_decode_attention_static_scratch_f32": (_st, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f32,
+                                                         _i64, _i64, _i64, _i64, _i64, _p]),
     "fx_packed_gate_up_swiglu_f32": (_st, [_p, _p, _p, _i64, _i64, _p]),
     "fx_linear_f32": (_st, [_p, _p, _p, _i64, _i64, _i64, _p]),
     "fx_greedy_argmax_f32": (_st, [_p, _i64, _p, _p]),

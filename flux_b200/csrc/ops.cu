@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 #include <string>
 
 namespace fx {
@@ -575,4 +576,81 @@ extern "C" fx_status fx_greedy_argmax_update_f32(const float* logits, int64_t vo
                                                            step, position, attention_length);
     FX_CUDA_TRY(cudaGetLastError(), "launching greedy argmax update");
     return FX_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free GQA decode attention.
+//
+// Some callers cannot allocate device memory: a host that reserves the whole
+// device budget for its own pool at start-up and treats any later cudaMalloc
+// as an out-of-memory risk and a device-wide synchronisation, or a plugin host
+// whose C FFI hands the plugin tensors but no allocator.  For them this entry
+// point runs fx_gqa_decode_attention_f32 with its split-K partials in a
+// fixed, file-scope device array instead of a caller-provided workspace.
+//
+// The array holds kStaticScratchFloats floats (1 MiB) and stays resident on
+// every device that loads this library until the process exits.  All calls on
+// a device share it and it keeps the last call's contents; nothing in it has
+// to start at zero (every partial the merge reads is written by the same
+// call), but two calls whose kernels overlap on the GPU (different streams
+// without ordering between them) race on it.
+//
+// The device address of the array is looked up once per device, with that
+// device current, on the first call there (cudaGetSymbolAddress); make that
+// first call before any stream capture begins.
+// ---------------------------------------------------------------------------
+
+namespace fx {
+namespace {
+
+constexpr int64_t kStaticScratchFloats = 262144;
+constexpr int kStaticScratchDevices = 64;
+
+static __device__ __align__(256) float g_gqa_static_scratch[kStaticScratchFloats];
+
+std::mutex g_static_scratch_mutex;
+float* g_static_scratch_address[kStaticScratchDevices] = {};
+
+// Device address of g_gqa_static_scratch on the current device (set-up on
+// the first call per device).
+fx_status static_scratch_address(float** out) {
+    int device = -1;
+    FX_CUDA_TRY(cudaGetDevice(&device), "querying the current device");
+    FX_REQUIRE(device >= 0 && device < kStaticScratchDevices,
+               "fx_gqa_decode_attention_static_scratch_f32: device ordinal beyond 63");
+    std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+    if (g_static_scratch_address[device] == nullptr) {
+        void* address = nullptr;
+        FX_CUDA_TRY(cudaGetSymbolAddress(&address, g_gqa_static_scratch),
+                    "looking up the static GQA scratch address");
+        g_static_scratch_address[device] = static_cast<float*>(address);
+    }
+    *out = g_static_scratch_address[device];
+    return FX_OK;
+}
+
+}  // namespace
+}  // namespace fx
+
+extern "C" int64_t fx_gqa_decode_attention_static_scratch_floats(void) { return fx::kStaticScratchFloats; }
+
+extern "C" fx_status fx_gqa_decode_attention_static_scratch_f32(
+    const float* query, const int64_t* query_strides4, const float* key_cache, const int64_t* key_strides4,
+    const float* value_cache, const int64_t* value_strides4, const float* mask, const int64_t* mask_sizes4,
+    const int64_t* mask_strides4, const int64_t* cache_length, float* output, float scale, int64_t batch,
+    int64_t query_heads, int64_t kv_heads, int64_t capacity, int64_t head_dim, void* stream) {
+    const int64_t needed = fx_gqa_decode_attention_workspace_floats(batch, query_heads, capacity, head_dim);
+    if (needed > fx::kStaticScratchFloats) {
+        fx::set_error("fx_gqa_decode_attention_static_scratch_f32: batch * query_heads * ceil(capacity / 128) * "
+                      "(head_dim + 2) = " + std::to_string(needed) + " floats of split-K scratch exceeds the " +
+                      std::to_string(fx::kStaticScratchFloats) + "-float static array");
+        return FX_ERR_INVALID;
+    }
+    float* scratch = nullptr;
+    const fx_status status = fx::static_scratch_address(&scratch);
+    if (status != FX_OK) return status;
+    return fx_gqa_decode_attention_f32(query, query_strides4, key_cache, key_strides4, value_cache, value_strides4,
+                                       mask, mask_sizes4, mask_strides4, cache_length, output, scratch,
+                                       fx::kStaticScratchFloats, scale, batch, query_heads, kv_heads, capacity,
+                                       head_dim, stream);
 }

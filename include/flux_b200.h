@@ -119,6 +119,23 @@ FX_API fx_status fx_gqa_decode_attention_f32(const float* query, const int64_t* 
                                       float scale, int64_t batch, int64_t query_heads, int64_t kv_heads,
                                       int64_t capacity, int64_t head_dim, void* stream);
 
+/* Allocation-free form of fx_gqa_decode_attention_f32 for callers that cannot
+ * allocate device memory (a host that owns the whole device budget through its
+ * own pool, or a plugin host that passes tensors but no allocator).  No
+ * counterpart in the reference.  The split-K partials live in a file-scope
+ * device array of fx_gqa_decode_attention_static_scratch_floats() floats
+ * (1 MiB), resident on every device that loads the library until exit;
+ * larger problems are rejected with FX_ERR_INVALID.  All calls on a device
+ * share the array (calls that overlap on the GPU race); the first call on a
+ * device looks up its address and should come before any stream capture.
+ * Calls no allocator. */
+FX_API int64_t fx_gqa_decode_attention_static_scratch_floats(void);
+FX_API fx_status fx_gqa_decode_attention_static_scratch_f32(
+    const float* query, const int64_t* query_strides4, const float* key_cache, const int64_t* key_strides4,
+    const float* value_cache, const int64_t* value_strides4, const float* mask, const int64_t* mask_sizes4,
+    const int64_t* mask_strides4, const int64_t* cache_length, float* output, float scale, int64_t batch,
+    int64_t query_heads, int64_t kv_heads, int64_t capacity, int64_t head_dim, void* stream);
+
 /* out[i] = silu(W[i] . x) * (W[intermediate + i] . x), W [2I, width].
  * Replaces flux::packed_gate_up_swiglu_cuda_fp32
  * (csrc/packed_gate_up_gemv/packed_gate_up_gemv_cuda.h:8-12). */
