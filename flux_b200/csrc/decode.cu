@@ -495,9 +495,6 @@ struct DeviceGuard {
 };
 
 }  // namespace
-
-fx_status prepare_step_kernel(int device, int* grid);
-
 }  // namespace fx
 
 using namespace fx;
@@ -519,14 +516,15 @@ struct fx_decode {
     float* logits = nullptr;
     float* key_cache = nullptr;
     float* value_cache = nullptr;
-    float* down_t = nullptr;      // [30, 1536, 576] transposed down projections (persistent step)
     unsigned long long* timeline = nullptr;  // optional per-CTA phase stamps (persistent step)
     char* workspace = nullptr;
     size_t workspace_bytes = 0;
     // workspace views
-    float *h_a, *h_b, *h_mid, *q, *attn, *swiglu_out, *final_norm_out, *partials, *cand_value, *accum;
+    float *h_a, *h_b, *h_mid, *q, *attn, *swiglu_out, *final_norm_out, *partials, *cand_value;
     long long* cand_index;
     unsigned* counters;           // [3] attention + [1] lm head
+    unsigned* step_sync;          // persistent step: [0] LM-head arrivals, [1] step epoch
+    StepExchange exchange{};      // persistent step: tagged cross-CTA words
     int* error;
 
     int64_t* token() const { return state; }
@@ -577,8 +575,6 @@ fx_status allocate(fx_decode* r) {
     FX_CUDA_TRY(cudaMalloc(&r->key_cache, cache * sizeof(float)), "allocating K cache");
     FX_CUDA_TRY(cudaMalloc(&r->value_cache, cache * sizeof(float)), "allocating V cache");
     if (r->persistent) {
-        FX_CUDA_TRY(cudaMalloc(&r->down_t, static_cast<size_t>(kLayers) * kInter * kHidden * sizeof(float)),
-                    "allocating transposed down projections");
         const char* timeline = std::getenv("FLUX_B200_TIMELINE");
         if (timeline != nullptr && std::strcmp(timeline, "1") == 0) {
             const size_t bytes = static_cast<size_t>(r->step_grid) * kStepTimelineEvents * sizeof(unsigned long long);
@@ -597,11 +593,13 @@ fx_status allocate(fx_decode* r) {
         r->swiglu_out = carve<float>(cursor, kInter);
         r->final_norm_out = carve<float>(cursor, kHidden);
         r->partials = carve<float>(cursor, static_cast<size_t>(kKVHeads) * kGroup * r->nch * kPartialStride);
-        r->accum = carve<float>(cursor, static_cast<size_t>(2) * kStepReplicas * kHidden);
+        unsigned long long* words = carve<unsigned long long>(cursor, step_exchange_words(r->nch));
+        r->step_sync = carve<unsigned>(cursor, 4);
         r->cand_value = carve<float>(cursor, r->lm_blocks);
         r->cand_index = carve<long long>(cursor, r->lm_blocks);
         r->counters = carve<unsigned>(cursor, 8);
         r->error = carve<int>(cursor, 4);
+        if (pass == 1) r->exchange = step_exchange_views(words, r->nch);
         if (pass == 0) {
             r->workspace_bytes = static_cast<size_t>(reinterpret_cast<uintptr_t>(cursor)) + 256;
             FX_CUDA_TRY(cudaMalloc(&r->workspace, r->workspace_bytes), "allocating decode workspace");
@@ -636,7 +634,6 @@ fx_status initialize_state(fx_decode* r, const int64_t* token, const float* cons
     set_state_kernel<<<1, 32, 0, stream>>>(r->token(), token, r->position(), r->length(), r->step(), r->generated(),
                                            position, 0, false);
     FX_CUDA_TRY(cudaGetLastError(), "initializing decode state");
-    if (r->persistent) return launch_transpose_down(r->model.down, r->down_t, stream);
     return FX_OK;
 }
 
@@ -647,7 +644,7 @@ fx_status run_body(fx_decode* r, cudaStream_t stream) {
         StepArgs a{};
         for (int l = 0; l < kLayers; ++l) {
             a.layer[l] = StepLayer{m.input_norm[l], m.packed_qkv[l], m.o_proj[l], m.post_norm[l], m.gate_up[l],
-                                   r->down_t + static_cast<size_t>(l) * kInter * kHidden, m.attention_scale[l]};
+                                   m.down[l], m.attention_scale[l]};
         }
         a.embedding = m.embedding;
         a.final_norm = m.final_norm;
@@ -665,15 +662,11 @@ fx_status run_body(fx_decode* r, cudaStream_t stream) {
         a.step = r->step();
         a.generated = r->generated();
         a.logits = r->logits;
-        a.q = r->q;
-        a.attn = r->attn;
-        a.hidden_mid = r->h_mid;
-        a.accum = r->accum;
-        a.partials = r->partials;
+        a.x = r->exchange;
         a.final_norm_out = r->final_norm_out;
         a.cand_value = r->cand_value;
         a.cand_index = r->cand_index;
-        a.sync = r->counters;
+        a.sync = r->step_sync;
         a.error = r->error;
         a.nch = r->nch;
         a.timeline = r->timeline;
@@ -755,7 +748,6 @@ void release(fx_decode* r) {
     cudaFree(r->logits);
     cudaFree(r->key_cache);
     cudaFree(r->value_cache);
-    cudaFree(r->down_t);
     cudaFree(r->timeline);
     cudaFree(r->workspace);
     delete r;
@@ -774,8 +766,9 @@ fx_status create_impl(fx_decode* r, const int64_t* token, const float* const* ks
     if (r->persistent) {
         const fx_status prep = prepare_step_kernel(r->model.device, &r->step_grid);
         if (prep != FX_OK) return prep;
-        FX_REQUIRE(r->step_grid >= 60 && r->step_grid <= r->lm_blocks,
-                   "flux native decode: the persistent step needs 60 or more SMs");
+        FX_REQUIRE(r->step_grid >= kStepMinGrid && r->step_grid <= kStepMaxGrid && r->step_grid <= r->lm_blocks &&
+                       kKVHeads * r->nch <= r->step_grid,
+                   "flux native decode: the persistent step needs a GPU with 140 to 480 SMs");
     }
     const size_t attn_smem = static_cast<size_t>(kGroup) * r->chunk_max * sizeof(float);
     if (attn_smem > 48 * 1024)
@@ -935,10 +928,6 @@ extern "C" fx_status fx_decode_install_prefill(fx_decode* r, const int64_t* toke
     set_state_kernel<<<1, 32, 0, s>>>(r->token(), token, r->position(), r->length(), r->step(), r->generated(),
                                       position, 1, true);
     FX_CUDA_TRY(cudaGetLastError(), "installing prefill state");
-    if (r->persistent) {
-        const fx_status st = launch_transpose_down(r->model.down, r->down_t, s);
-        if (st != FX_OK) return st;
-    }
     FX_CUDA_TRY(cudaEventRecord(r->done, s), "recording prefill completion");
     r->start_position = position;
     r->replay_count = 0;

@@ -203,13 +203,14 @@ class _OwnedHandle:
 
     def __init__(self, ptr: int, destroy: str, keepalive: tuple = ()):
         self.ptr = ptr
-        self._destroy = destroy
+        # Bound now: at interpreter shutdown module globals may already be gone.
+        self._destroy = getattr(_native.load(), destroy)
         self._keepalive = keepalive
 
     def __del__(self):
-        if self.ptr and _native._LIB is not None:
-            getattr(_native._LIB, self._destroy)(self.ptr)
-            self.ptr = None
+        ptr, self.ptr = self.ptr, None
+        if ptr:
+            self._destroy(ptr)
 
 
 class NativeDecodeObject:
