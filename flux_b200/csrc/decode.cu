@@ -524,7 +524,8 @@ struct fx_decode {
     long long* cand_index;
     unsigned* counters;           // [3] attention + [1] lm head
     unsigned* step_sync;          // persistent step: [0] LM-head arrivals, [1] step epoch
-    StepExchange exchange{};      // persistent step: tagged cross-CTA words
+    StepExchange exchange{};      // persistent step: cross-CTA exchange region
+    StepLayer step_layers[kLayers]{};  // persistent step: per-layer pointers and strip tensor maps
     int* error;
 
     int64_t* token() const { return state; }
@@ -642,10 +643,7 @@ fx_status run_body(fx_decode* r, cudaStream_t stream) {
     const fx_model_desc& m = r->model;
     if (r->persistent) {
         StepArgs a{};
-        for (int l = 0; l < kLayers; ++l) {
-            a.layer[l] = StepLayer{m.input_norm[l], m.packed_qkv[l], m.o_proj[l], m.post_norm[l], m.gate_up[l],
-                                   m.down[l], m.attention_scale[l]};
-        }
+        for (int l = 0; l < kLayers; ++l) a.layer[l] = r->step_layers[l];
         a.embedding = m.embedding;
         a.final_norm = m.final_norm;
         a.lm_head = m.lm_head;
@@ -768,7 +766,17 @@ fx_status create_impl(fx_decode* r, const int64_t* token, const float* const* ks
         if (prep != FX_OK) return prep;
         FX_REQUIRE(r->step_grid >= kStepMinGrid && r->step_grid <= kStepMaxGrid && r->step_grid <= r->lm_blocks &&
                        kKVHeads * r->nch <= r->step_grid,
-                   "flux native decode: the persistent step needs a GPU with 140 to 480 SMs");
+                   "flux native decode: the persistent step needs a GPU with 140 to 384 SMs");
+        for (int l = 0; l < kLayers; ++l) {
+            StepLayer& L = r->step_layers[l];
+            const fx_status enc = encode_step_maps(r->model.o_proj[l], r->model.down[l], &L);
+            if (enc != FX_OK) return enc;
+            L.input_norm = r->model.input_norm[l];
+            L.qkv = r->model.packed_qkv[l];
+            L.post_norm = r->model.post_norm[l];
+            L.gate_up = r->model.gate_up[l];
+            L.scale = r->model.attention_scale[l];
+        }
     }
     const size_t attn_smem = static_cast<size_t>(kGroup) * r->chunk_max * sizeof(float);
     if (attn_smem > 48 * 1024)

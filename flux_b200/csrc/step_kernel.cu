@@ -2,49 +2,59 @@
 //
 // One CTA per SM, 512 threads: 15 consumer warps do the math, one producer
 // warp streams weights and cache rows into a ring of 7 x 27 KB shared-memory
-// slots with 1-D TMA bulk copies (cp.async.bulk, no multicast) completing on
-// full/empty mbarrier pairs.  The producer walks the CTA's tiles in the order
-// the consumers use them and runs up to 7 tiles ahead, so HBM keeps streaming
-// while the consumers wait for values from other CTAs.
+// slots with TMA (1-D cp.async.bulk for rows, 2-D cp.async.bulk.tensor for
+// column strips; never multicast) completing on full/empty mbarrier pairs.
+// The producer walks the CTA's tiles in consumption order and runs up to 7
+// tiles ahead, so HBM keeps streaming while the consumers wait for values
+// from other CTAs.
 //
 // Each CTA owns a fixed slice of every projection and one (kv head, chunk)
-// of the attention.  Per layer, six dependent phases and no grid barrier:
+// of the attention.  Per layer four dependent steps (no grid barrier):
 //
-//   A  poll h (576); RMSNorm; its QKV row pairs; RoPE; publish q / k / v of
-//      the current row; write the K / V row into the cache.
+//   A  h = h' + sum(down partials) once every CTA has added its down
+//      partial (arrival counter); RMSNorm; its QKV row pairs; RoPE;
+//      publish q / k / v of the current row; write K / V into the cache.
 //   B  poll q of its kv head (and the new K/V row if its chunk holds it);
 //      online softmax over its chunk of cache rows for the 3 q heads;
 //      publish (m, l, o) per head.
-//   M  every attention CTA merges 3-4 of the 192 output dims of its kv head
-//      over the partials of all chunks and publishes them.
-//   C  poll attn; its o_proj rows; publish h' = h + o_proj(attn).
-//   D  poll h'; RMSNorm; its gate and up rows; publish SwiGLU.
-//   E  poll SwiGLU (1536); its down rows; publish h_next = h' + down(SwiGLU).
+//   M  poll the partials of the 4-8 attention dims it owns; merge them;
+//      multiply by those 4-8 columns of o_proj (a split-K slice of the GEMV)
+//      and add the 576 products into the fixed-point h' accumulator.
+//   D  h' = h + sum(o_proj partials) once every CTA has added; RMSNorm; its
+//      8-12 gate/up features; SwiGLU; multiply by those columns of down and
+//      add the 576 products into the fixed-point down accumulator.
 //
 // then the LM head (its vocab rows and greedy candidate; the last CTA to
 // arrive picks the token, advances the device state and the step epoch).
 //
-// Cross-CTA values travel as 64-bit words (tag << 32 | float bits): a reader
-// polls a word with relaxed gpu-scope loads until it carries the tag of the
-// current (step, layer), so one L2 round trip both waits for and delivers the
-// value.  Every wait (mbarrier or poll) is bounded by %globaltimer; on expiry
-// the CTA sets error bit 2, drains its copies in flight and returns, and the
+// The split-K sums are exact integer adds of values rounded to 2^-32, so the
+// result does not depend on the order the CTAs arrive in.  Every wait
+// (mbarrier, tagged word, counter) is bounded by %globaltimer; on expiry the
+// CTA sets error bit 2, drains its copies in flight and returns, and the
 // other CTAs give up at their next wait once they see the error word.
 #include "step_kernel.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace fx {
 namespace {
 
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait
+constexpr unsigned long long kWaitNs = 2000000000ull;    // 2 s per wait
 constexpr unsigned long long kPeerCheckNs = 1000000ull;  // look at the error word after 1 ms
-constexpr int kConsumerWarps = kStepConsumers / 32;     // 15
-constexpr int kProducerWarp = kConsumerWarps;           // warp 15
-constexpr int kRowBytes = kHidden * 4;                  // one 576-float row
-constexpr int kMaxSeg = 10;
+constexpr int kConsumerWarps = kStepConsumers / 32;      // 15
+constexpr int kProducerWarp = kConsumerWarps;            // warp 15
+constexpr int kRowBytes = kHidden * 4;                   // one 576-float row
+constexpr int kStripBytes = kStepBlock * kStepStripRows * 4;  // one 2-D box (3072 B)
+constexpr int kStripBoxes = kHidden / kStepStripRows;    // boxes per 576-row strip (3)
+constexpr int kFeatureBlocks = kInter / kStepBlock;      // 384
+constexpr int kAttnBlocks = kGroup * kHeadDim / kStepBlock;  // 48 per kv head
 constexpr int kMaxChunks = 64;
-constexpr int kMergeDims = 8;  // output dims merged per attention CTA (192 / chunks, chunks >= 24)
+constexpr int kMaxOBlocks = 2;                           // needs >= 24 chunks per kv head
+constexpr int kMaxFeatures = 12;                         // needs grid >= 128
+constexpr double kFixedToFloat = 2.3283064365386962890625e-10;  // 2^-32
+constexpr float kFloatToFixed = 4294967296.0f;                  // 2^32
+constexpr float kFixedLimit = 1073741824.0f;                    // |partial| < 2^30
 
 // ------------------------------------------------------------- PTX helpers
 
@@ -92,9 +102,37 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 
+// 2-D tensor copy of one box at (x = column, y = row) (no multicast).  x is
+// a multiple of 4 floats, so the box starts on a 16-byte boundary.
+__device__ __forceinline__ void box_load(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ unsigned long long ld_word(const unsigned long long* p) {
     unsigned long long v;
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ long long ld_fixed(const long long* p) {
+    long long v;
+    asm volatile("ld.relaxed.gpu.global.s64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned ld_flag(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
@@ -109,6 +147,18 @@ __device__ __forceinline__ void st_word(unsigned long long* p, uint32_t tag, flo
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+__device__ __forceinline__ void st_fixed(long long* p, long long v) {
+    asm volatile("st.relaxed.gpu.global.s64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ void red_fixed(long long* p, long long v) {
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ void arrive_release(unsigned long long* p) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(p) : "memory");
+}
+
 __device__ __forceinline__ uint32_t word_tag(unsigned long long v) { return static_cast<uint32_t>(v >> 32); }
 __device__ __forceinline__ float word_value(unsigned long long v) {
     return __uint_as_float(static_cast<uint32_t>(v));
@@ -119,12 +169,12 @@ __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 480;
 
 __device__ __forceinline__ int64_t min64(int64_t x, int64_t y) { return x < y ? x : y; }
 
-#define LAYER_MARK(event) STEP_MARK(1 + kStepTimelinePerLayer * l + (event))
 #define STEP_MARK(event)                                                                                  \
     do {                                                                                                  \
         if (a.timeline != nullptr && threadIdx.x == 0)                                                     \
             a.timeline[static_cast<size_t>(blockIdx.x) * kStepTimelineEvents + (event)] = global_timer(); \
     } while (0)
+#define LAYER_MARK(event) STEP_MARK(1 + kStepTimelinePerLayer * l + (event))
 
 // ------------------------------------------------------------ shared state
 
@@ -137,24 +187,23 @@ struct AttnCombine {
 struct Shared {
     uint64_t full[kStepSlots];
     uint64_t empty[kStepSlots];
-    alignas(16) float hraw[kHidden];          // layer input h (residual of phase C)
-    alignas(16) float mid[kHidden];           // h' (phase D input)
-    alignas(16) float xs[kHidden];            // normalised vector / attention output
+    alignas(16) float hraw[kHidden];          // layer input h
+    alignas(16) float mid[kHidden];           // h' (kept for the next layer's h)
+    alignas(16) float xs[kHidden];            // normalised vector
+    alignas(16) float wpost[kHidden];         // post-attention norm weight of the layer
     alignas(16) float qs[kGroup * kHeadDim];  // q of this CTA's kv head
     alignas(16) float knew[kHeadDim];
     alignas(16) float vnew[kHeadDim];
-    float gate[32];
-    float mid_rows[8];                        // h' of this CTA's o_proj / down rows
+    alignas(16) float attn[kMaxOBlocks * kStepBlock];  // merged attention dims owned
+    alignas(16) float act[kMaxFeatures];      // SwiGLU of the features owned
+    float gate[kMaxFeatures];
     float scratch[32];
     float cv[kConsumerWarps];
     long long ci[kConsumerWarps];
-    float mm[kMergeDims][kMaxChunks];  // phase M: m, l, o[d] per (output dim, chunk)
-    float ml[kMergeDims][kMaxChunks];
-    float mo[kMergeDims][kMaxChunks];
-    union {
-        AttnCombine att;
-        alignas(16) float s[kInter];
-    } u;
+    float mm[kMaxOBlocks * kStepBlock][kMaxChunks];  // phase M: m, l, o[d] per (dim, chunk)
+    float ml[kMaxOBlocks * kStepBlock][kMaxChunks];
+    float mo[kMaxOBlocks * kStepBlock][kMaxChunks];
+    AttnCombine att;
     volatile int abort;
     int is_last;
     int consumed;  // tiles released by the consumers
@@ -166,8 +215,10 @@ constexpr size_t kRingOffset = (sizeof(Shared) + 127) / 128 * 128;
 // The CTA's fixed share of every phase, derived from (grid, CTA, position).
 struct Sched {
     int t0, t1;          // QKV row-pair tasks
-    int o0, o1;          // o_proj / down rows
-    int i0, i1;          // intermediate features
+    int o0, o1;          // accumulator rows this CTA zeroes
+    int f0, f1;          // MLP feature blocks (4 features each)
+    int ob[kMaxOBlocks]; // attention-dim blocks (4 dims each) of kv head g
+    int nob;
     int64_t v0, v1;      // vocab rows
     int g, c;            // attention kv head / chunk (g < 0: none)
     int64_t a0, a1;      // rows [a0, a1) of the valid length
@@ -175,16 +226,9 @@ struct Sched {
     bool owns_new;       // the chunk holds row `pos` (read from the exchange)
     bool has_rows;
     int active;          // active chunks per kv head
-    int n_att, n_down, n_lm, per_layer, total;
+    int n_att, n_lm, per_layer, total;
     int64_t pos, tok;
     uint32_t epoch;
-};
-
-struct Tile {
-    int nseg;
-    const float* src[kMaxSeg];
-    uint32_t bytes[kMaxSeg];
-    uint32_t total;
 };
 
 // QKV task -> its two rows.  Tasks 0..287: q (head, d < 32) with partner
@@ -209,8 +253,8 @@ __device__ void make_sched(const StepArgs& a, int G, int cta, Sched& s) {
     s.t1 = (cta + 1) * 480 / G;
     s.o0 = cta * kHidden / G;
     s.o1 = (cta + 1) * kHidden / G;
-    s.i0 = cta * kInter / G;
-    s.i1 = (cta + 1) * kInter / G;
+    s.f0 = cta * kFeatureBlocks / G;
+    s.f1 = (cta + 1) * kFeatureBlocks / G;
     s.v0 = static_cast<int64_t>(cta) * a.vocab / G;
     s.v1 = static_cast<int64_t>(cta + 1) * a.vocab / G;
     s.pos = *a.position;
@@ -222,6 +266,7 @@ __device__ void make_sched(const StepArgs& a, int G, int cta, Sched& s) {
     s.a0 = s.a1 = s.cached_end = 0;
     s.owns_new = s.has_rows = false;
     s.active = 0;
+    s.nob = 0;
     if (cta < kKVHeads * a.nch) {
         s.g = cta / a.nch;
         s.c = cta % a.nch;
@@ -234,72 +279,79 @@ __device__ void make_sched(const StepArgs& a, int G, int cta, Sched& s) {
             s.cached_end = min64(s.a1, s.pos);
             s.owns_new = s.pos >= s.a0 && s.pos < s.a1;
         }
+        for (int b = s.c; b < kAttnBlocks && s.nob < kMaxOBlocks; b += a.nch) s.ob[s.nob++] = b;
     }
     const int64_t cached = s.cached_end > s.a0 ? s.cached_end - s.a0 : 0;
     s.n_att = static_cast<int>((cached + kStepAttnRows - 1) / kStepAttnRows);
-    s.n_down = (s.o1 - s.o0 + kStepDownRows - 1) / kStepDownRows;
-    s.per_layer = 1 + s.n_att + 3 + s.n_down;
+    s.per_layer = 1 + s.n_att + 4;  // A, attention, misc (norm + o strips), gate, up, down strips
     s.n_lm = s.v1 > s.v0 ? 1 + static_cast<int>((s.v1 - s.v0 + kStepLmRows - 1) / kStepLmRows) : 0;
     s.total = kLayers * s.per_layer + s.n_lm;
 }
 
-// The k-th tile of this CTA, in consumption order.
-__device__ void make_tile(const StepArgs& a, const Sched& s, int k, Tile& t) {
-    t.nseg = 0;
-    t.total = 0;
-    auto add = [&](const float* src, uint32_t bytes) {
-        t.src[t.nseg] = src;
-        t.bytes[t.nseg] = bytes;
-        t.total += bytes;
-        ++t.nseg;
+// Producer: bytes of tile k, then its copies.  Tiles of a layer, in
+// consumption order: A = [input norm][row_a, row_b per QKV task];
+// attention = [K rows][V rows]; misc = [post norm][o_proj strip per owned
+// block, 576 x 4]; gate = [gate rows]; up = [up rows]; down = [down strip per
+// feature block, 576 x 4].  LM head: [final norm], then 12-row vocab tiles.
+__device__ uint32_t issue_tile(const StepArgs& a, const Sched& s, int k, unsigned char* dst, uint64_t* bar,
+                               bool issue) {
+    uint32_t off = 0;
+    auto row_copy = [&](const float* src, uint32_t bytes) {
+        if (issue) bulk_load(dst + off, src, bytes, bar);
+        off += bytes;
+    };
+    auto strip_copy = [&](const CUtensorMap* map, int x) {
+        for (int b = 0; b < kStripBoxes; ++b) {
+            if (issue) box_load(dst + off, map, x, b * kStepStripRows, bar);
+            off += kStripBytes;
+        }
     };
     if (k < kLayers * s.per_layer) {
         const int l = k / s.per_layer;
         int sub = k % s.per_layer;
         const StepLayer& L = a.layer[l];
-        if (sub == 0) {  // [input norm][row_a, row_b per task]
-            add(L.input_norm, kRowBytes);
+        if (sub == 0) {
+            row_copy(L.input_norm, kRowBytes);
             for (int task = s.t0; task < s.t1; ++task) {
                 int ra, rb, kind;
                 task_rows(task, ra, rb, kind);
-                add(L.qkv + static_cast<int64_t>(ra) * kHidden, kRowBytes);
-                add(L.qkv + static_cast<int64_t>(rb) * kHidden, kRowBytes);
+                row_copy(L.qkv + static_cast<int64_t>(ra) * kHidden, kRowBytes);
+                row_copy(L.qkv + static_cast<int64_t>(rb) * kHidden, kRowBytes);
             }
-            return;
+            return off;
         }
         sub -= 1;
-        if (sub < s.n_att) {  // [K rows][V rows]
+        if (sub < s.n_att) {
             const int64_t r0 = s.a0 + static_cast<int64_t>(sub) * kStepAttnRows;
             const int64_t n = min64(kStepAttnRows, s.cached_end - r0);
             const int64_t base = ((static_cast<int64_t>(l) * kKVHeads + s.g) * a.capacity + r0) * kHeadDim;
-            add(a.key_cache + base, static_cast<uint32_t>(n * kHeadDim * 4));
-            add(a.value_cache + base, static_cast<uint32_t>(n * kHeadDim * 4));
-            return;
+            row_copy(a.key_cache + base, static_cast<uint32_t>(n * kHeadDim * 4));
+            row_copy(a.value_cache + base, static_cast<uint32_t>(n * kHeadDim * 4));
+            return off;
         }
         sub -= s.n_att;
-        const int ni = s.i1 - s.i0;
+        const int nf = (s.f1 - s.f0) * kStepBlock;
         if (sub == 0) {
-            add(L.o_proj + static_cast<int64_t>(s.o0) * kHidden, (s.o1 - s.o0) * kRowBytes);
-        } else if (sub == 1) {  // [post norm][gate rows]
-            add(L.post_norm, kRowBytes);
-            add(L.gate_up + static_cast<int64_t>(s.i0) * kHidden, ni * kRowBytes);
-        } else if (sub == 2) {  // [up rows]
-            add(L.gate_up + static_cast<int64_t>(kInter + s.i0) * kHidden, ni * kRowBytes);
-        } else {  // [down rows] (1536 floats each)
-            const int r0 = s.o0 + (sub - 3) * kStepDownRows;
-            const int n = min(kStepDownRows, s.o1 - r0);
-            add(L.down + static_cast<int64_t>(r0) * kInter, n * kInter * 4);
+            row_copy(L.post_norm, kRowBytes);
+            for (int j = 0; j < s.nob; ++j) strip_copy(&L.o_map, s.g * kGroup * kHeadDim + s.ob[j] * kStepBlock);
+        } else if (sub == 1) {
+            row_copy(L.gate_up + static_cast<int64_t>(s.f0) * kStepBlock * kHidden, nf * kRowBytes);
+        } else if (sub == 2) {
+            row_copy(L.gate_up + static_cast<int64_t>(kInter + s.f0 * kStepBlock) * kHidden, nf * kRowBytes);
+        } else {
+            for (int f = s.f0; f < s.f1; ++f) strip_copy(&L.down_map, f * kStepBlock);
         }
-        return;
+        return off;
     }
     const int j = k - kLayers * s.per_layer;
     if (j == 0) {
-        add(a.final_norm, kRowBytes);
-        return;
+        row_copy(a.final_norm, kRowBytes);
+        return off;
     }
     const int64_t r0 = s.v0 + static_cast<int64_t>(j - 1) * kStepLmRows;
     const int64_t n = min64(kStepLmRows, s.v1 - r0);
-    add(a.lm_head + r0 * kHidden, static_cast<uint32_t>(n * kRowBytes));
+    row_copy(a.lm_head + r0 * kHidden, static_cast<uint32_t>(n * kRowBytes));
+    return off;
 }
 
 __device__ __forceinline__ void fail(const StepArgs& a, Shared& sh) {
@@ -362,24 +414,59 @@ __device__ unsigned long long poll_word(const StepArgs& a, Shared& sh, const uns
 // The consumers poll n tagged words into dst; false (uniformly) on abort.
 __device__ bool poll_into(const StepArgs& a, Shared& sh, const unsigned long long* src, int n, uint32_t tag,
                           float* dst) {
-    const int ct = threadIdx.x;
-    const unsigned long long ready = static_cast<unsigned long long>(tag) << 32;
-    for (int base = ct; base < n; base += 4 * kStepConsumers) {
-        unsigned long long v[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int i = base + j * kStepConsumers;
-            v[j] = i < n ? ld_word(src + i) : ready;
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int i = base + j * kStepConsumers;
-            if (word_tag(v[j]) != tag) v[j] = poll_word(a, sh, src + i, v[j], tag);
-            if (i < n) dst[i] = word_value(v[j]);
+    for (int i = threadIdx.x; i < n; i += kStepConsumers) {
+        unsigned long long v = ld_word(src + i);
+        if (word_tag(v) != tag) v = poll_word(a, sh, src + i, v, tag);
+        dst[i] = word_value(v);
+    }
+    consumer_sync();
+    return !sh.abort;
+}
+
+// Thread 0 waits (bounded) until the arrival counter reaches `target`;
+// false (uniformly) on abort.
+__device__ bool wait_count(const StepArgs& a, Shared& sh, const unsigned long long* counter,
+                           unsigned long long target) {
+    if (threadIdx.x == 0) {
+        unsigned long long v = ld_acquire(counter);
+        if (v < target) {
+            const unsigned long long t0 = global_timer();
+            do {
+                v = ld_acquire(counter);
+                const unsigned long long dt = global_timer() - t0;
+                if (dt > kPeerCheckNs && ld_error(a.error) != 0) {
+                    sh.abort = 1;
+                    break;
+                }
+                if (dt > kWaitNs) {
+                    fail(a, sh);
+                    break;
+                }
+            } while (v < target);
         }
     }
     consumer_sync();
     return !sh.abort;
+}
+
+__device__ __forceinline__ long long to_fixed(float x, bool& bad) {
+    if (!(fabsf(x) < kFixedLimit)) {
+        bad = true;
+        return 0;
+    }
+    return __float2ll_rn(x * kFloatToFixed);
+}
+
+__device__ __forceinline__ float from_fixed(long long v) {
+    return static_cast<float>(static_cast<double>(v) * kFixedToFloat);
+}
+
+// dst[i] = base[i] + sum[i] for the 576 accumulator words (NaN when a partial was bad).
+__device__ void add_accumulated(const long long* acc, const unsigned* bad, const float* base, float* dst) {
+    const bool poisoned = ld_flag(bad) != 0;
+    for (int i = threadIdx.x; i < kHidden; i += kStepConsumers)
+        dst[i] = poisoned ? __int_as_float(0x7fc00000) : base[i] + from_fixed(ld_fixed(acc + i));
+    consumer_sync();
 }
 
 // Sum over the 480 consumer threads (fixed order); every consumer gets it.
@@ -421,6 +508,25 @@ __device__ __forceinline__ float row_dot(const float* row, const float* xs, int 
     return group_sum<16>(acc);
 }
 
+// Split-K slice: out[r] = sum_j coef[j] * strip[j / 4][r][j % 4] for the 576
+// rows r, added into the fixed-point accumulator.
+__device__ void strip_products(const float* strips, const float* coef, int blocks, long long* acc, unsigned* bad) {
+    bool poisoned = false;
+    for (int r = threadIdx.x; r < kHidden; r += kStepConsumers) {
+        float y = 0.0f;
+        for (int b = 0; b < blocks; ++b) {
+            const float4 w = reinterpret_cast<const float4*>(strips + static_cast<size_t>(b) * kHidden * kStepBlock)[r];
+            const float4 c = reinterpret_cast<const float4*>(coef)[b];
+            y = fmaf(w.x, c.x, y);
+            y = fmaf(w.y, c.y, y);
+            y = fmaf(w.z, c.z, y);
+            y = fmaf(w.w, c.w, y);
+        }
+        red_fixed(acc + r, to_fixed(y, poisoned));
+    }
+    if (poisoned) atomicOr(bad, 1u);
+}
+
 __device__ __forceinline__ void argmax_take(float& bv, long long& bi, float v, long long i) {
     if (argmax_precedes(v, i, bv, bi)) {
         bv = v;
@@ -459,7 +565,8 @@ __device__ __forceinline__ void attend_row(const float4 (&qa)[kGroup], const flo
     }
 }
 
-__device__ __forceinline__ size_t buf(int l) { return static_cast<size_t>(l & 1); }
+__device__ __forceinline__ size_t parity(int l) { return static_cast<size_t>(l & 1); }
+__device__ __forceinline__ size_t rot3(int l) { return static_cast<size_t>(l % 3); }
 
 // ------------------------------------------------------------------ kernel
 
@@ -496,16 +603,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             for (int k = 0; k < s.total; ++k) {
                 const int slot = k % kStepSlots;
                 if (!wait_bar(a, sh, &sh.empty[slot], (static_cast<uint32_t>(k / kStepSlots) & 1u) ^ 1u)) break;
-                Tile t;
-                make_tile(a, s, k, t);
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive_expect_tx(&sh.full[slot], t.total);
-                uint32_t off = 0;
                 unsigned char* dst = ring + static_cast<size_t>(slot) * kStepSlotBytes;
-                for (int i = 0; i < t.nseg; ++i) {
-                    bulk_load(dst + off, t.src[i], t.bytes[i], &sh.full[slot]);
-                    off += t.bytes[i];
-                }
+                const uint32_t bytes = issue_tile(a, s, k, dst, &sh.full[slot], false);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive_expect_tx(&sh.full[slot], bytes);
+                issue_tile(a, s, k, dst, &sh.full[slot], true);
                 sh.issued = k + 1;
             }
         }
@@ -513,6 +615,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         // --------------------------------------------------------- consumers
         const int half = lane >> 4, l16 = lane & 15;
         const int64_t cap = a.capacity;
+        const unsigned long long base = static_cast<unsigned long long>(s.epoch) * kLayers * G;
+        unsigned long long* down_count = a.x.counters;
+        unsigned long long* mid_count = a.x.counters + 16;
         int k = 0;
         for (int l = 0; l < kLayers; ++l) {
             const uint32_t tag = s.epoch * 64u + static_cast<uint32_t>(l) + 1u;
@@ -522,14 +627,23 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 for (int i = tid; i < kHidden; i += kStepConsumers)
                     sh.hraw[i] = valid ? __ldg(a.embedding + s.tok * kHidden + i) : 0.0f;
                 consumer_sync();
-            } else if (!poll_into(a, sh, a.x.hidden + buf(l) * kHidden, kHidden, tag, sh.hraw)) {
-                goto done;
+            } else {
+                if (!wait_count(a, sh, down_count, base + static_cast<unsigned long long>(l) * G)) goto done;
+                add_accumulated(a.x.acc_down + rot3(l - 1) * kHidden, a.x.bad + 3 + rot3(l - 1), sh.mid, sh.hraw);
+            }
+            // Zero the accumulators two layers ahead (every reader of them is done).
+            for (int r = s.o0 + tid; r < s.o1; r += kStepConsumers) {
+                st_fixed(a.x.acc_mid + rot3(l + 1) * kHidden + r, 0);
+                st_fixed(a.x.acc_down + rot3(l + 1) * kHidden + r, 0);
+            }
+            if (cta == 0 && tid == 0) {
+                a.x.bad[rot3(l + 1)] = 0u;
+                a.x.bad[3 + rot3(l + 1)] = 0u;
             }
             LAYER_MARK(0);
             {
                 const float* t = acquire(a, sh, ring, k);
                 if (t == nullptr) goto done;
-                LAYER_MARK(1);
                 normalise(sh, sh.hraw, t, a.eps);
                 if (warp < s.t1 - s.t0) {
                     int ra, rb, kind;
@@ -537,35 +651,36 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     const float y = row_dot(t + kHidden * (1 + 2 * warp + half), sh.xs, l16);
                     const float ya = __shfl_sync(0xffffffffu, y, 0);
                     const float yb = __shfl_sync(0xffffffffu, y, 16);
-                    if (l16 == 0) {
-                        const int row = half ? rb : ra;
-                        unsigned long long* out = a.x.qkv + buf(l) * kQKV;
-                        if (kind == 2) {
+                    float out = y;
+                    const int row = half ? rb : ra;
+                    if (kind == 2) {
+                        if (l16 == 0) {
                             const int u = row - kHidden - kKVHeads * kHeadDim;
                             a.value_cache[((static_cast<int64_t>(l) * kKVHeads + u / kHeadDim) * cap + s.pos) *
                                               kHeadDim +
                                           u % kHeadDim] = y;
-                            st_word(out + row, tag, y);
-                        } else {
-                            const int d = row % kHeadDim;
-                            const float c = __ldg(a.cos_table + s.pos * kHeadDim + d);
-                            const float sn = __ldg(a.sin_table + s.pos * kHeadDim + d);
-                            const float r = half ? rope_value(yb, ya, c, sn, false) : rope_value(ya, yb, c, sn, true);
-                            if (kind == 1) {
-                                const int h = (row - kHidden) / kHeadDim;
-                                a.key_cache[((static_cast<int64_t>(l) * kKVHeads + h) * cap + s.pos) * kHeadDim + d] = r;
-                            }
-                            st_word(out + row, tag, r);
+                        }
+                    } else {
+                        const int d = row % kHeadDim;
+                        const float c = __ldg(a.cos_table + s.pos * kHeadDim + d);
+                        const float sn = __ldg(a.sin_table + s.pos * kHeadDim + d);
+                        out = half ? rope_value(yb, ya, c, sn, false) : rope_value(ya, yb, c, sn, true);
+                        if (kind == 1 && l16 == 0) {
+                            const int h = (row - kHidden) / kHeadDim;
+                            a.key_cache[((static_cast<int64_t>(l) * kKVHeads + h) * cap + s.pos) * kHeadDim + d] = out;
                         }
                     }
+                    // lanes 0..3 of each half publish the replicas
+                    if (l16 < kStepReplicas)
+                        st_word(a.x.qkv + (parity(l) * kStepReplicas + l16) * kQKV + row, tag, out);
                 }
                 release(sh, k++);
             }
-            LAYER_MARK(2);
+            LAYER_MARK(1);
 
             // ------------------------------------------------------ phase B
             if (s.has_rows) {
-                const unsigned long long* qkv = a.x.qkv + buf(l) * kQKV;
+                const unsigned long long* qkv = a.x.qkv + (parity(l) * kStepReplicas + cta % kStepReplicas) * kQKV;
                 if (!poll_into(a, sh, qkv + s.g * kGroup * kHeadDim, kGroup * kHeadDim, tag, sh.qs)) goto done;
                 if (s.owns_new) {
                     if (!poll_into(a, sh, qkv + kHidden + s.g * kHeadDim, kHeadDim, tag, sh.knew)) goto done;
@@ -573,7 +688,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                                    sh.vnew))
                         goto done;
                 }
-                LAYER_MARK(3);
+                LAYER_MARK(2);
                 const float scale = a.layer[l].scale;
                 const int l8 = lane & 7, grp = warp * 4 + (lane >> 3);
                 float4 qa[kGroup], qb[kGroup];
@@ -602,12 +717,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     }
                     release(sh, k++);
                 }
-                LAYER_MARK(4);
                 if (s.owns_new && grp == 0) {
                     const float4* k4 = reinterpret_cast<const float4*>(sh.knew);
                     const float4* v4 = reinterpret_cast<const float4*>(sh.vnew);
                     attend_row(qa, qb, k4[l8], k4[8 + l8], v4[l8], v4[8 + l8], scale, m, lsum, o);
                 }
+                LAYER_MARK(3);
                 // Combine the four row groups of each warp, then the 15 warps.
 #pragma unroll
                 for (int h = 0; h < kGroup; ++h) {
@@ -628,13 +743,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     }
                     if (lane < 8) {
                         if (lane == 0) {
-                            sh.u.att.wm[warp][h] = m[h];
-                            sh.u.att.wl[warp][h] = lsum[h];
+                            sh.att.wm[warp][h] = m[h];
+                            sh.att.wl[warp][h] = lsum[h];
                         }
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            sh.u.att.wo[warp][h][4 * l8 + j] = o[h][j];
-                            sh.u.att.wo[warp][h][32 + 4 * l8 + j] = o[h][4 + j];
+                            sh.att.wo[warp][h][4 * l8 + j] = o[h][j];
+                            sh.att.wo[warp][h][32 + 4 * l8 + j] = o[h][4 + j];
                         }
                     }
                 }
@@ -643,15 +758,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     const int h = tid / kHeadDim, d = tid % kHeadDim;
                     float mx = -INFINITY;
 #pragma unroll
-                    for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, sh.u.att.wm[w][h]);
+                    for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, sh.att.wm[w][h]);
                     float total = 0.0f, acc = 0.0f;
 #pragma unroll
                     for (int w = 0; w < kConsumerWarps; ++w) {
-                        const float f = sh.u.att.wm[w][h] == -INFINITY ? 0.0f : expf(sh.u.att.wm[w][h] - mx);
-                        total = fmaf(sh.u.att.wl[w][h], f, total);
-                        acc = fmaf(sh.u.att.wo[w][h][d], f, acc);
+                        const float f = sh.att.wm[w][h] == -INFINITY ? 0.0f : expf(sh.att.wm[w][h] - mx);
+                        total = fmaf(sh.att.wl[w][h], f, total);
+                        acc = fmaf(sh.att.wo[w][h][d], f, acc);
                     }
-                    unsigned long long* pw = a.x.partial + buf(l) * (static_cast<size_t>(kQHeads) * a.nch * kStepPartial) +
+                    unsigned long long* pw = a.x.partial + parity(l) * (static_cast<size_t>(kQHeads) * a.nch * kStepPartial) +
                                              ((static_cast<size_t>(s.g) * kGroup + h) * a.nch + s.c) * kStepPartial;
                     st_word(pw + 2 + d, tag, acc);
                     if (d == 0) {
@@ -661,132 +776,90 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 }
                 consumer_sync();
             }
-            LAYER_MARK(5);
+            LAYER_MARK(4);
 
             // ------------------------------------------------------ phase M
-            // Every attention CTA (g, c) merges output dims j = c, c + nch, ...
-            // (< 192) of kv head g over the active chunks: one round of loads.
-            if (s.g >= 0) {
-                const unsigned long long* part = a.x.partial +
-                                                 buf(l) * (static_cast<size_t>(kQHeads) * a.nch * kStepPartial) +
-                                                 static_cast<size_t>(s.g) * kGroup * a.nch * kStepPartial;
-                const int act = s.active;
-                const int nd = (kGroup * kHeadDim - s.c + a.nch - 1) / a.nch;
-                if (tid < nd * act) {
-                    const int q = tid / act, cc = tid % act;
-                    const int j = s.c + q * a.nch, h = j / kHeadDim, d = j % kHeadDim;
-                    const unsigned long long* p = part + (static_cast<size_t>(h) * a.nch + cc) * kStepPartial;
-                    unsigned long long vm = ld_word(p), vl = ld_word(p + 1), vo = ld_word(p + 2 + d);
-                    if (word_tag(vm) != tag) vm = poll_word(a, sh, p, vm, tag);
-                    if (word_tag(vl) != tag) vl = poll_word(a, sh, p + 1, vl, tag);
-                    if (word_tag(vo) != tag) vo = poll_word(a, sh, p + 2 + d, vo, tag);
-                    sh.mm[q][cc] = word_value(vm);
-                    sh.ml[q][cc] = word_value(vl);
-                    sh.mo[q][cc] = word_value(vo);
-                }
-                consumer_sync();
-                if (sh.abort) goto done;
-                LAYER_MARK(6);
-                if (warp < nd) {
-                    float mx = -INFINITY;
-                    for (int cc = lane; cc < act; cc += 32) mx = fmaxf(mx, sh.mm[warp][cc]);
-                    mx = warp_max(mx);
-                    float total = 0.0f, acc = 0.0f;
-                    for (int cc = lane; cc < act; cc += 32) {
-                        const float w = expf(sh.mm[warp][cc] - mx);
-                        total = fmaf(w, sh.ml[warp][cc], total);
-                        acc = fmaf(w, sh.mo[warp][cc], acc);
-                    }
-                    total = warp_sum(total);
-                    acc = warp_sum(acc);
-                    if (lane == 0) {
-                        const int j = s.c + warp * a.nch;
-                        st_word(a.x.attn + buf(l) * kHidden + s.g * kGroup * kHeadDim + j, tag, acc / total);
-                    }
-                }
-            }
-            LAYER_MARK(7);
-
-            // ------------------------------------------------------ phase C
-            if (!poll_into(a, sh, a.x.attn + buf(l) * kHidden, kHidden, tag, sh.xs)) goto done;
-            LAYER_MARK(8);
+            // Merge the owned attention dims over all chunks, then add their
+            // o_proj products (a split-K slice) into the h' accumulator.
             {
+                const int nd = s.nob * kStepBlock;
+                if (nd > 0) {
+                    const unsigned long long* part = a.x.partial +
+                                                     parity(l) * (static_cast<size_t>(kQHeads) * a.nch * kStepPartial) +
+                                                     static_cast<size_t>(s.g) * kGroup * a.nch * kStepPartial;
+                    const int act = s.active;
+                    for (int it = tid; it < nd * act; it += kStepConsumers) {
+                        const int q = it / act, cc = it % act;
+                        const int j = s.ob[q / kStepBlock] * kStepBlock + q % kStepBlock;
+                        const int h = j / kHeadDim, d = j % kHeadDim;
+                        const unsigned long long* p = part + (static_cast<size_t>(h) * a.nch + cc) * kStepPartial;
+                        unsigned long long vm = ld_word(p), vl = ld_word(p + 1), vo = ld_word(p + 2 + d);
+                        if (word_tag(vm) != tag) vm = poll_word(a, sh, p, vm, tag);
+                        if (word_tag(vl) != tag) vl = poll_word(a, sh, p + 1, vl, tag);
+                        if (word_tag(vo) != tag) vo = poll_word(a, sh, p + 2 + d, vo, tag);
+                        sh.mm[q][cc] = word_value(vm);
+                        sh.ml[q][cc] = word_value(vl);
+                        sh.mo[q][cc] = word_value(vo);
+                    }
+                    consumer_sync();
+                    if (sh.abort) goto done;
+                    LAYER_MARK(5);
+                    if (warp < nd) {
+                        float mx = -INFINITY;
+                        for (int cc = lane; cc < act; cc += 32) mx = fmaxf(mx, sh.mm[warp][cc]);
+                        mx = warp_max(mx);
+                        float total = 0.0f, acc = 0.0f;
+                        for (int cc = lane; cc < act; cc += 32) {
+                            const float w = expf(sh.mm[warp][cc] - mx);
+                            total = fmaf(w, sh.ml[warp][cc], total);
+                            acc = fmaf(w, sh.mo[warp][cc], acc);
+                        }
+                        total = warp_sum(total);
+                        acc = warp_sum(acc);
+                        if (lane == 0) sh.attn[warp] = acc / total;
+                    }
+                }
                 const float* t = acquire(a, sh, ring, k);
                 if (t == nullptr) goto done;
-                LAYER_MARK(9);
-                const int nrows = s.o1 - s.o0;
-                const int w2 = warp * 2 + half;
-                if (warp * 2 < nrows) {  // whole warps enter the half-warp shuffles
-                    const int rr = w2 < nrows ? w2 : 0;
-                    const float y = row_dot(t + rr * kHidden, sh.xs, l16);
-                    if (l16 == 0 && w2 < nrows) {
-                        const int r = s.o0 + w2;
-                        const float mid = sh.hraw[r] + y;
-                        sh.mid_rows[w2] = mid;
-                        st_word(a.x.mid + buf(l) * kHidden + r, tag, mid);
-                    }
-                }
+                for (int i = tid; i < kHidden; i += kStepConsumers) sh.wpost[i] = t[i];
+                if (nd > 0) strip_products(t + kHidden, sh.attn, s.nob, a.x.acc_mid + rot3(l) * kHidden, a.x.bad + rot3(l));
                 release(sh, k++);
+                if (tid == 0) arrive_release(mid_count);
             }
-            LAYER_MARK(10);
+            LAYER_MARK(6);
 
             // ------------------------------------------------------ phase D
-            if (!poll_into(a, sh, a.x.mid + buf(l) * kHidden, kHidden, tag, sh.mid)) goto done;
-            LAYER_MARK(11);
+            if (!wait_count(a, sh, mid_count, base + static_cast<unsigned long long>(l + 1) * G)) goto done;
+            add_accumulated(a.x.acc_mid + rot3(l) * kHidden, a.x.bad + rot3(l), sh.hraw, sh.mid);
+            LAYER_MARK(7);
             {
-                const int ni = s.i1 - s.i0;
+                const int nf = (s.f1 - s.f0) * kStepBlock;
                 const int w2 = warp * 2 + half;
+                normalise(sh, sh.mid, sh.wpost, a.eps);
                 const float* t = acquire(a, sh, ring, k);
                 if (t == nullptr) goto done;
-                normalise(sh, sh.mid, t, a.eps);
-                if (warp * 2 < ni) {
-                    const int rr = w2 < ni ? w2 : 0;
-                    const float y = row_dot(t + kHidden * (1 + rr), sh.xs, l16);
-                    if (l16 == 0 && w2 < ni) sh.gate[w2] = y;
+                if (warp * 2 < nf) {  // whole warps enter the half-warp shuffles
+                    const int rr = w2 < nf ? w2 : 0;
+                    const float y = row_dot(t + rr * kHidden, sh.xs, l16);
+                    if (l16 == 0 && w2 < nf) sh.gate[w2] = y;
                 }
                 release(sh, k++);
                 const float* tu = acquire(a, sh, ring, k);
                 if (tu == nullptr) goto done;
-                if (warp * 2 < ni) {
-                    const int rr = w2 < ni ? w2 : 0;
+                if (warp * 2 < nf) {
+                    const int rr = w2 < nf ? w2 : 0;
                     const float y = row_dot(tu + rr * kHidden, sh.xs, l16);
-                    if (l16 == 0 && w2 < ni)
-                        st_word(a.x.swiglu + buf(l) * kInter + s.i0 + w2, tag, swiglu(sh.gate[w2], y));
+                    if (l16 == 0 && w2 < nf) sh.act[w2] = swiglu(sh.gate[w2], y);
                 }
                 release(sh, k++);
-            }
-            LAYER_MARK(12);
-
-            // ------------------------------------------------------ phase E
-            if (!poll_into(a, sh, a.x.swiglu + buf(l) * kInter, kInter, tag, sh.u.s)) goto done;
-            LAYER_MARK(13);
-            for (int j = 0; j < s.n_down; ++j) {
-                const float* t = acquire(a, sh, ring, k);
-                if (t == nullptr) goto done;
-                const int r0 = s.o0 + j * kStepDownRows;
-                const int n = min(kStepDownRows, s.o1 - r0);
-                if (warp < n) {
-                    const float4* w4 = reinterpret_cast<const float4*>(t + warp * kInter);
-                    const float4* s4 = reinterpret_cast<const float4*>(sh.u.s);
-                    float acc = 0.0f;
-#pragma unroll
-                    for (int q = 0; q < kInter / 128; ++q) {
-                        const float4 w = w4[lane + 32 * q];
-                        const float4 x = s4[lane + 32 * q];
-                        acc = fmaf(w.x, x.x, acc);
-                        acc = fmaf(w.y, x.y, acc);
-                        acc = fmaf(w.z, x.z, acc);
-                        acc = fmaf(w.w, x.w, acc);
-                    }
-                    acc = warp_sum(acc);
-                    if (lane == 0) {
-                        const int r = r0 + warp;
-                        st_word(a.x.hidden + buf(l + 1) * kHidden + r, tag + 1u, sh.mid_rows[r - s.o0] + acc);
-                    }
-                }
+                LAYER_MARK(8);
+                const float* td = acquire(a, sh, ring, k);
+                if (td == nullptr) goto done;
+                strip_products(td, sh.act, s.f1 - s.f0, a.x.acc_down + rot3(l) * kHidden, a.x.bad + 3 + rot3(l));
                 release(sh, k++);
+                if (tid == 0) arrive_release(down_count);
             }
-            LAYER_MARK(14);
+            LAYER_MARK(9);
         }
 
         // ---------------------------------------------------------- LM head
@@ -795,8 +868,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             float bv = 0.0f;
             long long bi = -1;
             if (s.n_lm > 0) {
-                const uint32_t tag = s.epoch * 64u + static_cast<uint32_t>(kLayers) + 1u;
-                if (!poll_into(a, sh, a.x.hidden + buf(kLayers) * kHidden, kHidden, tag, sh.hraw)) goto done;
+                if (!wait_count(a, sh, down_count, base + static_cast<unsigned long long>(kLayers) * G)) goto done;
+                add_accumulated(a.x.acc_down + rot3(kLayers - 1) * kHidden, a.x.bad + 3 + rot3(kLayers - 1), sh.mid,
+                                sh.hraw);
                 const float* t = acquire(a, sh, ring, k);
                 if (t == nullptr) goto done;
                 normalise(sh, sh.hraw, t, a.eps);
@@ -856,7 +930,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     *a.step = st + 1;
                     *a.position = s.pos + 1;
                     a.sync[0] = 0u;
-                    a.sync[1] = s.epoch + 1u;  // the next step's tags
+                    a.sync[1] = s.epoch + 1u;  // the next step's tags and counter base
                 }
             }
         }
@@ -873,23 +947,69 @@ done:
     }
 }
 
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+fx_status encode_strip_map(CUtensorMap* map, const float* base, uint64_t columns, const char* what) {
+    static std::once_flag once;
+    static EncodeTiled encode = nullptr;
+    static cudaError_t lookup = cudaSuccess;
+    std::call_once(once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult found{};
+        lookup = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &found);
+        if (lookup == cudaSuccess && found == cudaDriverEntryPointSuccess) encode = reinterpret_cast<EncodeTiled>(fn);
+    });
+    if (encode == nullptr) {
+        set_error("flux native decode: cuTensorMapEncodeTiled is unavailable from the driver");
+        return FX_ERR_CUDA;
+    }
+    const cuuint64_t dims[2] = {columns, static_cast<cuuint64_t>(kHidden)};
+    const cuuint64_t strides[1] = {columns * sizeof(float)};
+    const cuuint32_t box[2] = {kStepBlock, kStepStripRows};
+    const cuuint32_t element_strides[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+                              element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error(std::string("flux native decode: encoding the tensor map of ") + what + " failed (CUresult " +
+                  std::to_string(static_cast<int>(r)) + ")");
+        return FX_ERR_CUDA;
+    }
+    return FX_OK;
+}
+
 }  // namespace
 
+size_t step_exchange_words(int nch) {
+    auto up = [](size_t w) { return (w + 31) / 32 * 32; };  // 256-byte sections
+    return up(2ull * kStepReplicas * kQKV) + up(2ull * kQHeads * nch * kStepPartial) + up(3ull * kHidden) +
+           up(3ull * kHidden) + 32 + 32;
+}
+
 StepExchange step_exchange_views(unsigned long long* base, int nch) {
+    auto up = [](size_t w) { return (w + 31) / 32 * 32; };
     StepExchange x{};
     unsigned long long* p = base;
-    x.hidden = p;
-    p += 2 * kHidden;
     x.qkv = p;
-    p += 2 * kQKV;
+    p += up(2ull * kStepReplicas * kQKV);
     x.partial = p;
-    p += 2ull * kQHeads * nch * kStepPartial;
-    x.attn = p;
-    p += 2 * kHidden;
-    x.mid = p;
-    p += 2 * kHidden;
-    x.swiglu = p;
+    p += up(2ull * kQHeads * nch * kStepPartial);
+    x.acc_mid = reinterpret_cast<long long*>(p);
+    p += up(3ull * kHidden);
+    x.acc_down = reinterpret_cast<long long*>(p);
+    p += up(3ull * kHidden);
+    x.bad = reinterpret_cast<unsigned*>(p);
+    p += 32;
+    x.counters = p;
     return x;
+}
+
+fx_status encode_step_maps(const float* o_proj, const float* down, StepLayer* layer) {
+    fx_status st = encode_strip_map(&layer->o_map, o_proj, kHidden, "o_proj");
+    if (st != FX_OK) return st;
+    return encode_strip_map(&layer->down_map, down, kInter, "the down projection");
 }
 
 size_t step_kernel_smem_bytes() { return kRingOffset + static_cast<size_t>(kStepSlots) * kStepSlotBytes; }
@@ -924,7 +1044,7 @@ fx_status prepare_step_kernel(int device, int* grid) {
         return FX_ERR_CUDA;
     }
     if (sms < kStepMinGrid || sms > kStepMaxGrid) {
-        set_error("flux native decode: the persistent step needs a GPU with 140 to 480 SMs");
+        set_error("flux native decode: the persistent step needs a GPU with 140 to 384 SMs");
         return FX_ERR_INVALID;
     }
     *grid = sms;

@@ -1,6 +1,8 @@
 // Arguments of the persistent single-launch decode step (step_kernel.cu).
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace fx {
@@ -11,32 +13,40 @@ constexpr int kStepSlots = 7;              // TMA staging slots per CTA
 constexpr int kStepSlotBytes = 27648;      // 12 rows of 576 floats
 constexpr int kStepAttnRows = 54;          // cache rows (K and V) per attention tile
 constexpr int kStepLmRows = 12;            // LM-head rows per tile
-constexpr int kStepDownRows = 4;           // down-projection rows (1536 floats) per tile
 constexpr int kStepPartial = 66;           // m, l, o[64] per (head, chunk)
+constexpr int kStepBlock = 4;              // columns per split-K strip (one 16-byte TMA box row)
+constexpr int kStepStripRows = 192;        // rows per 2-D TMA box of a strip
+constexpr int kStepReplicas = 4;           // copies of the published q | k | v words
 constexpr int kStepMinGrid = 140;          // the per-CTA slices must fit one slot
-constexpr int kStepMaxGrid = 480;
+constexpr int kStepMaxGrid = 384;          // every CTA owns at least one block of 4 MLP features
 
 struct StepLayer {
+    CUtensorMap o_map;        // o_proj [576, 576]: boxes of 4 columns x 192 rows
+    CUtensorMap down_map;     // down   [576, 1536]: boxes of 4 columns x 192 rows
     const float* input_norm;  // [576]
     const float* qkv;         // [960, 576]
-    const float* o_proj;      // [576, 576]
     const float* post_norm;   // [576]
     const float* gate_up;     // [3072, 576]
-    const float* down;        // [576, 1536]
     float scale;
 };
 
-// Cross-CTA exchange buffers, double-buffered by layer parity.  Every word is
-// (tag << 32 | float bits): a reader polls the word until it carries the tag
-// of the current (step, layer), so one L2 round trip both waits for and
-// delivers the value -- no grid barrier, no fence.
+// Cross-CTA exchange region.
+//  * q | k | v of the current row and the attention partials travel as
+//    64-bit words (tag << 32 | float bits), double-buffered by layer parity: a
+//    reader polls a word until it carries the tag of the current (step,
+//    layer), so one L2 round trip both waits for and delivers it.
+//  * o_proj and down are split-K over the CTAs; their partial sums meet in
+//    int64 fixed-point accumulators (2^-32 units, so the sum is exact and
+//    order-independent) followed by a release-add on an arrival counter.
+//    Accumulators rotate over 3 buffers by layer; each layer zeroes the
+//    buffer two layers ahead.
 struct StepExchange {
-    unsigned long long* hidden;    // [2][576]   layer input h (tag of the layer it enters)
-    unsigned long long* qkv;       // [2][960]   RoPE'd q | RoPE'd k | v of the current row
-    unsigned long long* partial;   // [2][3][3][nch][66] attention split-K partials
-    unsigned long long* attn;      // [2][576]   merged attention output
-    unsigned long long* mid;       // [2][576]   h' = h + o_proj(attn)
-    unsigned long long* swiglu;    // [2][1536]  SwiGLU output
+    unsigned long long* qkv;       // [2][kStepReplicas][960]
+    unsigned long long* partial;   // [2][3][3][nch][66]
+    long long* acc_mid;            // [3][576]  sum of o_proj partials (h' = h + acc)
+    long long* acc_down;           // [3][576]  sum of down partials (h_next = h' + acc)
+    unsigned* bad;                 // [2][3] a partial was non-finite or out of range (mid, down)
+    unsigned long long* counters;  // [0] down arrivals, [16] o_proj arrivals (monotonic, own lines)
 };
 
 struct StepArgs {
@@ -67,19 +77,19 @@ struct StepArgs {
     unsigned long long* timeline;  // optional [grid][kStepTimelineEvents] %globaltimer stamps
 };
 
-// Timeline events per CTA: 0 = start, then per layer 15 stamps (A: h polled,
-// tile landed, done; B: q polled, cache tiles done, partial published; M:
-// partials polled, done; C: attn polled, tile landed, done; D: h' polled,
-// done; E: SwiGLU polled, done), then LM-head start and end.
-constexpr int kStepTimelinePerLayer = 15;
+// Timeline events per CTA: 0 = start, then per layer 10 stamps (A: h ready,
+// done; B: q polled, cache tiles done, partial published; M: partials
+// polled, o_proj partial added; D: h' ready, gate/up done, down partial
+// added), then LM-head start and end.
+constexpr int kStepTimelinePerLayer = 10;
 constexpr int kStepTimelineEvents = 1 + kStepTimelinePerLayer * kLayers + 2;
 
-// Words of the exchange region for `nch` chunks per kv head.
-inline size_t step_exchange_words(int nch) {
-    return 2ull * (576 + 960 + 9ull * nch * kStepPartial + 576 + 576 + 1536);
-}
-// Carve the exchange region (base must be 16-byte aligned).
+// 64-bit words of the exchange region for `nch` chunks per kv head.
+size_t step_exchange_words(int nch);
+// Carve the exchange region (base must be 256-byte aligned).
 StepExchange step_exchange_views(unsigned long long* base, int nch);
+// Fill the layer's tensor maps for the split-K strips of o_proj and down.
+fx_status encode_step_maps(const float* o_proj, const float* down, StepLayer* layer);
 
 // Enqueue one decode step as a single cooperative launch of `grid` CTAs.
 fx_status launch_step_kernel(const StepArgs& args, int grid, cudaStream_t stream);
