@@ -50,11 +50,29 @@ constexpr int kStripBoxes = kHidden / kStepStripRows;    // boxes per 576-row st
 constexpr int kFeatureBlocks = kInter / kStepBlock;      // 384
 constexpr int kAttnBlocks = kGroup * kHeadDim / kStepBlock;  // 48 per kv head
 constexpr int kMaxChunks = 64;
+constexpr int kBatchTiles = 4;                           // attention tiles held at once
+constexpr int kRowGroups = kConsumerWarps * 4;           // 8-lane row groups (60)
+constexpr int kRowSlots = (kBatchTiles * kStepAttnRows + 1 + kRowGroups - 1) / kRowGroups;  // rows per group per batch
 constexpr int kMaxOBlocks = 2;                           // needs >= 24 chunks per kv head
 constexpr int kMaxFeatures = 12;                         // needs grid >= 128
-constexpr double kFixedToFloat = 2.3283064365386962890625e-10;  // 2^-32
-constexpr float kFloatToFixed = 4294967296.0f;                  // 2^32
-constexpr float kFixedLimit = 1073741824.0f;                    // |partial| < 2^30
+// Tally words of the split-K sums: [7-bit contributor count | 5-bit count
+// of out-of-range contributors | 52-bit sum of biased fixed-point terms].  A
+// contributor adds 2^57 + 2^44 + round(y * 2^30) for |y| < 2^14, or
+// 2^57 + 2^52 when y is out of range or not finite; the 2^44 bias keeps
+// every term in (0, 2^45), so up to 127 terms never carry out of the sum.
+// The count and the sum travel in one atomic word: a reader that sees the
+// full count has the full sum.  More than 31 out-of-range contributors to
+// one word carry into the count, which a reader also reports as NaN.
+constexpr int kTallyCountShift = 57;
+constexpr int kTallyBadShift = 52;
+constexpr unsigned long long kTallyOne = 1ull << kTallyCountShift;
+constexpr unsigned long long kTallyBadOne = 1ull << kTallyBadShift;
+constexpr unsigned long long kTallyValueMask = kTallyBadOne - 1;
+constexpr long long kTallyBias = 1ll << 44;
+constexpr float kTallyScale = 1073741824.0f;                 // 2^30
+constexpr double kTallyUnit = 9.31322574615478515625e-10;    // 2^-30
+constexpr float kTallyLimit = 16384.0f;                      // |y| < 2^14
+constexpr int kTallyWords = 2 * kStepAccReplicas * kHidden;  // one layer: (o_proj, down) x replicas x 576
 
 // ------------------------------------------------------------- PTX helpers
 
@@ -118,24 +136,6 @@ __device__ __forceinline__ unsigned long long ld_word(const unsigned long long* 
     return v;
 }
 
-__device__ __forceinline__ unsigned long long ld_acquire(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ long long ld_fixed(const long long* p) {
-    long long v;
-    asm volatile("ld.relaxed.gpu.global.s64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ unsigned ld_flag(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 __device__ __forceinline__ int ld_error(const int* p) {
     int v;
     asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -147,16 +147,12 @@ __device__ __forceinline__ void st_word(unsigned long long* p, uint32_t tag, flo
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-__device__ __forceinline__ void st_fixed(long long* p, long long v) {
-    asm volatile("st.relaxed.gpu.global.s64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void st_zero(unsigned long long* p) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], 0;" ::"l"(p) : "memory");
 }
 
-__device__ __forceinline__ void red_fixed(long long* p, long long v) {
+__device__ __forceinline__ void red_tally(unsigned long long* p, unsigned long long v) {
     asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ void arrive_release(unsigned long long* p) {
-    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(p) : "memory");
 }
 
 __device__ __forceinline__ uint32_t word_tag(unsigned long long v) { return static_cast<uint32_t>(v >> 32); }
@@ -215,7 +211,7 @@ constexpr size_t kRingOffset = (sizeof(Shared) + 127) / 128 * 128;
 // The CTA's fixed share of every phase, derived from (grid, CTA, position).
 struct Sched {
     int t0, t1;          // QKV row-pair tasks
-    int o0, o1;          // accumulator rows this CTA zeroes
+    int replica;         // tally replica this CTA adds into (word offset)
     int f0, f1;          // MLP feature blocks (4 features each)
     int ob[kMaxOBlocks]; // attention-dim blocks (4 dims each) of kv head g
     int nob;
@@ -251,8 +247,7 @@ __device__ __forceinline__ void task_rows(int task, int& row_a, int& row_b, int&
 __device__ void make_sched(const StepArgs& a, int G, int cta, Sched& s) {
     s.t0 = cta * 480 / G;
     s.t1 = (cta + 1) * 480 / G;
-    s.o0 = cta * kHidden / G;
-    s.o1 = (cta + 1) * kHidden / G;
+    s.replica = (cta % kStepAccReplicas) * kHidden;
     s.f0 = cta * kFeatureBlocks / G;
     s.f1 = (cta + 1) * kFeatureBlocks / G;
     s.v0 = static_cast<int64_t>(cta) * a.vocab / G;
@@ -293,16 +288,18 @@ __device__ void make_sched(const StepArgs& a, int G, int cta, Sched& s) {
 // attention = [K rows][V rows]; misc = [post norm][o_proj strip per owned
 // block, 576 x 4]; gate = [gate rows]; up = [up rows]; down = [down strip per
 // feature block, 576 x 4].  LM head: [final norm], then 12-row vocab tiles.
+enum class TileOp { kCount, kLoad };
+
 __device__ uint32_t issue_tile(const StepArgs& a, const Sched& s, int k, unsigned char* dst, uint64_t* bar,
-                               bool issue) {
+                               TileOp op) {
     uint32_t off = 0;
     auto row_copy = [&](const float* src, uint32_t bytes) {
-        if (issue) bulk_load(dst + off, src, bytes, bar);
+        if (op == TileOp::kLoad) bulk_load(dst + off, src, bytes, bar);
         off += bytes;
     };
     auto strip_copy = [&](const CUtensorMap* map, int x) {
         for (int b = 0; b < kStripBoxes; ++b) {
-            if (issue) box_load(dst + off, map, x, b * kStepStripRows, bar);
+            if (op == TileOp::kLoad) box_load(dst + off, map, x, b * kStepStripRows, bar);
             off += kStripBytes;
         }
     };
@@ -382,6 +379,22 @@ __device__ const float* acquire(const StepArgs& a, Shared& sh, unsigned char* ri
     return reinterpret_cast<const float*>(ring + static_cast<size_t>(slot) * kStepSlotBytes);
 }
 
+// Tiles k .. k + n - 1 (one attention batch): wait until all landed; false (uniformly) on abort.
+__device__ bool acquire_batch(const StepArgs& a, Shared& sh, int k, int n) {
+    for (int b = 0; b < n; ++b)
+        if (!wait_bar(a, sh, &sh.full[(k + b) % kStepSlots], static_cast<uint32_t>((k + b) / kStepSlots) & 1u)) break;
+    consumer_sync();
+    return !sh.abort;
+}
+
+__device__ void release_batch(Shared& sh, int k, int n) {
+    consumer_sync();
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < n; ++b) mbar_arrive(&sh.empty[(k + b) % kStepSlots]);
+        sh.consumed = k + n;
+    }
+}
+
 __device__ void release(Shared& sh, int k) {
     consumer_sync();
     if (threadIdx.x == 0) {
@@ -423,16 +436,35 @@ __device__ bool poll_into(const StepArgs& a, Shared& sh, const unsigned long lon
     return !sh.abort;
 }
 
-// Thread 0 waits (bounded) until the arrival counter reaches `target`;
-// false (uniformly) on abort.
-__device__ bool wait_count(const StepArgs& a, Shared& sh, const unsigned long long* counter,
-                           unsigned long long target) {
-    if (threadIdx.x == 0) {
-        unsigned long long v = ld_acquire(counter);
-        if (v < target) {
+// Contributors per replica: CTA c adds into replica c % kStepAccReplicas.
+__device__ __forceinline__ unsigned long long tally_expected(int G, int r) {
+    return static_cast<unsigned long long>((G - r + kStepAccReplicas - 1) / kStepAccReplicas);
+}
+
+// dst[i] = base[i] + the split-K sum i, once every contributor's add has
+// landed in every replica word (bounded polls; no fence needed: count and
+// sum share the word).  NaN where a contributor's partial was out of range.
+__device__ bool tally_read(const StepArgs& a, Shared& sh, const unsigned long long* acc, const float* base,
+                           float* dst, int G) {
+    for (int i = threadIdx.x; i < kHidden; i += kStepConsumers) {
+        unsigned long long w[kStepAccReplicas];
+        bool ready = true;
+#pragma unroll
+        for (int r = 0; r < kStepAccReplicas; ++r) {
+            w[r] = ld_word(acc + r * kHidden + i);
+            ready = ready && (w[r] >> kTallyCountShift) >= tally_expected(G, r);
+        }
+        if (!ready) {
             const unsigned long long t0 = global_timer();
-            do {
-                v = ld_acquire(counter);
+            while (true) {
+                __nanosleep(32);
+                ready = true;
+#pragma unroll
+                for (int r = 0; r < kStepAccReplicas; ++r) {
+                    if ((w[r] >> kTallyCountShift) < tally_expected(G, r)) w[r] = ld_word(acc + r * kHidden + i);
+                    ready = ready && (w[r] >> kTallyCountShift) >= tally_expected(G, r);
+                }
+                if (ready || sh.abort) break;
                 const unsigned long long dt = global_timer() - t0;
                 if (dt > kPeerCheckNs && ld_error(a.error) != 0) {
                     sh.abort = 1;
@@ -442,31 +474,19 @@ __device__ bool wait_count(const StepArgs& a, Shared& sh, const unsigned long lo
                     fail(a, sh);
                     break;
                 }
-            } while (v < target);
+            }
         }
+        long long total = 0;
+        bool bad = false;
+#pragma unroll
+        for (int r = 0; r < kStepAccReplicas; ++r) {
+            bad = bad || (w[r] >> kTallyBadShift) != (tally_expected(G, r) << (kTallyCountShift - kTallyBadShift));
+            total += static_cast<long long>(w[r] & kTallyValueMask) - static_cast<long long>(tally_expected(G, r)) * kTallyBias;
+        }
+        dst[i] = bad ? __int_as_float(0x7fc00000) : base[i] + static_cast<float>(static_cast<double>(total) * kTallyUnit);
     }
     consumer_sync();
     return !sh.abort;
-}
-
-__device__ __forceinline__ long long to_fixed(float x, bool& bad) {
-    if (!(fabsf(x) < kFixedLimit)) {
-        bad = true;
-        return 0;
-    }
-    return __float2ll_rn(x * kFloatToFixed);
-}
-
-__device__ __forceinline__ float from_fixed(long long v) {
-    return static_cast<float>(static_cast<double>(v) * kFixedToFloat);
-}
-
-// dst[i] = base[i] + sum[i] for the 576 accumulator words (NaN when a partial was bad).
-__device__ void add_accumulated(const long long* acc, const unsigned* bad, const float* base, float* dst) {
-    const bool poisoned = ld_flag(bad) != 0;
-    for (int i = threadIdx.x; i < kHidden; i += kStepConsumers)
-        dst[i] = poisoned ? __int_as_float(0x7fc00000) : base[i] + from_fixed(ld_fixed(acc + i));
-    consumer_sync();
 }
 
 // Sum over the 480 consumer threads (fixed order); every consumer gets it.
@@ -508,10 +528,9 @@ __device__ __forceinline__ float row_dot(const float* row, const float* xs, int 
     return group_sum<16>(acc);
 }
 
-// Split-K slice: out[r] = sum_j coef[j] * strip[j / 4][r][j % 4] for the 576
-// rows r, added into the fixed-point accumulator.
-__device__ void strip_products(const float* strips, const float* coef, int blocks, long long* acc, unsigned* bad) {
-    bool poisoned = false;
+// Split-K slice: y[r] = sum_j coef[j] * strip[j / 4][r][j % 4] for the 576
+// rows r (blocks = 0: zeros), added into this CTA's replica of the tally.
+__device__ void tally_products(const float* strips, const float* coef, int blocks, unsigned long long* acc) {
     for (int r = threadIdx.x; r < kHidden; r += kStepConsumers) {
         float y = 0.0f;
         for (int b = 0; b < blocks; ++b) {
@@ -522,9 +541,12 @@ __device__ void strip_products(const float* strips, const float* coef, int block
             y = fmaf(w.z, c.z, y);
             y = fmaf(w.w, c.w, y);
         }
-        red_fixed(acc + r, to_fixed(y, poisoned));
+        const unsigned long long term =
+            fabsf(y) < kTallyLimit
+                ? kTallyOne + static_cast<unsigned long long>(kTallyBias + __float2ll_rn(y * kTallyScale))
+                : kTallyOne + kTallyBadOne;
+        red_tally(acc + r, term);
     }
-    if (poisoned) atomicOr(bad, 1u);
 }
 
 __device__ __forceinline__ void argmax_take(float& bv, long long& bi, float v, long long i) {
@@ -534,39 +556,7 @@ __device__ __forceinline__ void argmax_take(float& bv, long long& bi, float v, l
     }
 }
 
-// Online-softmax update of one 8-lane row group with one cache row.
-__device__ __forceinline__ void attend_row(const float4 (&qa)[kGroup], const float4 (&qb)[kGroup], float4 k0,
-                                           float4 k1, float4 v0, float4 v1, float scale, float (&m)[kGroup],
-                                           float (&l)[kGroup], float (&o)[kGroup][8]) {
-#pragma unroll
-    for (int h = 0; h < kGroup; ++h) {
-        float d = qa[h].x * k0.x;
-        d = fmaf(qa[h].y, k0.y, d);
-        d = fmaf(qa[h].z, k0.z, d);
-        d = fmaf(qa[h].w, k0.w, d);
-        d = fmaf(qb[h].x, k1.x, d);
-        d = fmaf(qb[h].y, k1.y, d);
-        d = fmaf(qb[h].z, k1.z, d);
-        d = fmaf(qb[h].w, k1.w, d);
-        const float sc = group8_sum(d) * scale;  // only this row group need be active
-        const float mn = fmaxf(m[h], sc);
-        const float f = expf(m[h] - mn);  // m = -inf before the first row: f = 0
-        const float e = expf(sc - mn);
-        l[h] = l[h] * f + e;
-        o[h][0] = fmaf(o[h][0], f, e * v0.x);
-        o[h][1] = fmaf(o[h][1], f, e * v0.y);
-        o[h][2] = fmaf(o[h][2], f, e * v0.z);
-        o[h][3] = fmaf(o[h][3], f, e * v0.w);
-        o[h][4] = fmaf(o[h][4], f, e * v1.x);
-        o[h][5] = fmaf(o[h][5], f, e * v1.y);
-        o[h][6] = fmaf(o[h][6], f, e * v1.z);
-        o[h][7] = fmaf(o[h][7], f, e * v1.w);
-        m[h] = mn;
-    }
-}
-
 __device__ __forceinline__ size_t parity(int l) { return static_cast<size_t>(l & 1); }
-__device__ __forceinline__ size_t rot3(int l) { return static_cast<size_t>(l % 3); }
 
 // ------------------------------------------------------------------ kernel
 
@@ -604,10 +594,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 const int slot = k % kStepSlots;
                 if (!wait_bar(a, sh, &sh.empty[slot], (static_cast<uint32_t>(k / kStepSlots) & 1u) ^ 1u)) break;
                 unsigned char* dst = ring + static_cast<size_t>(slot) * kStepSlotBytes;
-                const uint32_t bytes = issue_tile(a, s, k, dst, &sh.full[slot], false);
+                const uint32_t bytes = issue_tile(a, s, k, dst, &sh.full[slot], TileOp::kCount);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 mbar_arrive_expect_tx(&sh.full[slot], bytes);
-                issue_tile(a, s, k, dst, &sh.full[slot], true);
+                issue_tile(a, s, k, dst, &sh.full[slot], TileOp::kLoad);
                 sh.issued = k + 1;
             }
         }
@@ -615,9 +605,18 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         // --------------------------------------------------------- consumers
         const int half = lane >> 4, l16 = lane & 15;
         const int64_t cap = a.capacity;
-        const unsigned long long base = static_cast<unsigned long long>(s.epoch) * kLayers * G;
-        unsigned long long* down_count = a.x.counters;
-        unsigned long long* mid_count = a.x.counters + 16;
+        // This step's tallies: set (epoch & 1), [layer][o_proj | down][replica][576].
+        unsigned long long* tallies = a.x.tally + static_cast<size_t>(s.epoch & 1u) * kLayers * kTallyWords;
+        auto mid_tally = [&](int l) { return tallies + static_cast<size_t>(l) * kTallyWords; };
+        auto down_tally = [&](int l) { return tallies + static_cast<size_t>(l) * kTallyWords + kTallyWords / 2; };
+        // Zero the other set for the next step (it was last read by the previous launch).
+        {
+            unsigned long long* next = a.x.tally + static_cast<size_t>((s.epoch + 1u) & 1u) * kLayers * kTallyWords;
+            const size_t n = static_cast<size_t>(kLayers) * kTallyWords;
+            for (size_t i = static_cast<size_t>(cta) * n / G + tid; i < static_cast<size_t>(cta + 1) * n / G;
+                 i += kStepConsumers)
+                st_zero(next + i);
+        }
         int k = 0;
         for (int l = 0; l < kLayers; ++l) {
             const uint32_t tag = s.epoch * 64u + static_cast<uint32_t>(l) + 1u;
@@ -627,18 +626,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 for (int i = tid; i < kHidden; i += kStepConsumers)
                     sh.hraw[i] = valid ? __ldg(a.embedding + s.tok * kHidden + i) : 0.0f;
                 consumer_sync();
-            } else {
-                if (!wait_count(a, sh, down_count, base + static_cast<unsigned long long>(l) * G)) goto done;
-                add_accumulated(a.x.acc_down + rot3(l - 1) * kHidden, a.x.bad + 3 + rot3(l - 1), sh.mid, sh.hraw);
-            }
-            // Zero the accumulators two layers ahead (every reader of them is done).
-            for (int r = s.o0 + tid; r < s.o1; r += kStepConsumers) {
-                st_fixed(a.x.acc_mid + rot3(l + 1) * kHidden + r, 0);
-                st_fixed(a.x.acc_down + rot3(l + 1) * kHidden + r, 0);
-            }
-            if (cta == 0 && tid == 0) {
-                a.x.bad[rot3(l + 1)] = 0u;
-                a.x.bad[3 + rot3(l + 1)] = 0u;
+            } else if (!tally_read(a, sh, down_tally(l - 1), sh.mid, sh.hraw, G)) {
+                goto done;
             }
             LAYER_MARK(0);
             {
@@ -697,74 +686,150 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     qa[h] = reinterpret_cast<const float4*>(sh.qs + h * kHeadDim)[l8];
                     qb[h] = reinterpret_cast<const float4*>(sh.qs + h * kHeadDim)[8 + l8];
                 }
-                float m[kGroup], lsum[kGroup], o[kGroup][8];
+                // Batches of up to 4 cache tiles: scores of every row first
+                // (rows independent), one CTA-wide max, then exponentials and
+                // the P.V sums.  The running max rescales earlier batches.
+                float mrun[kGroup], lsum[kGroup], o[kGroup][8];
 #pragma unroll
                 for (int h = 0; h < kGroup; ++h) {
-                    m[h] = -INFINITY;
+                    mrun[h] = -INFINITY;
                     lsum[h] = 0.0f;
 #pragma unroll
                     for (int j = 0; j < 8; ++j) o[h][j] = 0.0f;
                 }
-                for (int j = 0; j < s.n_att; ++j) {
-                    const float* t = acquire(a, sh, ring, k);
-                    if (t == nullptr) goto done;
+                int j = 0;
+                do {
+                    const int nb = min(kBatchTiles, s.n_att - j);
                     const int64_t r0 = s.a0 + static_cast<int64_t>(j) * kStepAttnRows;
-                    const int n = static_cast<int>(min64(kStepAttnRows, s.cached_end - r0));
-                    if (grp < n) {
-                        const float4* k4 = reinterpret_cast<const float4*>(t + grp * kHeadDim);
-                        const float4* v4 = reinterpret_cast<const float4*>(t + (n + grp) * kHeadDim);
-                        attend_row(qa, qb, k4[l8], k4[8 + l8], v4[l8], v4[8 + l8], scale, m, lsum, o);
+                    const int cached = static_cast<int>(
+                        max(static_cast<int64_t>(0), min64(static_cast<int64_t>(nb) * kStepAttnRows, s.cached_end - r0)));
+                    const bool with_new = j + nb == s.n_att && s.owns_new;
+                    const int rows = cached + (with_new ? 1 : 0);
+                    if (!acquire_batch(a, sh, k, nb)) goto done;
+                    // Row gi of the batch: tile gi / 54 (every tile but the chunk's last is full),
+                    // or the new row (gi == cached) from the exchange.
+                    auto key_row = [&](int gi) -> const float* {
+                        if (gi >= cached) return sh.knew;
+                        const int b = gi / kStepAttnRows;
+                        return reinterpret_cast<const float*>(ring + static_cast<size_t>((k + b) % kStepSlots) * kStepSlotBytes) +
+                               (gi - b * kStepAttnRows) * kHeadDim;
+                    };
+                    auto value_row = [&](int gi) -> const float* {
+                        if (gi >= cached) return sh.vnew;
+                        const int b = gi / kStepAttnRows;
+                        const int n = min(kStepAttnRows, cached - b * kStepAttnRows);
+                        return reinterpret_cast<const float*>(ring + static_cast<size_t>((k + b) % kStepSlots) * kStepSlotBytes) +
+                               (n + gi - b * kStepAttnRows) * kHeadDim;
+                    };
+                    float sc[kRowSlots][kGroup];
+#pragma unroll
+                    for (int i = 0; i < kRowSlots; ++i) {
+                        const int gi = grp + kRowGroups * i;
+#pragma unroll
+                        for (int h = 0; h < kGroup; ++h) sc[i][h] = -INFINITY;
+                        if (warp * 4 + kRowGroups * i < rows) {  // warp-uniform: full-mask shuffles
+                            const float4* k4 = reinterpret_cast<const float4*>(key_row(gi));
+                            const float4 k0 = k4[l8], k1 = k4[8 + l8];
+                            float d[kGroup];
+#pragma unroll
+                            for (int h = 0; h < kGroup; ++h) {
+                                float d0 = qa[h].x * k0.x, d1 = qb[h].x * k1.x;
+                                d0 = fmaf(qa[h].y, k0.y, d0);
+                                d1 = fmaf(qb[h].y, k1.y, d1);
+                                d0 = fmaf(qa[h].z, k0.z, d0);
+                                d1 = fmaf(qb[h].z, k1.z, d1);
+                                d0 = fmaf(qa[h].w, k0.w, d0);
+                                d1 = fmaf(qb[h].w, k1.w, d1);
+                                d[h] = d0 + d1;
+                            }
+#pragma unroll
+                            for (int off = 4; off > 0; off >>= 1)
+#pragma unroll
+                                for (int h = 0; h < kGroup; ++h) d[h] += __shfl_xor_sync(0xffffffffu, d[h], off);
+                            if (gi < rows)
+#pragma unroll
+                                for (int h = 0; h < kGroup; ++h) sc[i][h] = d[h] * scale;
+                        }
                     }
-                    release(sh, k++);
-                }
-                if (s.owns_new && grp == 0) {
-                    const float4* k4 = reinterpret_cast<const float4*>(sh.knew);
-                    const float4* v4 = reinterpret_cast<const float4*>(sh.vnew);
-                    attend_row(qa, qb, k4[l8], k4[8 + l8], v4[l8], v4[8 + l8], scale, m, lsum, o);
-                }
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) {
+                        float mb = sc[0][h];
+#pragma unroll
+                        for (int i = 1; i < kRowSlots; ++i) mb = fmaxf(mb, sc[i][h]);
+                        mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 8));
+                        mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 16));
+                        if (lane == 0) sh.att.wm[warp][h] = mb;
+                    }
+                    consumer_sync();
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) {
+                        float mx = sh.att.wm[0][h];
+#pragma unroll
+                        for (int w = 1; w < kConsumerWarps; ++w) mx = fmaxf(mx, sh.att.wm[w][h]);
+                        const float mn = fmaxf(mrun[h], mx);
+                        const float f = expf(mrun[h] - mn);  // first batch: mrun = -inf -> 0
+                        lsum[h] *= f;
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) o[h][q] *= f;
+                        mrun[h] = mn;
+                    }
+#pragma unroll
+                    for (int i = 0; i < kRowSlots; ++i) {
+                        const int gi = grp + kRowGroups * i;
+                        if (gi < rows) {
+                            const float4* v4 = reinterpret_cast<const float4*>(value_row(gi));
+                            const float4 v0 = v4[l8], v1 = v4[8 + l8];
+#pragma unroll
+                            for (int h = 0; h < kGroup; ++h) {
+                                const float pr = expf(sc[i][h] - mrun[h]);
+                                lsum[h] += pr;
+                                o[h][0] = fmaf(pr, v0.x, o[h][0]);
+                                o[h][1] = fmaf(pr, v0.y, o[h][1]);
+                                o[h][2] = fmaf(pr, v0.z, o[h][2]);
+                                o[h][3] = fmaf(pr, v0.w, o[h][3]);
+                                o[h][4] = fmaf(pr, v1.x, o[h][4]);
+                                o[h][5] = fmaf(pr, v1.y, o[h][5]);
+                                o[h][6] = fmaf(pr, v1.z, o[h][6]);
+                                o[h][7] = fmaf(pr, v1.w, o[h][7]);
+                            }
+                        }
+                    }
+                    release_batch(sh, k, nb);
+                    k += nb;
+                    j += nb;
+                } while (j < s.n_att);
                 LAYER_MARK(3);
-                // Combine the four row groups of each warp, then the 15 warps.
+                // Sum the 60 row groups: 4 per warp by shuffles, then the 15 warps.
 #pragma unroll
                 for (int h = 0; h < kGroup; ++h) {
+                    float lv = lsum[h];
+                    lv += __shfl_xor_sync(0xffffffffu, lv, 8);
+                    lv += __shfl_xor_sync(0xffffffffu, lv, 16);
 #pragma unroll
-                    for (int off = 8; off <= 16; off <<= 1) {
-                        const float mo = __shfl_xor_sync(0xffffffffu, m[h], off);
-                        const float lo = __shfl_xor_sync(0xffffffffu, lsum[h], off);
-                        const float mn = fmaxf(m[h], mo);
-                        const float fa = m[h] == -INFINITY ? 0.0f : expf(m[h] - mn);
-                        const float fb = mo == -INFINITY ? 0.0f : expf(mo - mn);
-                        lsum[h] = lsum[h] * fa + lo * fb;
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const float oo = __shfl_xor_sync(0xffffffffu, o[h][j], off);
-                            o[h][j] = o[h][j] * fa + oo * fb;
-                        }
-                        m[h] = mn;
+                    for (int q = 0; q < 8; ++q) {
+                        float ov = o[h][q];
+                        ov += __shfl_xor_sync(0xffffffffu, ov, 8);
+                        ov += __shfl_xor_sync(0xffffffffu, ov, 16);
+                        o[h][q] = ov;
                     }
                     if (lane < 8) {
-                        if (lane == 0) {
-                            sh.att.wm[warp][h] = m[h];
-                            sh.att.wl[warp][h] = lsum[h];
-                        }
+                        if (lane == 0) sh.att.wl[warp][h] = lv;
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            sh.att.wo[warp][h][4 * l8 + j] = o[h][j];
-                            sh.att.wo[warp][h][32 + 4 * l8 + j] = o[h][4 + j];
+                        for (int q = 0; q < 4; ++q) {
+                            sh.att.wo[warp][h][4 * l8 + q] = o[h][q];
+                            sh.att.wo[warp][h][32 + 4 * l8 + q] = o[h][4 + q];
                         }
                     }
                 }
                 consumer_sync();
                 if (tid < kGroup * kHeadDim) {
                     const int h = tid / kHeadDim, d = tid % kHeadDim;
-                    float mx = -INFINITY;
-#pragma unroll
-                    for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, sh.att.wm[w][h]);
+                    const float mx = h == 0 ? mrun[0] : (h == 1 ? mrun[1] : mrun[2]);
                     float total = 0.0f, acc = 0.0f;
 #pragma unroll
                     for (int w = 0; w < kConsumerWarps; ++w) {
-                        const float f = sh.att.wm[w][h] == -INFINITY ? 0.0f : expf(sh.att.wm[w][h] - mx);
-                        total = fmaf(sh.att.wl[w][h], f, total);
-                        acc = fmaf(sh.att.wo[w][h][d], f, acc);
+                        total += sh.att.wl[w][h];
+                        acc += sh.att.wo[w][h][d];
                     }
                     unsigned long long* pw = a.x.partial + parity(l) * (static_cast<size_t>(kQHeads) * a.nch * kStepPartial) +
                                              ((static_cast<size_t>(s.g) * kGroup + h) * a.nch + s.c) * kStepPartial;
@@ -822,15 +887,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 const float* t = acquire(a, sh, ring, k);
                 if (t == nullptr) goto done;
                 for (int i = tid; i < kHidden; i += kStepConsumers) sh.wpost[i] = t[i];
-                if (nd > 0) strip_products(t + kHidden, sh.attn, s.nob, a.x.acc_mid + rot3(l) * kHidden, a.x.bad + rot3(l));
+                tally_products(t + kHidden, sh.attn, s.nob, mid_tally(l) + s.replica);
                 release(sh, k++);
-                if (tid == 0) arrive_release(mid_count);
             }
             LAYER_MARK(6);
 
             // ------------------------------------------------------ phase D
-            if (!wait_count(a, sh, mid_count, base + static_cast<unsigned long long>(l + 1) * G)) goto done;
-            add_accumulated(a.x.acc_mid + rot3(l) * kHidden, a.x.bad + rot3(l), sh.hraw, sh.mid);
+            if (!tally_read(a, sh, mid_tally(l), sh.hraw, sh.mid, G)) goto done;
             LAYER_MARK(7);
             {
                 const int nf = (s.f1 - s.f0) * kStepBlock;
@@ -855,9 +918,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 LAYER_MARK(8);
                 const float* td = acquire(a, sh, ring, k);
                 if (td == nullptr) goto done;
-                strip_products(td, sh.act, s.f1 - s.f0, a.x.acc_down + rot3(l) * kHidden, a.x.bad + 3 + rot3(l));
+                tally_products(td, sh.act, s.f1 - s.f0, down_tally(l) + s.replica);
                 release(sh, k++);
-                if (tid == 0) arrive_release(down_count);
             }
             LAYER_MARK(9);
         }
@@ -868,9 +930,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             float bv = 0.0f;
             long long bi = -1;
             if (s.n_lm > 0) {
-                if (!wait_count(a, sh, down_count, base + static_cast<unsigned long long>(kLayers) * G)) goto done;
-                add_accumulated(a.x.acc_down + rot3(kLayers - 1) * kHidden, a.x.bad + 3 + rot3(kLayers - 1), sh.mid,
-                                sh.hraw);
+                if (!tally_read(a, sh, down_tally(kLayers - 1), sh.mid, sh.hraw, G)) goto done;
                 const float* t = acquire(a, sh, ring, k);
                 if (t == nullptr) goto done;
                 normalise(sh, sh.hraw, t, a.eps);
@@ -984,8 +1044,8 @@ fx_status encode_strip_map(CUtensorMap* map, const float* base, uint64_t columns
 
 size_t step_exchange_words(int nch) {
     auto up = [](size_t w) { return (w + 31) / 32 * 32; };  // 256-byte sections
-    return up(2ull * kStepReplicas * kQKV) + up(2ull * kQHeads * nch * kStepPartial) + up(3ull * kHidden) +
-           up(3ull * kHidden) + 32 + 32;
+    return up(2ull * kStepReplicas * kQKV) + up(2ull * kQHeads * nch * kStepPartial) +
+           up(2ull * kLayers * kTallyWords);
 }
 
 StepExchange step_exchange_views(unsigned long long* base, int nch) {
@@ -996,13 +1056,7 @@ StepExchange step_exchange_views(unsigned long long* base, int nch) {
     p += up(2ull * kStepReplicas * kQKV);
     x.partial = p;
     p += up(2ull * kQHeads * nch * kStepPartial);
-    x.acc_mid = reinterpret_cast<long long*>(p);
-    p += up(3ull * kHidden);
-    x.acc_down = reinterpret_cast<long long*>(p);
-    p += up(3ull * kHidden);
-    x.bad = reinterpret_cast<unsigned*>(p);
-    p += 32;
-    x.counters = p;
+    x.tally = p;
     return x;
 }
 

@@ -17,6 +17,7 @@ constexpr int kStepPartial = 66;           // m, l, o[64] per (head, chunk)
 constexpr int kStepBlock = 4;              // columns per split-K strip (one 16-byte TMA box row)
 constexpr int kStepStripRows = 192;        // rows per 2-D TMA box of a strip
 constexpr int kStepReplicas = 4;           // copies of the published q | k | v words
+constexpr int kStepAccReplicas = 2;        // copies of each split-K accumulator (spreads the atomics)
 constexpr int kStepMinGrid = 140;          // the per-CTA slices must fit one slot
 constexpr int kStepMaxGrid = 384;          // every CTA owns at least one block of 4 MLP features
 
@@ -36,17 +37,17 @@ struct StepLayer {
 //    reader polls a word until it carries the tag of the current (step,
 //    layer), so one L2 round trip both waits for and delivers it.
 //  * o_proj and down are split-K over the CTAs; their partial sums meet in
-//    int64 fixed-point accumulators (2^-32 units, so the sum is exact and
-//    order-independent) followed by a release-add on an arrival counter.
-//    Accumulators rotate over 3 buffers by layer; each layer zeroes the
-//    buffer two layers ahead.
+//    64-bit tally words [contributor count | out-of-range count | sum of
+//    biased 2^-30 fixed-point terms] -- integer adds, so the sum is exact
+//    and order-independent, and count and sum arrive in one atomic word: a
+//    reader polls until every word's count is complete, no fence needed.
+//    CTA c adds into replica c % 2; readers sum the replicas.  Every layer
+//    has its own tally words and the steps alternate between two sets; each
+//    step zeroes the set of the next step, which only a later launch reads.
 struct StepExchange {
     unsigned long long* qkv;       // [2][kStepReplicas][960]
     unsigned long long* partial;   // [2][3][3][nch][66]
-    long long* acc_mid;            // [3][576]  sum of o_proj partials (h' = h + acc)
-    long long* acc_down;           // [3][576]  sum of down partials (h_next = h' + acc)
-    unsigned* bad;                 // [2][3] a partial was non-finite or out of range (mid, down)
-    unsigned long long* counters;  // [0] down arrivals, [16] o_proj arrivals (monotonic, own lines)
+    unsigned long long* tally;     // [2 steps][30][o_proj, down][2 replicas][576]
 };
 
 struct StepArgs {
