@@ -51,8 +51,12 @@ constexpr int kFeatureBlocks = kInter / kStepBlock;      // 384
 constexpr int kAttnBlocks = kGroup * kHeadDim / kStepBlock;  // 48 per kv head
 constexpr int kMaxChunks = 64;
 constexpr int kBatchTiles = 4;                           // attention tiles held at once
-constexpr int kRowGroups = kConsumerWarps * 4;           // 8-lane row groups (60)
-constexpr int kRowSlots = (kBatchTiles * kStepAttnRows + 1 + kRowGroups - 1) / kRowGroups;  // rows per group per batch
+constexpr int kBatchRows = kBatchTiles * kStepAttnRows + 4;  // + the new row, padded (220)
+constexpr int kRowGroups = kConsumerWarps * 8;           // 4-lane score groups (120)
+constexpr int kRowSlots = (kBatchTiles * kStepAttnRows + 1 + kRowGroups - 1) / kRowGroups;  // rows per group per batch (2)
+constexpr int kPvSplits = kStepConsumers / (kGroup * kHeadDim / 4);  // P.V row splits (10)
+constexpr float kLog2e = 1.4426950408889634f;            // log2(e): scores kept in base-2 units
+constexpr float kLn2 = 0.6931471805599453f;              // ln(2)
 constexpr int kMaxOBlocks = 2;                           // needs >= 24 chunks per kv head
 constexpr int kMaxFeatures = 12;                         // needs grid >= 128
 // Tally words of the split-K sums: [7-bit contributor count | 5-bit count
@@ -174,10 +178,13 @@ __device__ __forceinline__ int64_t min64(int64_t x, int64_t y) { return x < y ? 
 
 // ------------------------------------------------------------ shared state
 
-struct AttnCombine {
+// Phase B scratch: scores (then probabilities) of one batch, per-warp
+// maxima, and the P.V partial sums of the row splits.
+struct AttnScratch {
+    alignas(16) float p[kGroup][kBatchRows];
     float wm[kConsumerWarps][kGroup];
-    float wl[kConsumerWarps][kGroup];
-    float wo[kConsumerWarps][kGroup][kHeadDim];
+    alignas(16) float o[kPvSplits][kGroup][kHeadDim];
+    float l[kPvSplits][kGroup];
 };
 
 struct Shared {
@@ -193,13 +200,16 @@ struct Shared {
     alignas(16) float attn[kMaxOBlocks * kStepBlock];  // merged attention dims owned
     alignas(16) float act[kMaxFeatures];      // SwiGLU of the features owned
     float gate[kMaxFeatures];
+    float up[kMaxFeatures];
+    float rope_c[kHeadDim];                   // RoPE row of the step's position
+    float rope_s[kHeadDim];
     float scratch[32];
     float cv[kConsumerWarps];
     long long ci[kConsumerWarps];
     float mm[kMaxOBlocks * kStepBlock][kMaxChunks];  // phase M: m, l, o[d] per (dim, chunk)
     float ml[kMaxOBlocks * kStepBlock][kMaxChunks];
     float mo[kMaxOBlocks * kStepBlock][kMaxChunks];
-    AttnCombine att;
+    AttnScratch att;
     volatile int abort;
     int is_last;
     int consumed;  // tiles released by the consumers
@@ -444,8 +454,10 @@ __device__ __forceinline__ unsigned long long tally_expected(int G, int r) {
 // dst[i] = base[i] + the split-K sum i, once every contributor's add has
 // landed in every replica word (bounded polls; no fence needed: count and
 // sum share the word).  NaN where a contributor's partial was out of range.
+// The per-warp sums of squares of dst are left in sh.scratch for normalise().
 __device__ bool tally_read(const StepArgs& a, Shared& sh, const unsigned long long* acc, const float* base,
                            float* dst, int G) {
+    float ss = 0.0f;  // sum of squares of dst (per-warp partials left in scratch for the RMSNorm)
     for (int i = threadIdx.x; i < kHidden; i += kStepConsumers) {
         unsigned long long w[kStepAccReplicas];
         bool ready = true;
@@ -484,28 +496,21 @@ __device__ bool tally_read(const StepArgs& a, Shared& sh, const unsigned long lo
             total += static_cast<long long>(w[r] & kTallyValueMask) - static_cast<long long>(tally_expected(G, r)) * kTallyBias;
         }
         dst[i] = bad ? __int_as_float(0x7fc00000) : base[i] + static_cast<float>(static_cast<double>(total) * kTallyUnit);
+        ss = fmaf(dst[i], dst[i], ss);
     }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) sh.scratch[threadIdx.x >> 5] = ss;
     consumer_sync();
     return !sh.abort;
 }
 
-// Sum over the 480 consumer threads (fixed order); every consumer gets it.
-__device__ float consumer_sum(Shared& sh, float v) {
-    v = warp_sum(v);
-    consumer_sync();
-    if ((threadIdx.x & 31) == 0) sh.scratch[threadIdx.x >> 5] = v;
-    consumer_sync();
-    float t = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) t += sh.scratch[w];
-    return t;
-}
-
-// xs = src * rsqrt(mean(src^2) + eps) * w (rmsnorm_cuda.cu:23-89).
+// xs = src * rsqrt(mean(src^2) + eps) * w (rmsnorm_cuda.cu:23-89); the
+// per-warp sums of squares of src are already in sh.scratch (tally_read or
+// the embedding gather wrote them before a consumer barrier).
 __device__ void normalise(Shared& sh, const float* src, const float* w, float eps) {
     float ss = 0.0f;
-    for (int i = threadIdx.x; i < kHidden; i += kStepConsumers) ss = fmaf(src[i], src[i], ss);
-    ss = consumer_sum(sh, ss);
+#pragma unroll
+    for (int q = 0; q < kConsumerWarps; ++q) ss += sh.scratch[q];
     const float inv = rsqrtf(ss / static_cast<float>(kHidden) + eps);
     for (int i = threadIdx.x; i < kHidden; i += kStepConsumers) sh.xs[i] = src[i] * inv * w[i];
     consumer_sync();
@@ -623,8 +628,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             // ------------------------------------------------------ phase A
             if (l == 0) {
                 const bool valid = s.tok >= 0 && s.tok < a.vocab;
-                for (int i = tid; i < kHidden; i += kStepConsumers)
+                float ss = 0.0f;
+                for (int i = tid; i < kHidden; i += kStepConsumers) {
                     sh.hraw[i] = valid ? __ldg(a.embedding + s.tok * kHidden + i) : 0.0f;
+                    ss = fmaf(sh.hraw[i], sh.hraw[i], ss);
+                }
+                ss = warp_sum(ss);
+                if (lane == 0) sh.scratch[warp] = ss;
+                if (tid < kHeadDim) {
+                    sh.rope_c[tid] = __ldg(a.cos_table + s.pos * kHeadDim + tid);
+                    sh.rope_s[tid] = __ldg(a.sin_table + s.pos * kHeadDim + tid);
+                }
                 consumer_sync();
             } else if (!tally_read(a, sh, down_tally(l - 1), sh.mid, sh.hraw, G)) {
                 goto done;
@@ -651,8 +665,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                         }
                     } else {
                         const int d = row % kHeadDim;
-                        const float c = __ldg(a.cos_table + s.pos * kHeadDim + d);
-                        const float sn = __ldg(a.sin_table + s.pos * kHeadDim + d);
+                        const float c = sh.rope_c[d];
+                        const float sn = sh.rope_s[d];
                         out = half ? rope_value(yb, ya, c, sn, false) : rope_value(ya, yb, c, sn, true);
                         if (kind == 1 && l16 == 0) {
                             const int h = (row - kHidden) / kHeadDim;
@@ -678,25 +692,28 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                         goto done;
                 }
                 LAYER_MARK(2);
-                const float scale = a.layer[l].scale;
-                const int l8 = lane & 7, grp = warp * 4 + (lane >> 3);
-                float4 qa[kGroup], qb[kGroup];
+                // Scores in base-2 units: s2 = (q . k) * scale * log2(e), so p = exp2(s2 - max).
+                const float scale2 = a.layer[l].scale * kLog2e;
+                // Score groups of 4 lanes; lane (gl, l4) of a warp covers the 16-byte
+                // chunks l4 + 4 m of a row, visiting m = (j + gl) % 4 at step j so the
+                // 32 lanes of one load hit 8 distinct bank groups.
+                const int l4 = lane & 3, gl = lane >> 2, g4 = warp * 8 + gl;
+                float4 qr[kGroup][4];
 #pragma unroll
-                for (int h = 0; h < kGroup; ++h) {
-                    qa[h] = reinterpret_cast<const float4*>(sh.qs + h * kHeadDim)[l8];
-                    qb[h] = reinterpret_cast<const float4*>(sh.qs + h * kHeadDim)[8 + l8];
-                }
-                // Batches of up to 4 cache tiles: scores of every row first
-                // (rows independent), one CTA-wide max, then exponentials and
-                // the P.V sums.  The running max rescales earlier batches.
-                float mrun[kGroup], lsum[kGroup], o[kGroup][8];
+                for (int h = 0; h < kGroup; ++h)
 #pragma unroll
-                for (int h = 0; h < kGroup; ++h) {
-                    mrun[h] = -INFINITY;
-                    lsum[h] = 0.0f;
+                    for (int j = 0; j < 4; ++j)
+                        qr[h][j] = reinterpret_cast<const float4*>(sh.qs + h * kHeadDim)[l4 + 4 * ((j + gl) & 3)];
+                // P.V threads: (4-dim quad, head, row split).
+                const int pq = tid & 15, ph = (tid >> 4) % kGroup, psplit = tid / (kGroup * 16);
+                float4 pacc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                float plsum = 0.0f;
+                float mrun[kGroup];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) o[h][j] = 0.0f;
-                }
+                for (int h = 0; h < kGroup; ++h) mrun[h] = -INFINITY;
+                // Batches of up to 4 cache tiles (every tile but the chunk's last
+                // holds 54 rows); the last batch also takes the new row from the
+                // exchange.  A running max rescales the earlier batches.
                 int j = 0;
                 do {
                     const int nb = min(kBatchTiles, s.n_att - j);
@@ -706,130 +723,149 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     const bool with_new = j + nb == s.n_att && s.owns_new;
                     const int rows = cached + (with_new ? 1 : 0);
                     if (!acquire_batch(a, sh, k, nb)) goto done;
-                    // Row gi of the batch: tile gi / 54 (every tile but the chunk's last is full),
-                    // or the new row (gi == cached) from the exchange.
+                    auto tile_base = [&](int gi) {
+                        return reinterpret_cast<const float*>(
+                            ring + static_cast<size_t>((k + gi / kStepAttnRows) % kStepSlots) * kStepSlotBytes);
+                    };
                     auto key_row = [&](int gi) -> const float* {
                         if (gi >= cached) return sh.knew;
-                        const int b = gi / kStepAttnRows;
-                        return reinterpret_cast<const float*>(ring + static_cast<size_t>((k + b) % kStepSlots) * kStepSlotBytes) +
-                               (gi - b * kStepAttnRows) * kHeadDim;
+                        return tile_base(gi) + (gi % kStepAttnRows) * kHeadDim;
                     };
-                    auto value_row = [&](int gi) -> const float* {
-                        if (gi >= cached) return sh.vnew;
-                        const int b = gi / kStepAttnRows;
-                        const int n = min(kStepAttnRows, cached - b * kStepAttnRows);
-                        return reinterpret_cast<const float*>(ring + static_cast<size_t>((k + b) % kStepSlots) * kStepSlotBytes) +
-                               (n + gi - b * kStepAttnRows) * kHeadDim;
-                    };
-                    float sc[kRowSlots][kGroup];
+                    // Scores of the batch's rows -> p (smem), per-warp maxima.
+                    float mb[kGroup];
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) mb[h] = -INFINITY;
 #pragma unroll
                     for (int i = 0; i < kRowSlots; ++i) {
-                        const int gi = grp + kRowGroups * i;
+                        const int gi = g4 + kRowGroups * i;
+                        if (warp * 8 + kRowGroups * i < rows) {  // warp-uniform: full-mask shuffles
+                            const float4* k4 = reinterpret_cast<const float4*>(key_row(gi < rows ? gi : 0));
+                            float d[kGroup] = {0.0f, 0.0f, 0.0f};
 #pragma unroll
-                        for (int h = 0; h < kGroup; ++h) sc[i][h] = -INFINITY;
-                        if (warp * 4 + kRowGroups * i < rows) {  // warp-uniform: full-mask shuffles
-                            const float4* k4 = reinterpret_cast<const float4*>(key_row(gi));
-                            const float4 k0 = k4[l8], k1 = k4[8 + l8];
-                            float d[kGroup];
+                            for (int jj = 0; jj < 4; ++jj) {
+                                const float4 kv = k4[l4 + 4 * ((jj + gl) & 3)];
 #pragma unroll
-                            for (int h = 0; h < kGroup; ++h) {
-                                float d0 = qa[h].x * k0.x, d1 = qb[h].x * k1.x;
-                                d0 = fmaf(qa[h].y, k0.y, d0);
-                                d1 = fmaf(qb[h].y, k1.y, d1);
-                                d0 = fmaf(qa[h].z, k0.z, d0);
-                                d1 = fmaf(qb[h].z, k1.z, d1);
-                                d0 = fmaf(qa[h].w, k0.w, d0);
-                                d1 = fmaf(qb[h].w, k1.w, d1);
-                                d[h] = d0 + d1;
+                                for (int h = 0; h < kGroup; ++h) {
+                                    d[h] = fmaf(qr[h][jj].x, kv.x, d[h]);
+                                    d[h] = fmaf(qr[h][jj].y, kv.y, d[h]);
+                                    d[h] = fmaf(qr[h][jj].z, kv.z, d[h]);
+                                    d[h] = fmaf(qr[h][jj].w, kv.w, d[h]);
+                                }
                             }
 #pragma unroll
-                            for (int off = 4; off > 0; off >>= 1)
+                            for (int off = 1; off < 4; off <<= 1)
 #pragma unroll
                                 for (int h = 0; h < kGroup; ++h) d[h] += __shfl_xor_sync(0xffffffffu, d[h], off);
-                            if (gi < rows)
+                            if (gi < rows) {
 #pragma unroll
-                                for (int h = 0; h < kGroup; ++h) sc[i][h] = d[h] * scale;
-                        }
-                    }
-#pragma unroll
-                    for (int h = 0; h < kGroup; ++h) {
-                        float mb = sc[0][h];
-#pragma unroll
-                        for (int i = 1; i < kRowSlots; ++i) mb = fmaxf(mb, sc[i][h]);
-                        mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 8));
-                        mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 16));
-                        if (lane == 0) sh.att.wm[warp][h] = mb;
-                    }
-                    consumer_sync();
-#pragma unroll
-                    for (int h = 0; h < kGroup; ++h) {
-                        float mx = sh.att.wm[0][h];
-#pragma unroll
-                        for (int w = 1; w < kConsumerWarps; ++w) mx = fmaxf(mx, sh.att.wm[w][h]);
-                        const float mn = fmaxf(mrun[h], mx);
-                        const float f = expf(mrun[h] - mn);  // first batch: mrun = -inf -> 0
-                        lsum[h] *= f;
-#pragma unroll
-                        for (int q = 0; q < 8; ++q) o[h][q] *= f;
-                        mrun[h] = mn;
-                    }
-#pragma unroll
-                    for (int i = 0; i < kRowSlots; ++i) {
-                        const int gi = grp + kRowGroups * i;
-                        if (gi < rows) {
-                            const float4* v4 = reinterpret_cast<const float4*>(value_row(gi));
-                            const float4 v0 = v4[l8], v1 = v4[8 + l8];
-#pragma unroll
-                            for (int h = 0; h < kGroup; ++h) {
-                                const float pr = expf(sc[i][h] - mrun[h]);
-                                lsum[h] += pr;
-                                o[h][0] = fmaf(pr, v0.x, o[h][0]);
-                                o[h][1] = fmaf(pr, v0.y, o[h][1]);
-                                o[h][2] = fmaf(pr, v0.z, o[h][2]);
-                                o[h][3] = fmaf(pr, v0.w, o[h][3]);
-                                o[h][4] = fmaf(pr, v1.x, o[h][4]);
-                                o[h][5] = fmaf(pr, v1.y, o[h][5]);
-                                o[h][6] = fmaf(pr, v1.z, o[h][6]);
-                                o[h][7] = fmaf(pr, v1.w, o[h][7]);
+                                for (int h = 0; h < kGroup; ++h) {
+                                    d[h] *= scale2;
+                                    mb[h] = fmaxf(mb[h], d[h]);
+                                }
+                                if (l4 < kGroup) sh.att.p[l4][gi] = l4 == 0 ? d[0] : (l4 == 1 ? d[1] : d[2]);
                             }
                         }
+                    }
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) {
+#pragma unroll
+                        for (int off = 4; off < 32; off <<= 1) mb[h] = fmaxf(mb[h], __shfl_xor_sync(0xffffffffu, mb[h], off));
+                        if (lane == 0) sh.att.wm[warp][h] = mb[h];
+                    }
+                    consumer_sync();
+                    // New running max (uniform over the CTA); rescale earlier batches.
+                    float mnew[kGroup];
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) {
+                        float mx = lane < kConsumerWarps ? sh.att.wm[lane][h] : -INFINITY;
+#pragma unroll
+                        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+                        mnew[h] = fmaxf(mrun[h], mx);
+                    }
+                    {
+                        const float mo = ph == 0 ? mrun[0] : (ph == 1 ? mrun[1] : mrun[2]);
+                        const float mn = ph == 0 ? mnew[0] : (ph == 1 ? mnew[1] : mnew[2]);
+                        const float f = exp2f(mo - mn);  // first batch: mrun = -inf -> 0
+                        pacc.x *= f;
+                        pacc.y *= f;
+                        pacc.z *= f;
+                        pacc.w *= f;
+                        plsum *= f;
+                    }
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) mrun[h] = mnew[h];
+                    // p = exp2(s2 - max), in place.
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h)
+                        for (int r = tid; r < rows; r += kStepConsumers) sh.att.p[h][r] = exp2f(sh.att.p[h][r] - mrun[h]);
+                    consumer_sync();
+                    // P.V: rows psplit, psplit + 10, ... of the batch, tile by tile.
+                    {
+                        const float* prow = sh.att.p[ph];
+                        float4 acc2 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                        for (int b = 0; b < nb; ++b) {
+                            const int base = b * kStepAttnRows;
+                            const int n = min(kStepAttnRows, cached - base);
+                            const float* vb = reinterpret_cast<const float*>(
+                                                  ring + static_cast<size_t>((k + b) % kStepSlots) * kStepSlotBytes) +
+                                              n * kHeadDim + pq * 4;
+                            int rr = psplit - base % kPvSplits;
+                            if (rr < 0) rr += kPvSplits;
+                            for (; rr + kPvSplits < n; rr += 2 * kPvSplits) {  // two rows per trip
+                                const float p0 = prow[base + rr], p1 = prow[base + rr + kPvSplits];
+                                const float4 v0 = *reinterpret_cast<const float4*>(vb + rr * kHeadDim);
+                                const float4 v1 = *reinterpret_cast<const float4*>(vb + (rr + kPvSplits) * kHeadDim);
+                                pacc.x = fmaf(p0, v0.x, pacc.x);
+                                pacc.y = fmaf(p0, v0.y, pacc.y);
+                                pacc.z = fmaf(p0, v0.z, pacc.z);
+                                pacc.w = fmaf(p0, v0.w, pacc.w);
+                                acc2.x = fmaf(p1, v1.x, acc2.x);
+                                acc2.y = fmaf(p1, v1.y, acc2.y);
+                                acc2.z = fmaf(p1, v1.z, acc2.z);
+                                acc2.w = fmaf(p1, v1.w, acc2.w);
+                                plsum += p0 + p1;
+                            }
+                            if (rr < n) {
+                                const float p0 = prow[base + rr];
+                                const float4 v0 = *reinterpret_cast<const float4*>(vb + rr * kHeadDim);
+                                pacc.x = fmaf(p0, v0.x, pacc.x);
+                                pacc.y = fmaf(p0, v0.y, pacc.y);
+                                pacc.z = fmaf(p0, v0.z, pacc.z);
+                                pacc.w = fmaf(p0, v0.w, pacc.w);
+                                plsum += p0;
+                            }
+                        }
+                        if (with_new && cached % kPvSplits == psplit) {
+                            const float p0 = prow[cached];
+                            const float4 v0 = reinterpret_cast<const float4*>(sh.vnew)[pq];
+                            pacc.x = fmaf(p0, v0.x, pacc.x);
+                            pacc.y = fmaf(p0, v0.y, pacc.y);
+                            pacc.z = fmaf(p0, v0.z, pacc.z);
+                            pacc.w = fmaf(p0, v0.w, pacc.w);
+                            plsum += p0;
+                        }
+                        pacc.x += acc2.x;
+                        pacc.y += acc2.y;
+                        pacc.z += acc2.z;
+                        pacc.w += acc2.w;
                     }
                     release_batch(sh, k, nb);
                     k += nb;
                     j += nb;
                 } while (j < s.n_att);
                 LAYER_MARK(3);
-                // Sum the 60 row groups: 4 per warp by shuffles, then the 15 warps.
-#pragma unroll
-                for (int h = 0; h < kGroup; ++h) {
-                    float lv = lsum[h];
-                    lv += __shfl_xor_sync(0xffffffffu, lv, 8);
-                    lv += __shfl_xor_sync(0xffffffffu, lv, 16);
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        float ov = o[h][q];
-                        ov += __shfl_xor_sync(0xffffffffu, ov, 8);
-                        ov += __shfl_xor_sync(0xffffffffu, ov, 16);
-                        o[h][q] = ov;
-                    }
-                    if (lane < 8) {
-                        if (lane == 0) sh.att.wl[warp][h] = lv;
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            sh.att.wo[warp][h][4 * l8 + q] = o[h][q];
-                            sh.att.wo[warp][h][32 + 4 * l8 + q] = o[h][4 + q];
-                        }
-                    }
-                }
+                // Sum the row splits.
+                reinterpret_cast<float4*>(sh.att.o[psplit][ph])[pq] = pacc;
+                if (pq == 0) sh.att.l[psplit][ph] = plsum;
                 consumer_sync();
                 if (tid < kGroup * kHeadDim) {
                     const int h = tid / kHeadDim, d = tid % kHeadDim;
-                    const float mx = h == 0 ? mrun[0] : (h == 1 ? mrun[1] : mrun[2]);
+                    const float mx = (h == 0 ? mrun[0] : (h == 1 ? mrun[1] : mrun[2])) * kLn2;  // natural-log units
                     float total = 0.0f, acc = 0.0f;
 #pragma unroll
-                    for (int w = 0; w < kConsumerWarps; ++w) {
-                        total += sh.att.wl[w][h];
-                        acc += sh.att.wo[w][h][d];
+                    for (int w = 0; w < kPvSplits; ++w) {
+                        total += sh.att.l[w][h];
+                        acc += sh.att.o[w][h][d];
                     }
                     unsigned long long* pw = a.x.partial + parity(l) * (static_cast<size_t>(kQHeads) * a.nch * kStepPartial) +
                                              ((static_cast<size_t>(s.g) * kGroup + h) * a.nch + s.c) * kStepPartial;
@@ -897,29 +933,29 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             LAYER_MARK(7);
             {
                 const int nf = (s.f1 - s.f0) * kStepBlock;
-                const int w2 = warp * 2 + half;
                 normalise(sh, sh.mid, sh.wpost, a.eps);
-                const float* t = acquire(a, sh, ring, k);
-                if (t == nullptr) goto done;
-                if (warp * 2 < nf) {  // whole warps enter the half-warp shuffles
-                    const int rr = w2 < nf ? w2 : 0;
-                    const float y = row_dot(t + rr * kHidden, sh.xs, l16);
-                    if (l16 == 0 && w2 < nf) sh.gate[w2] = y;
+                // gate, up and down tiles together: gate rows on warps 0-5, up rows on 6-11.
+                if (!acquire_batch(a, sh, k, 3)) goto done;
+                auto slot = [&](int i) {
+                    return reinterpret_cast<const float*>(ring + static_cast<size_t>((k + i) % kStepSlots) * kStepSlotBytes);
+                };
+                {
+                    const bool is_up = warp >= kMaxFeatures / 2;
+                    const int wr = is_up ? warp - kMaxFeatures / 2 : warp;
+                    const int w2 = wr * 2 + half;
+                    if (warp < kMaxFeatures && wr * 2 < nf) {  // whole warps enter the half-warp shuffles
+                        const int rr = w2 < nf ? w2 : 0;
+                        const float y = row_dot(slot(is_up ? 1 : 0) + rr * kHidden, sh.xs, l16);
+                        if (l16 == 0 && w2 < nf) (is_up ? sh.up : sh.gate)[w2] = y;
+                    }
                 }
-                release(sh, k++);
-                const float* tu = acquire(a, sh, ring, k);
-                if (tu == nullptr) goto done;
-                if (warp * 2 < nf) {
-                    const int rr = w2 < nf ? w2 : 0;
-                    const float y = row_dot(tu + rr * kHidden, sh.xs, l16);
-                    if (l16 == 0 && w2 < nf) sh.act[w2] = swiglu(sh.gate[w2], y);
-                }
-                release(sh, k++);
+                consumer_sync();
+                if (tid < nf) sh.act[tid] = swiglu(sh.gate[tid], sh.up[tid]);
+                consumer_sync();
                 LAYER_MARK(8);
-                const float* td = acquire(a, sh, ring, k);
-                if (td == nullptr) goto done;
-                tally_products(td, sh.act, s.f1 - s.f0, down_tally(l) + s.replica);
-                release(sh, k++);
+                tally_products(slot(2), sh.act, s.f1 - s.f0, down_tally(l) + s.replica);
+                release_batch(sh, k, 3);
+                k += 3;
             }
             LAYER_MARK(9);
         }
