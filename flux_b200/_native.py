@@ -108,6 +108,24 @@ class PrefillBuffers(ctypes.Structure):
     ]
 
 
+class BatchBuffers(ctypes.Structure):
+    """``fx_batch_buffers``."""
+
+    _fields_ = [
+        ("tokens", _p),
+        ("positions", _p),
+        ("logits", _p),
+        ("generated", _p),
+        ("step", _p),
+        ("key_cache", _p),
+        ("value_cache", _p),
+        ("batch", _i64),
+        ("capacity", _i64),
+        ("generated_capacity", _i64),
+        ("kernels_per_step", _i64),
+    ]
+
+
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
     "fx_last_error": (ctypes.c_char_p, []),
@@ -139,6 +157,13 @@ SIGNATURES: dict[str, tuple] = {
     "fx_decode_read_state": (_st, [_p, _i32, ctypes.POINTER(_i64)]),
     "fx_decode_get_info": (_st, [_p, ctypes.POINTER(DecodeInfo)]),
     "fx_decode_destroy": (None, [_p]),
+    "fx_batch_create": (_st, [ctypes.POINTER(ModelDesc), _i64, _i64, _p, ctypes.POINTER(_p)]),
+    "fx_batch_load": (_st, [_p, _i64, _p, _p, _p, _i64, _i64, _p]),
+    "fx_batch_step": (_st, [_p, _i64, _p]),
+    "fx_batch_wait": (_st, [_p, _p]),
+    "fx_batch_check": (_st, [_p]),
+    "fx_batch_get_buffers": (_st, [_p, ctypes.POINTER(BatchBuffers)]),
+    "fx_batch_destroy": (None, [_p]),
     "fx_prefill_create": (_st, [ctypes.POINTER(ModelDesc), _p, _i64, _p, ctypes.POINTER(_p)]),
     "fx_prefill_run": (_st, [_p, _p, _p]),
     "fx_prefill_decode": (_p, [_p]),

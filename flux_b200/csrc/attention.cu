@@ -1,0 +1,266 @@
+// Split-K decode attention over the compact cache [B][3][cap][64] (GQA, 3 q
+// heads per kv head), ragged valid lengths per sequence.
+//
+// Chunk kernel, grid (chunks, 3 kv heads, B), 256 threads: one CTA owns 128
+// cache rows of one (sequence, kv head).  Thread 0 starts two 1-D TMA bulk
+// copies (K rows, V rows; no multicast) into shared memory on separate
+// mbarriers, so scoring starts as soon as K has landed.  Scores: 16-lane
+// groups, one row each, 3 heads from one K load; softmax in base 2 over the
+// chunk; P.V with one thread per (4-dim quad, head, row split).  Each CTA
+// writes (max, sum, unnormalised o[64]) per q head -- the workspace format of
+// gqa_decode_attention_cuda.cu:551-633 -- and the merge kernel combines the
+// active chunks of each (sequence, q head).
+//
+// HBM: every K/V row of the valid lengths is read once; with 64 KB in
+// flight per CTA and three CTAs per SM the kernel streams at HBM rate when
+// the grid is large.
+#include "attention.cuh"
+
+namespace fx {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kPart = kHeadDim + 2;
+constexpr int kSplits = 5;                     // P.V row splits (5 x 3 heads x 16 quads = 240 threads)
+constexpr float kLog2e = 1.4426950408889634f;  // log2(e)
+constexpr float kLn2 = 0.6931471805599453f;    // ln(2)
+constexpr unsigned long long kWaitNs = 2000000000ull;
+
+struct ChunkShared {
+    uint64_t bar[2];
+    alignas(16) float p[kGroup][kCompactChunk];
+    float wmax[kWarps][kGroup];
+    float wsum[kWarps][kGroup];
+    alignas(16) float o[kSplits][kGroup][kHeadDim];
+    float l[kSplits][kGroup];
+    int failed;
+};
+constexpr size_t kTileBytes = static_cast<size_t>(kCompactChunk) * kHeadDim * sizeof(float);  // 32 KB
+constexpr size_t kSharedHead = (sizeof(ChunkShared) + 127) / 128 * 128;
+constexpr size_t kChunkSmem = kSharedHead + 2 * kTileBytes;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_timer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ bool try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait for phase 0 of `bar`; false if it gave up.
+__device__ bool wait_landed(uint64_t* bar) {
+    if (try_wait(bar, 0)) return true;
+    const unsigned long long t0 = global_timer();
+    while (!try_wait(bar, 0))
+        if (global_timer() - t0 > kWaitNs) return false;
+    return true;
+}
+
+__device__ __forceinline__ int64_t sequence_length(const CompactAttention& a, int64_t b) {
+    const int64_t requested = a.lengths == nullptr ? a.cap : a.lengths[b * a.length_stride];
+    return requested < 1 ? 1 : (requested > a.cap ? a.cap : requested);
+}
+
+__global__ void __launch_bounds__(kThreads) compact_chunk_kernel(const __grid_constant__ CompactAttention a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    ChunkShared& sh = *reinterpret_cast<ChunkShared*>(smem);
+    float* ktile = reinterpret_cast<float*>(smem + kSharedHead);
+    float* vtile = ktile + kCompactChunk * kHeadDim;
+    const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int64_t len = sequence_length(a, b);
+    const int64_t start = c * kCompactChunk;
+    if (start >= len) return;
+    const int n = static_cast<int>(len - start < kCompactChunk ? len - start : kCompactChunk);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const size_t row0 = ((static_cast<size_t>(b) * kKVHeads + g) * a.cap + start) * kHeadDim;
+    if (tid == 0) {
+        sh.failed = 0;
+        for (int i = 0; i < 2; ++i)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&sh.bar[i])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        const uint32_t bytes = static_cast<uint32_t>(n) * kHeadDim * sizeof(float);
+        const float* src[2] = {a.k + row0, a.v + row0};
+        float* dst[2] = {ktile, vtile};
+        for (int i = 0; i < 2; ++i) {
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&sh.bar[i])),
+                         "r"(bytes)
+                         : "memory");
+            asm volatile(
+                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                    smem_u32(dst[i])),
+                "l"(src[i]), "r"(bytes), "r"(smem_u32(&sh.bar[i]))
+                : "memory");
+        }
+    }
+    // q chunk l16 (4 dims) of the 3 q heads, pre-scaled to base-2 units.
+    const int l16 = lane & 15, grp = warp * 2 + (lane >> 4);
+    const float scale2 = a.scale * kLog2e;
+    float4 q[kGroup];
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h) {
+        q[h] = reinterpret_cast<const float4*>(a.q + (static_cast<size_t>(b) * kQHeads + g * kGroup + h) * kHeadDim)[l16];
+        q[h].x *= scale2;
+        q[h].y *= scale2;
+        q[h].z *= scale2;
+        q[h].w *= scale2;
+    }
+    __syncthreads();  // barriers initialised
+    if (!wait_landed(&sh.bar[0])) sh.failed = 1;
+    // Scores: 16 groups of 16 lanes, rows grp, grp + 16, ...
+    float mloc[kGroup] = {-INFINITY, -INFINITY, -INFINITY};
+    for (int r0 = warp * 2; r0 < n; r0 += 2 * kWarps) {  // warp-uniform: full-mask shuffles
+        const int r = r0 + (lane >> 4);
+        const float4 kv = reinterpret_cast<const float4*>(ktile + (r < n ? r : r0) * kHeadDim)[l16];
+        float d[kGroup];
+#pragma unroll
+        for (int h = 0; h < kGroup; ++h) {
+            d[h] = q[h].x * kv.x;
+            d[h] = fmaf(q[h].y, kv.y, d[h]);
+            d[h] = fmaf(q[h].z, kv.z, d[h]);
+            d[h] = fmaf(q[h].w, kv.w, d[h]);
+        }
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1)
+#pragma unroll
+            for (int h = 0; h < kGroup; ++h) d[h] += __shfl_xor_sync(0xffffffffu, d[h], off);
+        if (r < n) {
+#pragma unroll
+            for (int h = 0; h < kGroup; ++h) mloc[h] = fmaxf(mloc[h], d[h]);
+            if (l16 < kGroup) sh.p[l16][r] = l16 == 0 ? d[0] : (l16 == 1 ? d[1] : d[2]);
+        }
+    }
+    (void)grp;
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h) {
+        mloc[h] = warp_max(mloc[h]);
+        if (lane == 0) sh.wmax[warp][h] = mloc[h];
+    }
+    __syncthreads();
+    float m[kGroup], lsum[kGroup];
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h) {
+        float v = lane < kWarps ? sh.wmax[lane][h] : -INFINITY;
+        m[h] = warp_max(v);
+        lsum[h] = 0.0f;
+    }
+    for (int r = tid; r < n; r += kThreads)
+#pragma unroll
+        for (int h = 0; h < kGroup; ++h) {
+            const float e = exp2f(sh.p[h][r] - m[h]);
+            sh.p[h][r] = e;
+            lsum[h] += e;
+        }
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h) {
+        lsum[h] = warp_sum(lsum[h]);
+        if (lane == 0) sh.wsum[warp][h] = lsum[h];
+    }
+    if (!wait_landed(&sh.bar[1])) sh.failed = 1;
+    __syncthreads();
+    // P.V: thread (quad, head, split) sums rows split, split + 5, ...
+    const int pq = tid & 15, ph = (tid >> 4) % kGroup, psplit = tid / (16 * kGroup);
+    if (psplit < kSplits) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float4 acc2 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const float* prow = sh.p[ph];
+        int r = psplit;
+        for (; r + kSplits < n; r += 2 * kSplits) {
+            const float p0 = prow[r], p1 = prow[r + kSplits];
+            const float4 v0 = reinterpret_cast<const float4*>(vtile + r * kHeadDim)[pq];
+            const float4 v1 = reinterpret_cast<const float4*>(vtile + (r + kSplits) * kHeadDim)[pq];
+            acc.x = fmaf(p0, v0.x, acc.x);
+            acc.y = fmaf(p0, v0.y, acc.y);
+            acc.z = fmaf(p0, v0.z, acc.z);
+            acc.w = fmaf(p0, v0.w, acc.w);
+            acc2.x = fmaf(p1, v1.x, acc2.x);
+            acc2.y = fmaf(p1, v1.y, acc2.y);
+            acc2.z = fmaf(p1, v1.z, acc2.z);
+            acc2.w = fmaf(p1, v1.w, acc2.w);
+        }
+        if (r < n) {
+            const float p0 = prow[r];
+            const float4 v0 = reinterpret_cast<const float4*>(vtile + r * kHeadDim)[pq];
+            acc.x = fmaf(p0, v0.x, acc.x);
+            acc.y = fmaf(p0, v0.y, acc.y);
+            acc.z = fmaf(p0, v0.z, acc.z);
+            acc.w = fmaf(p0, v0.w, acc.w);
+        }
+        acc.x += acc2.x;
+        acc.y += acc2.y;
+        acc.z += acc2.z;
+        acc.w += acc2.w;
+        reinterpret_cast<float4*>(sh.o[psplit][ph])[pq] = acc;
+    }
+    __syncthreads();
+    if (tid < kGroup * kHeadDim) {
+        const int h = tid / kHeadDim, d = tid % kHeadDim;
+        float o = 0.0f;
+#pragma unroll
+        for (int s = 0; s < kSplits; ++s) o += sh.o[s][h][d];
+        float* w = a.ws + ((static_cast<size_t>(b) * kQHeads + g * kGroup + h) * a.chunks + c) * kPart;
+        if (sh.failed) o = __int_as_float(0x7fc00000);
+        w[2 + d] = o;
+        if (d == 0) {
+            float total = 0.0f;
+#pragma unroll
+            for (int w8 = 0; w8 < kWarps; ++w8) total += sh.wsum[w8][h];
+            w[0] = (h == 0 ? m[0] : (h == 1 ? m[1] : m[2])) * kLn2;  // natural-log units
+            w[1] = total;
+        }
+    }
+    if (tid == 0 && sh.failed && a.error != nullptr) atomicOr(a.error, 1u);
+}
+
+// grid (B * 9), 64 threads: combine the active chunks of one (sequence, q head).
+__global__ void __launch_bounds__(kHeadDim) compact_merge_kernel(const __grid_constant__ CompactAttention a) {
+    const int64_t bh = blockIdx.x, b = bh / kQHeads;
+    const int64_t active = (sequence_length(a, b) + kCompactChunk - 1) / kCompactChunk;
+    const float* w = a.ws + bh * a.chunks * kPart;
+    float m = -INFINITY;
+    for (int64_t c = 0; c < active; ++c) m = fmaxf(m, w[c * kPart]);
+    float total = 0.0f, acc = 0.0f;
+    const int d = threadIdx.x;
+    for (int64_t c = 0; c < active; ++c) {
+        const float f = expf(w[c * kPart] - m);
+        total = fmaf(w[c * kPart + 1], f, total);
+        acc = fmaf(w[c * kPart + 2 + d], f, acc);
+    }
+    a.out[bh * kHeadDim + d] = acc / total;
+}
+
+}  // namespace
+
+fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream) {
+    static bool configured = false;
+    if (!configured) {
+        FX_CUDA_TRY(cudaFuncSetAttribute(compact_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kChunkSmem)),
+                    "raising attention shared memory");
+        configured = true;
+    }
+    FX_REQUIRE(a.batch >= 1 && a.batch <= 65535 && a.chunks >= 1 && a.chunks <= 0x7fffffff,
+               "flux attention: batch or capacity out of range");
+    const dim3 grid(static_cast<unsigned>(a.chunks), kKVHeads, static_cast<unsigned>(a.batch));
+    compact_chunk_kernel<<<grid, kThreads, kChunkSmem, stream>>>(a);
+    FX_CUDA_TRY(cudaGetLastError(), "launching compact attention chunks");
+    compact_merge_kernel<<<static_cast<unsigned>(a.batch * kQHeads), kHeadDim, 0, stream>>>(a);
+    FX_CUDA_TRY(cudaGetLastError(), "launching compact attention merge");
+    return FX_OK;
+}
+
+}  // namespace fx

@@ -1,0 +1,601 @@
+// Batched greedy decode: B <= 64 independent sequences of SmolLM2-135M advanced
+// together, one CUDA-graph replay per step.  The reference has no batched
+// runtime (it is batch 1 only); this serves the sequence-sharded batched
+// configuration, where each GPU owns its own sequences and replicas of the
+// weights and nothing crosses GPUs.
+//
+// Per layer (10 launches): RMSNorm rows -> QKV split-K GEMM -> RoPE + cache
+// write at each sequence's own position -> compact split-K attention over
+// each sequence's valid length (attention.cu) -> o_proj GEMM + residual ->
+// RMSNorm -> gate/up GEMM + SwiGLU -> down GEMM + residual; then the final
+// norm, the tied LM head GEMM and a per-row greedy argmax that advances each
+// sequence's token and position.
+//
+// The projections are skinny GEMMs (M = B <= 64 rows of activations against
+// the weight rows): 64 x 64 output tiles over a slice of K, so that small N
+// still spreads over every SM, then a fixed-order reduction of the K slices
+// that also applies the residual add or the SwiGLU -- deterministic, FP32.
+#include "attention.cuh"
+#include "common.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+namespace fx {
+namespace {
+
+constexpr int kMaxBatch = 64;
+constexpr int kTileM = 64, kTileN = 64, kTileK = 16, kGemmThreads = 256;
+constexpr int64_t kMaxCapacity = 131072;
+
+// ------------------------------------------------------------- kernels
+
+// h[b] = embedding[tokens[b]] (zeros for an out-of-range token).
+__global__ void embed_rows_kernel(const int64_t* __restrict__ tokens, const float* __restrict__ embedding,
+                                  int64_t vocab, float* __restrict__ h) {
+    const int b = blockIdx.x;
+    const int64_t t = tokens[b];
+    const bool valid = t >= 0 && t < vocab;
+    for (int i = threadIdx.x; i < kHidden; i += blockDim.x) h[b * kHidden + i] = valid ? embedding[t * kHidden + i] : 0.0f;
+}
+
+// out[b] = x[b] * rsqrt(mean(x[b]^2) + eps) * w; one CTA per row.
+__global__ void __launch_bounds__(192) norm_rows_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                        float* __restrict__ out, float eps) {
+    __shared__ float scratch[32];
+    const int b = blockIdx.x;
+    const float* row = x + static_cast<size_t>(b) * kHidden;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < kHidden; i += blockDim.x) ss = fmaf(row[i], row[i], ss);
+    ss = block_sum(ss, scratch);
+    const float inv = rsqrtf(ss / static_cast<float>(kHidden) + eps);
+    for (int i = threadIdx.x; i < kHidden; i += blockDim.x) out[static_cast<size_t>(b) * kHidden + i] = row[i] * inv * w[i];
+}
+
+// P[split][m][n] = sum over k in the split's slice of X[m][k] * W[n][k]
+// (M <= 64).  256 threads, 4 x 4 outputs each, K staged through shared
+// memory 16 columns at a time (transposed so the inner loop reads float4s).
+__global__ void __launch_bounds__(kGemmThreads) skinny_gemm_kernel(const float* __restrict__ X,
+                                                                   const float* __restrict__ W,
+                                                                   float* __restrict__ P, int M, int N, int K,
+                                                                   int k_per_split) {
+    __shared__ __align__(16) float As[kTileK][kTileM + 4];
+    __shared__ __align__(16) float Bs[kTileK][kTileN + 4];
+    const int n0 = blockIdx.x * kTileN;
+    const int split = blockIdx.y;
+    const int k0 = split * k_per_split;
+    const int k1 = min(K, k0 + k_per_split);
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    // loader: row lr (0..63), 4 consecutive k at lk
+    const int lr = tid >> 2, lk = (tid & 3) * 4;
+    float acc[4][4] = {};
+    for (int kk = k0; kk < k1; kk += kTileK) {
+        {
+            float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f), w = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (lr < M && kk + lk < k1) a = *reinterpret_cast<const float4*>(X + static_cast<size_t>(lr) * K + kk + lk);
+            if (n0 + lr < N && kk + lk < k1) w = *reinterpret_cast<const float4*>(W + static_cast<size_t>(n0 + lr) * K + kk + lk);
+            As[lk + 0][lr] = a.x;
+            As[lk + 1][lr] = a.y;
+            As[lk + 2][lr] = a.z;
+            As[lk + 3][lr] = a.w;
+            Bs[lk + 0][lr] = w.x;
+            Bs[lk + 1][lr] = w.y;
+            Bs[lk + 2][lr] = w.z;
+            Bs[lk + 3][lr] = w.w;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < kTileK; ++k) {
+            const float4 a = *reinterpret_cast<const float4*>(&As[k][ty * 4]);
+            const float4 b = *reinterpret_cast<const float4*>(&Bs[k][tx * 4]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = ty * 4 + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int n = n0 + tx * 4 + j;
+            if (n < N) P[(static_cast<size_t>(split) * M + m) * N + n] = acc[i][j];
+        }
+    }
+}
+
+// out[m][n] = sum_s P[s][m][n] (+ residual[m][n]), splits in order.
+__global__ void reduce_splits_kernel(const float* __restrict__ P, int splits, int M, int N,
+                                     const float* __restrict__ residual, float* __restrict__ out) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(M) * N) return;
+    float v = 0.0f;
+    for (int s = 0; s < splits; ++s) v += P[static_cast<size_t>(s) * M * N + i];
+    out[i] = residual != nullptr ? residual[i] + v : v;
+}
+
+// out[m][i] = swiglu(sum_s P[s][m][i], sum_s P[s][m][I + i]) for the packed gate|up columns.
+__global__ void reduce_swiglu_kernel(const float* __restrict__ P, int splits, int M, float* __restrict__ out) {
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= static_cast<int64_t>(M) * kInter) return;
+    const int64_t m = e / kInter, i = e % kInter;
+    float g = 0.0f, u = 0.0f;
+    for (int s = 0; s < splits; ++s) {
+        const float* row = P + (static_cast<size_t>(s) * M + m) * kGateUp;
+        g += row[i];
+        u += row[kInter + i];
+    }
+    out[e] = swiglu(g, u);
+}
+
+// RoPE on q/k of every sequence at its own position, K/V rows written into
+// the layer's cache [B][3][cap][64], q -> [B][9][64], lengths[b] = pos + 1.
+// One thread per (sequence, pair): q/k pairs (d, d + 32), v single values.
+__global__ void rope_cache_rows_kernel(const float* __restrict__ qkv, const int64_t* __restrict__ positions,
+                                       const float* __restrict__ cos_table, const float* __restrict__ sin_table,
+                                       float* __restrict__ kc, float* __restrict__ vc, float* __restrict__ q,
+                                       int64_t* __restrict__ lengths, int64_t cap, int B, unsigned* __restrict__ error) {
+    constexpr int kPairs = (kQHeads + kKVHeads) * (kHeadDim / 2) + kKVHeads * kHeadDim;  // 384 + 192
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= static_cast<int64_t>(B) * kPairs) return;
+    const int b = static_cast<int>(e / kPairs), t = static_cast<int>(e % kPairs);
+    const int64_t pos = positions[b];
+    if (pos < 0 || pos >= cap) {
+        if (t == 0) atomicOr(error, 2u);
+        return;
+    }
+    if (t == 0) lengths[b] = pos + 1;
+    const float* row = qkv + static_cast<size_t>(b) * kQKV;
+    if (t < (kQHeads + kKVHeads) * (kHeadDim / 2)) {
+        const int head = t / (kHeadDim / 2), d = t % (kHeadDim / 2);  // heads 0..8 q, 9..11 k
+        const float x1 = row[head * kHeadDim + d], x2 = row[head * kHeadDim + d + kHeadDim / 2];
+        const float* c = cos_table + pos * kHeadDim;
+        const float* s = sin_table + pos * kHeadDim;
+        const float r1 = rope_value(x1, x2, c[d], s[d], true);
+        const float r2 = rope_value(x2, x1, c[d + kHeadDim / 2], s[d + kHeadDim / 2], false);
+        if (head < kQHeads) {
+            q[(static_cast<size_t>(b) * kQHeads + head) * kHeadDim + d] = r1;
+            q[(static_cast<size_t>(b) * kQHeads + head) * kHeadDim + d + kHeadDim / 2] = r2;
+        } else {
+            float* dst = kc + ((static_cast<size_t>(b) * kKVHeads + (head - kQHeads)) * cap + pos) * kHeadDim;
+            dst[d] = r1;
+            dst[d + kHeadDim / 2] = r2;
+        }
+    } else {
+        const int u = t - (kQHeads + kKVHeads) * (kHeadDim / 2);
+        vc[((static_cast<size_t>(b) * kKVHeads + u / kHeadDim) * cap + pos) * kHeadDim + u % kHeadDim] =
+            row[kHidden + kKVHeads * kHeadDim + u];
+    }
+}
+
+// One CTA per sequence: token = argmax(logits[b]) (NaN as max, lowest index
+// on ties), generated[b][step] = token, position += 1; CTA 0 advances step
+// (after every CTA read it: the step counter is read again only by the next
+// launch).
+__global__ void __launch_bounds__(1024) greedy_rows_kernel(const float* __restrict__ logits, int64_t vocab,
+                                                           int64_t* __restrict__ tokens, int64_t* __restrict__ positions,
+                                                           int64_t* __restrict__ generated, int64_t gen_cap,
+                                                           const int64_t* __restrict__ step_in, int64_t* __restrict__ step_out) {
+    __shared__ float sv[32];
+    __shared__ long long si[32];
+    const int b = blockIdx.x;
+    const float* row = logits + static_cast<size_t>(b) * vocab;
+    float bv = 0.0f;
+    long long bi = -1;
+    for (int64_t i = threadIdx.x; i < vocab; i += blockDim.x)
+        if (argmax_precedes(row[i], i, bv, bi)) {
+            bv = row[i];
+            bi = i;
+        }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float v = __shfl_xor_sync(0xffffffffu, bv, off);
+        const long long i = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (argmax_precedes(v, i, bv, bi)) {
+            bv = v;
+            bi = i;
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+            if (argmax_precedes(sv[w], si[w], bv, bi)) {
+                bv = sv[w];
+                bi = si[w];
+            }
+        const int64_t token = bi < 0 ? 0 : bi;
+        const int64_t st = *step_in;
+        tokens[b] = token;
+        positions[b] += 1;
+        if (st >= 0 && st < gen_cap) generated[static_cast<size_t>(b) * gen_cap + st] = token;
+    }
+}
+
+__global__ void advance_step_kernel(int64_t* step) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) *step += 1;
+}
+
+__global__ void set_sequence_kernel(int64_t* tokens, int64_t* positions, const int64_t* token, int64_t index,
+                                    int64_t position, int64_t* step, int64_t* generated, int64_t gen_cap) {
+    if (threadIdx.x == 0) {
+        tokens[index] = *token;
+        positions[index] = position;
+        *step = 0;
+    }
+    for (int64_t i = threadIdx.x; i < gen_cap; i += blockDim.x) generated[index * gen_cap + i] = 0;
+}
+
+struct GemmPlan {
+    int splits = 1, k_per_split = 0;
+};
+
+GemmPlan plan_gemm(int N, int K, int sms) {
+    const int tiles = (N + kTileN - 1) / kTileN;
+    int splits = std::max(1, (2 * sms + tiles - 1) / tiles);
+    splits = std::min(splits, std::max(1, K / 32));
+    int kps = (K + splits - 1) / splits;
+    kps = (kps + kTileK - 1) / kTileK * kTileK;
+    GemmPlan p;
+    p.k_per_split = kps;
+    p.splits = (K + kps - 1) / kps;
+    return p;
+}
+
+}  // namespace
+}  // namespace fx
+
+using namespace fx;
+
+struct fx_batch {
+    fx_model_desc model{};
+    int64_t batch = 0, capacity = 0, gen_cap = 0, vocab = 0;
+    int sms = 0;
+    int64_t host_max_position = 0;  // host mirror of max(positions): refuses steps past capacity
+    bool pending = false;
+    cudaStream_t capture_stream = nullptr;
+    cudaEvent_t done = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    cudaGraph_t graph = nullptr;
+    // owned device memory
+    int64_t *tokens = nullptr, *positions = nullptr, *lengths = nullptr, *generated = nullptr, *step = nullptr;
+    float *logits = nullptr, *key_cache = nullptr, *value_cache = nullptr;
+    float *h = nullptr, *h2 = nullptr, *norm = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
+    float *partials = nullptr, *attn_ws = nullptr;
+    unsigned* error = nullptr;
+    GemmPlan qkv_plan, o_plan, gu_plan, down_plan, lm_plan;
+    size_t layer_stride() const { return static_cast<size_t>(batch) * kKVHeads * capacity * kHeadDim; }
+};
+
+namespace fx {
+namespace {
+
+fx_status gemm(fx_batch* r, const float* x, const float* w, int N, int K, const GemmPlan& p, float* direct_out,
+               cudaStream_t s) {
+    const int M = static_cast<int>(r->batch);
+    float* out = p.splits == 1 && direct_out != nullptr ? direct_out : r->partials;
+    const dim3 grid((N + kTileN - 1) / kTileN, p.splits);
+    skinny_gemm_kernel<<<grid, kGemmThreads, 0, s>>>(x, w, out, M, N, K, p.k_per_split);
+    FX_CUDA_TRY(cudaGetLastError(), "launching a batched projection");
+    return FX_OK;
+}
+
+fx_status reduce(fx_batch* r, const GemmPlan& p, int N, const float* residual, float* out, cudaStream_t s) {
+    const int M = static_cast<int>(r->batch);
+    const int64_t n = static_cast<int64_t>(M) * N;
+    reduce_splits_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(r->partials, p.splits, M, N, residual, out);
+    FX_CUDA_TRY(cudaGetLastError(), "launching a split-K reduction");
+    return FX_OK;
+}
+
+fx_status run_step(fx_batch* r, cudaStream_t s) {
+    const fx_model_desc& m = r->model;
+    const int B = static_cast<int>(r->batch);
+    fx_status st;
+    embed_rows_kernel<<<B, 192, 0, s>>>(r->tokens, m.embedding, r->vocab, r->h);
+    FX_CUDA_TRY(cudaGetLastError(), "launching the embedding gather");
+    for (int l = 0; l < kLayers; ++l) {
+        float* kc = r->key_cache + l * r->layer_stride();
+        float* vc = r->value_cache + l * r->layer_stride();
+        norm_rows_kernel<<<B, 192, 0, s>>>(r->h, m.input_norm[l], r->norm, m.epsilon);
+        if ((st = gemm(r, r->norm, m.packed_qkv[l], kQKV, kHidden, r->qkv_plan, r->qkv, s)) != FX_OK) return st;
+        if (r->qkv_plan.splits > 1 && (st = reduce(r, r->qkv_plan, kQKV, nullptr, r->qkv, s)) != FX_OK) return st;
+        {
+            const int64_t n = static_cast<int64_t>(B) * ((kQHeads + kKVHeads) * (kHeadDim / 2) + kKVHeads * kHeadDim);
+            rope_cache_rows_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
+                r->qkv, r->positions, m.rope_cos, m.rope_sin, kc, vc, r->q, r->lengths, r->capacity, B, r->error);
+            FX_CUDA_TRY(cudaGetLastError(), "launching the batched RoPE / cache write");
+        }
+        CompactAttention a{};
+        a.q = r->q;
+        a.k = kc;
+        a.v = vc;
+        a.lengths = r->lengths;
+        a.length_stride = 1;
+        a.out = r->attn;
+        a.ws = r->attn_ws;
+        a.error = r->error;
+        a.scale = m.attention_scale[l];
+        a.batch = B;
+        a.cap = r->capacity;
+        a.chunks = (r->capacity + kCompactChunk - 1) / kCompactChunk;
+        if ((st = launch_compact_attention(a, s)) != FX_OK) return st;
+        if ((st = gemm(r, r->attn, m.o_proj[l], kHidden, kHidden, r->o_plan, nullptr, s)) != FX_OK) return st;
+        if ((st = reduce(r, r->o_plan, kHidden, r->h, r->h2, s)) != FX_OK) return st;
+        norm_rows_kernel<<<B, 192, 0, s>>>(r->h2, m.post_norm[l], r->norm, m.epsilon);
+        if ((st = gemm(r, r->norm, m.gate_up[l], kGateUp, kHidden, r->gu_plan, nullptr, s)) != FX_OK) return st;
+        {
+            const int64_t n = static_cast<int64_t>(B) * kInter;
+            reduce_swiglu_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(r->partials, r->gu_plan.splits, B,
+                                                                                        r->act);
+            FX_CUDA_TRY(cudaGetLastError(), "launching the batched SwiGLU");
+        }
+        if ((st = gemm(r, r->act, m.down[l], kHidden, kInter, r->down_plan, nullptr, s)) != FX_OK) return st;
+        if ((st = reduce(r, r->down_plan, kHidden, r->h2, r->h, s)) != FX_OK) return st;
+    }
+    norm_rows_kernel<<<B, 192, 0, s>>>(r->h, m.final_norm, r->norm, m.epsilon);
+    if ((st = gemm(r, r->norm, m.lm_head, static_cast<int>(r->vocab), kHidden, r->lm_plan, r->logits, s)) != FX_OK)
+        return st;
+    if (r->lm_plan.splits > 1 && (st = reduce(r, r->lm_plan, static_cast<int>(r->vocab), nullptr, r->logits, s)) != FX_OK)
+        return st;
+    greedy_rows_kernel<<<B, 1024, 0, s>>>(r->logits, r->vocab, r->tokens, r->positions, r->generated, r->gen_cap,
+                                          r->step, r->step);
+    FX_CUDA_TRY(cudaGetLastError(), "launching the batched greedy update");
+    advance_step_kernel<<<1, 32, 0, s>>>(r->step);
+    FX_CUDA_TRY(cudaGetLastError(), "advancing the batched step");
+    return FX_OK;
+}
+
+struct DeviceScope {
+    int previous = -1;
+    explicit DeviceScope(int device) {
+        cudaGetDevice(&previous);
+        if (previous != device) cudaSetDevice(device);
+    }
+    ~DeviceScope() {
+        int current = -1;
+        cudaGetDevice(&current);
+        if (previous >= 0 && current != previous) cudaSetDevice(previous);
+    }
+};
+
+void destroy_batch(fx_batch* r) {
+    if (r == nullptr) return;
+    if (r->exec) cudaGraphExecDestroy(r->exec);
+    if (r->graph) cudaGraphDestroy(r->graph);
+    if (r->done) cudaEventDestroy(r->done);
+    if (r->capture_stream) cudaStreamDestroy(r->capture_stream);
+    for (void* p : {static_cast<void*>(r->tokens), static_cast<void*>(r->logits), static_cast<void*>(r->key_cache),
+                    static_cast<void*>(r->value_cache), static_cast<void*>(r->h), static_cast<void*>(r->partials),
+                    static_cast<void*>(r->attn_ws)})
+        cudaFree(p);
+    delete r;
+}
+
+fx_status create_batch(fx_batch* r, cudaStream_t stream) {
+    FX_CUDA_TRY(cudaDeviceGetAttribute(&r->sms, cudaDevAttrMultiProcessorCount, r->model.device), "querying SM count");
+    const int64_t B = r->batch;
+    // state: tokens, positions, lengths, step, generated (one allocation)
+    const size_t state_words = 3 * B + 1 + B * r->gen_cap;
+    FX_CUDA_TRY(cudaMalloc(&r->tokens, state_words * sizeof(int64_t) + 256), "allocating batched state");
+    r->positions = r->tokens + B;
+    r->lengths = r->positions + B;
+    r->step = r->lengths + B;
+    r->generated = r->step + 1;
+    r->error = reinterpret_cast<unsigned*>(r->generated + B * r->gen_cap);
+    FX_CUDA_TRY(cudaMalloc(&r->logits, static_cast<size_t>(B) * r->vocab * sizeof(float)), "allocating batched logits");
+    const size_t cache = static_cast<size_t>(kLayers) * r->layer_stride() * sizeof(float);
+    FX_CUDA_TRY(cudaMalloc(&r->key_cache, cache), "allocating the batched K cache");
+    FX_CUDA_TRY(cudaMalloc(&r->value_cache, cache), "allocating the batched V cache");
+    // activations
+    const size_t act_floats = static_cast<size_t>(B) * (3 * kHidden + kQKV + kHidden + kHidden + kInter);
+    FX_CUDA_TRY(cudaMalloc(&r->h, act_floats * sizeof(float)), "allocating batched activations");
+    r->h2 = r->h + B * kHidden;
+    r->norm = r->h2 + B * kHidden;
+    r->qkv = r->norm + B * kHidden;
+    r->q = r->qkv + B * kQKV;
+    r->attn = r->q + B * kHidden;
+    r->act = r->attn + B * kHidden;
+    r->qkv_plan = plan_gemm(kQKV, kHidden, r->sms);
+    r->o_plan = plan_gemm(kHidden, kHidden, r->sms);
+    r->gu_plan = plan_gemm(kGateUp, kHidden, r->sms);
+    r->down_plan = plan_gemm(kHidden, kInter, r->sms);
+    r->lm_plan = plan_gemm(static_cast<int>(r->vocab), kHidden, r->sms);
+    size_t partial_floats = 0;
+    const std::pair<const GemmPlan*, int> plans[] = {{&r->qkv_plan, kQKV}, {&r->o_plan, kHidden},
+                                                     {&r->gu_plan, kGateUp}, {&r->down_plan, kHidden},
+                                                     {&r->lm_plan, static_cast<int>(r->vocab)}};
+    for (const auto& p : plans)
+        if (p.first->splits > 1)
+            partial_floats = std::max(partial_floats, static_cast<size_t>(p.first->splits) * B * p.second);
+    // gate/up always reduces through the partial buffer (SwiGLU epilogue)
+    partial_floats = std::max(partial_floats, static_cast<size_t>(r->gu_plan.splits) * B * kGateUp);
+    FX_CUDA_TRY(cudaMalloc(&r->partials, partial_floats * sizeof(float)), "allocating split-K partials");
+    FX_CUDA_TRY(cudaMalloc(&r->attn_ws, compact_attention_workspace(B, r->capacity) * sizeof(float)),
+                "allocating the attention workspace");
+    FX_CUDA_TRY(cudaMemsetAsync(r->tokens, 0, state_words * sizeof(int64_t) + 256, stream), "clearing batched state");
+    FX_CUDA_TRY(cudaMemsetAsync(r->key_cache, 0, cache, stream), "clearing the batched K cache");
+    FX_CUDA_TRY(cudaMemsetAsync(r->value_cache, 0, cache, stream), "clearing the batched V cache");
+    FX_CUDA_TRY(cudaMemsetAsync(r->logits, 0, static_cast<size_t>(B) * r->vocab * sizeof(float), stream),
+                "clearing batched logits");
+    FX_CUDA_TRY(cudaStreamCreateWithFlags(&r->capture_stream, cudaStreamNonBlocking), "creating the capture stream");
+    FX_CUDA_TRY(cudaEventCreateWithFlags(&r->done, cudaEventDisableTiming), "creating the completion event");
+    FX_CUDA_TRY(cudaStreamSynchronize(stream), "initialising the batched runtime");
+    // Load every kernel once outside capture (function attributes, modules),
+    // then restore the cleared state and capture one step.
+    fx_status st = run_step(r, r->capture_stream);
+    if (st != FX_OK) return st;
+    FX_CUDA_TRY(cudaStreamSynchronize(r->capture_stream), "warming the batched step");
+    FX_CUDA_TRY(cudaMemsetAsync(r->tokens, 0, state_words * sizeof(int64_t) + 256, r->capture_stream),
+                "clearing batched state");
+    FX_CUDA_TRY(cudaMemsetAsync(r->key_cache, 0, cache, r->capture_stream), "clearing the batched K cache");
+    FX_CUDA_TRY(cudaMemsetAsync(r->value_cache, 0, cache, r->capture_stream), "clearing the batched V cache");
+    FX_CUDA_TRY(cudaStreamBeginCapture(r->capture_stream, cudaStreamCaptureModeThreadLocal), "beginning capture");
+    st = run_step(r, r->capture_stream);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t end = cudaStreamEndCapture(r->capture_stream, &graph);
+    if (st != FX_OK) {
+        if (graph) cudaGraphDestroy(graph);
+        return st;
+    }
+    FX_CUDA_TRY(end, "ending capture");
+    r->graph = graph;
+    FX_CUDA_TRY(cudaGraphInstantiate(&r->exec, r->graph, 0), "instantiating the batched graph");
+    FX_CUDA_TRY(cudaStreamSynchronize(r->capture_stream), "finalising the batched runtime");
+    return FX_OK;
+}
+
+}  // namespace
+}  // namespace fx
+
+extern "C" fx_status fx_batch_create(const fx_model_desc* model, int64_t batch, int64_t generated_capacity,
+                                     void* stream, fx_batch** out) {
+    FX_REQUIRE(out != nullptr, "fx_batch_create: output pointer is null");
+    *out = nullptr;
+    FX_REQUIRE(model != nullptr, "flux batched decode: model description is null");
+    FX_REQUIRE(batch >= 1 && batch <= kMaxBatch, "flux batched decode: batch must be in [1, 64]");
+    FX_REQUIRE(model->vocab > 0 && model->vocab <= 0x7fffffff, "flux batched decode: vocabulary size out of range");
+    FX_REQUIRE(model->capacity >= 1 && model->capacity <= kMaxCapacity,
+               "flux batched decode: cache capacity must be in [1, 131072]");
+    FX_REQUIRE(generated_capacity >= 1 && generated_capacity <= kMaxCapacity,
+               "flux batched decode: generated capacity must be in [1, 131072]");
+    FX_REQUIRE(std::isfinite(model->epsilon) && model->epsilon > 0.0f, "flux batched decode: epsilon must be positive");
+    FX_REQUIRE(model->embedding && model->final_norm && model->lm_head && model->rope_cos && model->rope_sin,
+               "flux batched decode: a model tensor pointer is null");
+    for (int l = 0; l < kLayers; ++l) {
+        FX_REQUIRE(model->input_norm[l] && model->packed_qkv[l] && model->o_proj[l] && model->post_norm[l] &&
+                       model->gate_up[l] && model->down[l],
+                   "flux batched decode: exactly 30 complete layer descriptors are required");
+        for (const void* p : {static_cast<const void*>(model->packed_qkv[l]), static_cast<const void*>(model->o_proj[l]),
+                              static_cast<const void*>(model->gate_up[l]), static_cast<const void*>(model->down[l])})
+            FX_REQUIRE(reinterpret_cast<uintptr_t>(p) % 16 == 0, "flux batched decode: weights must be 16-byte aligned");
+    }
+    FX_REQUIRE(reinterpret_cast<uintptr_t>(model->lm_head) % 16 == 0,
+               "flux batched decode: LM head must be 16-byte aligned");
+    DeviceScope scope(model->device);
+    fx_batch* r = new fx_batch();
+    r->model = *model;
+    r->batch = batch;
+    r->capacity = model->capacity;
+    r->gen_cap = generated_capacity;
+    r->vocab = model->vocab;
+    const fx_status st = create_batch(r, as_stream(stream));
+    if (st != FX_OK) {
+        destroy_batch(r);
+        return st;
+    }
+    *out = r;
+    return FX_OK;
+}
+
+extern "C" fx_status fx_batch_load(fx_batch* r, int64_t sequence, const int64_t* token,
+                                   const float* const* key_layers, const float* const* value_layers,
+                                   int64_t source_rows, int64_t length, void* stream) {
+    FX_REQUIRE(r != nullptr && token != nullptr, "fx_batch_load: null pointer");
+    FX_REQUIRE(sequence >= 0 && sequence < r->batch, "flux batched decode: sequence index out of range");
+    FX_REQUIRE(length >= 0 && length < r->capacity, "flux batched decode: length must be within cache capacity");
+    FX_REQUIRE(length == 0 || (key_layers != nullptr && value_layers != nullptr && source_rows >= length),
+               "flux batched decode: K/V sources must hold `length` rows");
+    DeviceScope scope(r->model.device);
+    cudaStream_t s = as_stream(stream);
+    if (r->pending) FX_CUDA_TRY(cudaStreamWaitEvent(s, r->done, 0), "ordering after batched work");
+    const size_t dpitch = static_cast<size_t>(r->capacity) * kHeadDim * sizeof(float);
+    for (int l = 0; l < kLayers; ++l) {
+        float* kd = r->key_cache + l * r->layer_stride() + static_cast<size_t>(sequence) * kKVHeads * r->capacity * kHeadDim;
+        float* vd = r->value_cache + l * r->layer_stride() + static_cast<size_t>(sequence) * kKVHeads * r->capacity * kHeadDim;
+        FX_CUDA_TRY(cudaMemsetAsync(kd, 0, kKVHeads * dpitch, s), "clearing a sequence's K cache");
+        FX_CUDA_TRY(cudaMemsetAsync(vd, 0, kKVHeads * dpitch, s), "clearing a sequence's V cache");
+        if (length > 0) {
+            FX_REQUIRE(key_layers[l] != nullptr && value_layers[l] != nullptr,
+                       "flux batched decode: one K/V tensor per layer is required");
+            const size_t spitch = static_cast<size_t>(source_rows) * kHeadDim * sizeof(float);
+            const size_t width = static_cast<size_t>(length) * kHeadDim * sizeof(float);
+            FX_CUDA_TRY(cudaMemcpy2DAsync(kd, dpitch, key_layers[l], spitch, width, kKVHeads, cudaMemcpyDeviceToDevice, s),
+                        "importing a sequence's K cache");
+            FX_CUDA_TRY(cudaMemcpy2DAsync(vd, dpitch, value_layers[l], spitch, width, kKVHeads, cudaMemcpyDeviceToDevice, s),
+                        "importing a sequence's V cache");
+        }
+    }
+    set_sequence_kernel<<<1, 256, 0, s>>>(r->tokens, r->positions, token, sequence, length, r->step, r->generated,
+                                          r->gen_cap);
+    FX_CUDA_TRY(cudaGetLastError(), "installing a sequence");
+    FX_CUDA_TRY(cudaEventRecord(r->done, s), "recording the load");
+    r->pending = true;
+    r->host_max_position = std::max(r->host_max_position, length);
+    return FX_OK;
+}
+
+extern "C" fx_status fx_batch_step(fx_batch* r, int64_t steps, void* stream) {
+    FX_REQUIRE(r != nullptr, "fx_batch_step: runtime is null");
+    FX_REQUIRE(steps >= 0, "fx_batch_step: steps must be non-negative");
+    if (r->host_max_position + steps > r->capacity) {
+        set_error("flux batched decode: cache capacity exhausted");
+        return FX_ERR_EXHAUSTED;
+    }
+    DeviceScope scope(r->model.device);
+    cudaStream_t s = as_stream(stream);
+    if (r->pending) FX_CUDA_TRY(cudaStreamWaitEvent(s, r->done, 0), "ordering after batched work");
+    for (int64_t i = 0; i < steps; ++i) FX_CUDA_TRY(cudaGraphLaunch(r->exec, s), "launching the batched step");
+    FX_CUDA_TRY(cudaEventRecord(r->done, s), "recording the batched step");
+    r->pending = true;
+    r->host_max_position += steps;
+    return FX_OK;
+}
+
+extern "C" fx_status fx_batch_wait(fx_batch* r, void* stream) {
+    FX_REQUIRE(r != nullptr, "fx_batch_wait: runtime is null");
+    DeviceScope scope(r->model.device);
+    if (r->pending) FX_CUDA_TRY(cudaStreamWaitEvent(as_stream(stream), r->done, 0), "ordering after batched work");
+    return FX_OK;
+}
+
+extern "C" fx_status fx_batch_check(fx_batch* r) {
+    FX_REQUIRE(r != nullptr, "fx_batch_check: runtime is null");
+    DeviceScope scope(r->model.device);
+    if (r->pending) FX_CUDA_TRY(cudaEventSynchronize(r->done), "waiting for batched work");
+    unsigned error = 0;
+    FX_CUDA_TRY(cudaMemcpy(&error, r->error, sizeof(error), cudaMemcpyDeviceToHost), "reading the batched error word");
+    if (error & 2u) {
+        set_error("flux batched decode: a sequence position is outside the cache capacity");
+        return FX_ERR_DEVICE;
+    }
+    if (error & 1u) {
+        set_error("flux batched decode: a bounded wait in the attention kernel gave up");
+        return FX_ERR_DEVICE;
+    }
+    return FX_OK;
+}
+
+extern "C" fx_status fx_batch_get_buffers(const fx_batch* r, fx_batch_buffers* out) {
+    FX_REQUIRE(r != nullptr && out != nullptr, "fx_batch_get_buffers: null pointer");
+    out->tokens = r->tokens;
+    out->positions = r->positions;
+    out->logits = r->logits;
+    out->generated = r->generated;
+    out->step = r->step;
+    out->key_cache = r->key_cache;
+    out->value_cache = r->value_cache;
+    out->batch = r->batch;
+    out->capacity = r->capacity;
+    out->generated_capacity = r->gen_cap;
+    out->kernels_per_step = 2 + kLayers * 10 + 3 + (r->qkv_plan.splits > 1 ? kLayers : 0) +
+                            (r->lm_plan.splits > 1 ? 1 : 0);
+    return FX_OK;
+}
+
+extern "C" void fx_batch_destroy(fx_batch* r) {
+    if (r == nullptr) return;
+    DeviceScope scope(r->model.device);
+    if (r->pending && r->done != nullptr) cudaEventSynchronize(r->done);
+    destroy_batch(r);
+}

@@ -3,6 +3,7 @@
 // These keep the reference operators' semantics (argument meaning, error
 // behaviour, rounding of the RoPE products); the fused decode step lives in
 // decode.cu.  None of them is on the timed decode path.
+#include "attention.cuh"
 #include "common.cuh"
 
 #include <algorithm>
@@ -520,6 +521,25 @@ extern "C" fx_status fx_gqa_decode_attention_f32(const float* query, const int64
         for (int d = 0; d < 4; ++d)
             FX_REQUIRE(mask_sizes4[d] == 1 || mask_sizes4[d] == target[d],
                        "fx_gqa_decode_attention_f32: mask is not broadcastable");
+    }
+    // SmolLM2 geometry over contiguous compact caches: the TMA-staged kernel
+    // (attention.cu), same workspace format.
+    const int64_t q_compact[4] = {query_heads * head_dim, head_dim, head_dim, 1};
+    const int64_t kv_compact[4] = {kv_heads * capacity * head_dim, capacity * head_dim, head_dim, 1};
+    bool compact = mask == nullptr && head_dim == kHeadDim && query_heads == kQHeads && kv_heads == kKVHeads &&
+                   reinterpret_cast<uintptr_t>(key_cache) % 16 == 0 && reinterpret_cast<uintptr_t>(value_cache) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(query) % 16 == 0;
+    for (int d = 0; d < 4 && compact; ++d) {
+        if (d != 2 && query_strides4[d] != q_compact[d]) compact = false;
+        if (key_strides4[d] != kv_compact[d] || value_strides4[d] != kv_compact[d]) compact = false;
+    }
+    if (compact) {
+        CompactAttention c{};
+        c.q = query; c.k = key_cache; c.v = value_cache;
+        c.lengths = cache_length; c.length_stride = 0;
+        c.out = output; c.ws = workspace; c.error = nullptr; c.scale = scale;
+        c.batch = batch; c.cap = capacity; c.chunks = chunks;
+        return launch_compact_attention(c, as_stream(stream));
     }
     a.mask = mask; a.length = cache_length; a.out = output; a.ws = workspace; a.scale = scale;
     a.batch = batch; a.hq = query_heads; a.hkv = kv_heads; a.cap = capacity; a.dim = head_dim; a.chunks = chunks;

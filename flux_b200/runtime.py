@@ -659,7 +659,105 @@ def native_smollm2_greedy_generate(model: nn.Module, input_ids: torch.Tensor, *,
     return torch.cat((input_ids, generated), dim=-1)
 
 
+class NativeSmolLM2BatchedDecode:
+    """Greedy decode of ``batch`` (1..64) independent sequences advanced
+    together, one CUDA-graph replay per step (``fx_batch_*``).
+
+    No counterpart in the reference, whose runtime is batch 1 only; the
+    sequence-sharded batched configuration runs one of these per GPU with its
+    own sequences and nothing shared between GPUs.  Sequence ``i`` is installed
+    with :meth:`load` from a compact per-layer cache ``[1, 3, rows, 64]`` (or
+    ``[3, rows, 64]``) and its next input token; :meth:`step` then advances
+    every sequence by greedy steps, each at its own position."""
+
+    _PREFIX = "flux native batched decode"
+
+    def __init__(self, model: nn.Module, batch: int, cache_capacity: int, generated_capacity: int | None = None):
+        if not 1 <= batch <= 64:
+            raise ValueError("batched decode supports 1 to 64 sequences per runtime")
+        if cache_capacity < 1 or cache_capacity > int(model.config.max_position_embeddings):
+            raise ValueError("requested native cache exceeds the model position limit")
+        if not native_smollm2_runtime_is_available():
+            raise RuntimeError(f"flux_b200 native runtime is not available: {_native.load_error()}")
+        device = next(model.parameters()).device
+        cos, sin = _rope_tables(model, cache_capacity, device)
+        weights = _model_weights(model)
+        desc = _model_desc(weights, cos, sin, cache_capacity, self._PREFIX)
+        generated_capacity = cache_capacity if generated_capacity is None else int(generated_capacity)
+        handle = ctypes.c_void_p()
+        lib = _native.load()
+        with torch.cuda.device(device):
+            _native.check(lib.fx_batch_create(ctypes.byref(desc), batch, generated_capacity, _stream(device),
+                                              ctypes.byref(handle)))
+        self._owner = _OwnedHandle(handle.value, "fx_batch_destroy", (weights, cos, sin, desc))
+        self._handle = handle.value
+        self._device = device
+        self.batch = batch
+        self.capacity = cache_capacity
+        b = _native.BatchBuffers()
+        _native.check(lib.fx_batch_get_buffers(self._handle, ctypes.byref(b)))
+        vocab = int(weights["embedding"].shape[0])
+        self._tokens = _view(b.tokens, (batch,), torch.long, self._owner, device)
+        self._positions = _view(b.positions, (batch,), torch.long, self._owner, device)
+        self._logits = _view(b.logits, (batch, vocab), torch.float32, self._owner, device)
+        self._generated = _view(b.generated, (batch, b.generated_capacity), torch.long, self._owner, device)
+        self._step = _view(b.step, (1,), torch.long, self._owner, device)
+        shape = (LAYERS, batch, 3, cache_capacity, 64)
+        self._key_cache = _view(b.key_cache, shape, torch.float32, self._owner, device)
+        self._value_cache = _view(b.value_cache, shape, torch.float32, self._owner, device)
+        self.kernels_per_step = int(b.kernels_per_step)
+
+    def load(self, index: int, token: torch.Tensor | int, key_caches: Sequence[torch.Tensor],
+             value_caches: Sequence[torch.Tensor], length: int) -> None:
+        """Install sequence ``index``: ``length`` cached rows per layer and its next input token."""
+        if not 0 <= index < self.batch:
+            raise ValueError("sequence index out of range")
+        if not 0 <= length < self.capacity:
+            raise RuntimeError(f"{self._PREFIX}: length must be within cache capacity")
+        if not isinstance(token, torch.Tensor):
+            token = torch.tensor([int(token)], dtype=torch.long, device=self._device)
+        token = token.reshape(1).to(device=self._device, dtype=torch.long).contiguous()
+        rows, keys, values = 0, None, None
+        if length > 0:
+            if len(key_caches) != LAYERS or len(value_caches) != LAYERS:
+                raise RuntimeError(f"{self._PREFIX}: one K/V tensor per layer is required")
+            srcs = []
+            for t in list(key_caches) + list(value_caches):
+                t3 = t.reshape(3, t.shape[-2], 64) if t.dim() in (3, 4) else t
+                if t3.device != self._device or t3.dtype != torch.float32 or not t3.is_contiguous():
+                    raise RuntimeError(f"{self._PREFIX}: K/V sources must be contiguous float32 on the runtime device")
+                srcs.append(t3)
+            rows = int(srcs[0].shape[1])
+            if rows < length or any(int(t.shape[1]) != rows for t in srcs):
+                raise RuntimeError(f"{self._PREFIX}: K/V sources must hold `length` rows")
+            keys = _native.pointer_array(t.data_ptr() for t in srcs[:LAYERS])
+            values = _native.pointer_array(t.data_ptr() for t in srcs[LAYERS:])
+            self._keepalive = (srcs, token)
+        with torch.cuda.device(self._device):
+            _native.check(_native.load().fx_batch_load(self._handle, index, token.data_ptr(), keys, values, rows,
+                                                       length, _stream(self._device)))
+
+    def step(self, steps: int = 1) -> torch.Tensor:
+        """Enqueue ``steps`` greedy steps; returns the (stable) logits ``[B, vocab]`` of the last."""
+        with torch.cuda.device(self._device):
+            _native.check(_native.load().fx_batch_step(self._handle, steps, _stream(self._device)))
+        return self._logits
+
+    def check(self) -> None:
+        """Wait for enqueued steps; raise if a kernel reported an error."""
+        _native.check(_native.load().fx_batch_check(self._handle))
+
+    def logits(self) -> torch.Tensor: return self._logits
+    def tokens(self) -> torch.Tensor: return self._tokens
+    def positions(self) -> torch.Tensor: return self._positions
+    def generated_tokens(self) -> torch.Tensor: return self._generated
+    def device_generation_step(self) -> torch.Tensor: return self._step
+    def key_cache(self) -> torch.Tensor: return self._key_cache
+    def value_cache(self) -> torch.Tensor: return self._value_cache
+
+
 __all__ = [
-    "NativeDecodeRuntimeMemory", "NativePrefillRuntimeMemory", "NativeSmolLM2Decode", "NativeSmolLM2Prefill",
-    "native_smollm2_greedy_generate", "native_smollm2_prefill_is_available", "native_smollm2_runtime_is_available",
+    "NativeDecodeRuntimeMemory", "NativePrefillRuntimeMemory", "NativeSmolLM2BatchedDecode", "NativeSmolLM2Decode",
+    "NativeSmolLM2Prefill", "native_smollm2_greedy_generate", "native_smollm2_prefill_is_available",
+    "native_smollm2_runtime_is_available",
 ]

@@ -308,6 +308,55 @@ FX_API fx_status fx_prefill_get_buffers(const fx_prefill* runtime, fx_prefill_bu
 FX_API int64_t fx_prefill_prompt_length(const fx_prefill* runtime);
 FX_API void fx_prefill_destroy(fx_prefill* runtime);
 
+/* ------------------------------------------------------------------------
+ * Batched greedy decode: 1 to 64 independent sequences advanced together,
+ * one CUDA-graph replay per step.  No counterpart in the reference (its
+ * decode runtime and attention op are batch 1 only,
+ * csrc/gqa_decode_attention/gqa_decode_attention_torch.cpp:35-36); it serves
+ * the sequence-sharded batched configuration: each GPU holds its own
+ * sequences and weights, nothing crosses GPUs.  Same weights descriptor as
+ * the batch-1 runtime (borrowed); model->capacity is the cache capacity of
+ * every sequence and the rope-table row count.
+ * ---------------------------------------------------------------------- */
+
+typedef struct fx_batch fx_batch;
+
+typedef struct fx_batch_buffers {
+    int64_t* tokens;             /* [B] input token of each sequence's next step */
+    int64_t* positions;          /* [B] cache row each sequence's next step writes */
+    float* logits;               /* [B, vocab] of the last step */
+    int64_t* generated;          /* [B, generated_capacity] greedy tokens emitted per sequence */
+    int64_t* step;               /* [1] steps since the last fx_batch_load */
+    float* key_cache;            /* [30, B, 3, capacity, 64] */
+    float* value_cache;          /* [30, B, 3, capacity, 64] */
+    int64_t batch;
+    int64_t capacity;
+    int64_t generated_capacity;
+    int64_t kernels_per_step;    /* launches in one step's graph */
+} fx_batch_buffers;
+
+/* Allocate caches and state for `batch` sequences and capture the step graph
+ * (synchronous). */
+FX_API fx_status fx_batch_create(const fx_model_desc* model, int64_t batch, int64_t generated_capacity,
+                                 void* stream, fx_batch** out);
+/* Install sequence `sequence`: rows [0, length) of every layer's K/V from
+ * key_layers[l] / value_layers[l] ([3, source_rows, 64] each; may be NULL
+ * when length == 0), next input token *token (device), position = length;
+ * clears its generated row and resets the step counter. */
+FX_API fx_status fx_batch_load(fx_batch* runtime, int64_t sequence, const int64_t* token,
+                               const float* const* key_layers, const float* const* value_layers,
+                               int64_t source_rows, int64_t length, void* stream);
+/* Enqueue `steps` greedy steps for every sequence; FX_ERR_EXHAUSTED if a
+ * sequence would pass the cache capacity. */
+FX_API fx_status fx_batch_step(fx_batch* runtime, int64_t steps, void* stream);
+/* Make `stream` wait for the runtime's enqueued work. */
+FX_API fx_status fx_batch_wait(fx_batch* runtime, void* stream);
+/* Wait for the runtime's work and report a device-side error
+ * (FX_ERR_DEVICE: a position outside capacity, a bounded wait gave up). */
+FX_API fx_status fx_batch_check(fx_batch* runtime);
+FX_API fx_status fx_batch_get_buffers(const fx_batch* runtime, fx_batch_buffers* out);
+FX_API void fx_batch_destroy(fx_batch* runtime);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif
