@@ -14,6 +14,12 @@ Under torchrun with N > 1 every rank runs an independent replica (the batch-1
 path does not shard; no collective is on the data path) and the value is the
 max over ranks.
 
+The line also carries ``batched`` (configs[3]: 64 ragged sequences per GPU,
+greedy steps through the batched runtime, sequences sharded by rank with no
+collective; aggregate tokens/s over all ranks, max-over-ranks time) and, at
+N = 1, ``attention`` (configs[4]: the isolated decode attention GB/s over
+B in {1, 16, 64, 256} x L in {128, 1024, 8192}, L2 flushed per launch).
+
 ``--impl reference`` times the reference's own FP32 CPU path (transformers
 ``LlamaForCausalLM`` eager, as ``benchmarks/benchmark_flux.py:533-564`` drives
 it) on the host cores for the same config, rank 0 only.
@@ -52,6 +58,9 @@ def parse_args(argv=None):
     p.add_argument("--context", type=int, default=8192)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--batched-steps", type=int, default=256, help="greedy steps of the batched configuration")
+    p.add_argument("--no-batched", action="store_true", help="skip the batched configuration")
+    p.add_argument("--no-attention", action="store_true", help="skip the isolated-attention sweep")
     return p.parse_args(argv)
 
 
@@ -221,6 +230,17 @@ def run_native(args) -> dict | None:
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     elapsed_ms, e2e_ms = times.tolist()
+    peaks = measured_peaks()
+    peak = peaks.get("hbm_gbs")
+    peak_src = "measured" if peak else "fallback"
+    peak = peak or FALLBACK_HBM_GBS
+    del runtime, native
+    torch.cuda.empty_cache()
+    batched = None
+    if not args.no_batched:
+        with torch.inference_mode():
+            batched = run_batched(args, model, device, world, rank, peak, peak_src)
+        torch.cuda.empty_cache()
     if rank != 0:
         return None
 
@@ -229,10 +249,6 @@ def run_native(args) -> dict | None:
     first_len = ctx + W + 1
     mean_len = first_len + (K - 1) / 2.0
     bytes_per_step = WEIGHT_BYTES + KV_BYTES_PER_ROW * mean_len + KV_BYTES_PER_ROW
-    peaks = measured_peaks()
-    peak = peaks.get("hbm_gbs")
-    peak_src = "measured" if peak else "fallback"
-    peak = peak or FALLBACK_HBM_GBS
     achieved = bytes_per_step / (ms_per_step * 1e-3) / 1e9
     line = {
         "metric": METRIC,
@@ -267,9 +283,126 @@ def run_native(args) -> dict | None:
         "gpu_launches": int(kernels_per_step * K),
         "clocks": clocks.summary(),
     }
+    if batched is not None:
+        line["batched"] = batched
+    if world == 1 and not args.no_attention:
+        line["attention"] = run_attention_sweep(device, peak)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cpu_model, config, ctx)
     return line
+
+
+BATCH = 64                      # sequences per GPU
+BATCH_CONTEXT = (512, 4096)     # ragged contexts drawn uniformly (seeded)
+
+
+def run_batched(args, model, device, world: int, rank: int, peak: float, peak_src: str) -> dict | None:
+    """64 independent sequences per GPU, ragged contexts ~U[512, 4096]
+    (seeded per rank), greedy steps through ``NativeSmolLM2BatchedDecode``;
+    sequences are sharded by rank with no collective on the data path.  Caches
+    are seeded N(0, 0.5) rows (no prefill; the step does not depend on how the
+    rows were produced)."""
+    import torch.distributed as dist
+    from flux_b200.runtime import NativeSmolLM2BatchedDecode
+    steps, warm = args.batched_steps, max(3, args.warmup)
+    gen = torch.Generator().manual_seed(args.seed * 1000 + 17 + rank)
+    lengths = torch.randint(BATCH_CONTEXT[0], BATCH_CONTEXT[1] + 1, (BATCH,), generator=gen).tolist()
+    tokens = torch.randint(0, 49152, (BATCH,), generator=gen).tolist()
+    capacity = BATCH_CONTEXT[1] + warm + steps + 1
+    runtime = NativeSmolLM2BatchedDecode(model, BATCH, capacity)
+    dgen = torch.Generator(device=device).manual_seed(args.seed * 1000 + 29 + rank)
+    for i, n in enumerate(lengths):
+        keys = torch.randn(30, 3, n, 64, device=device, generator=dgen) * 0.5
+        values = torch.randn(30, 3, n, 64, device=device, generator=dgen) * 0.5
+        runtime.load(i, tokens[i], list(keys), list(values), n)
+        runtime.check()
+        del keys, values
+    stream = torch.cuda.current_stream(device)
+    runtime.step(warm)
+    runtime.check()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    runtime.step(steps)
+    end.record(stream)
+    torch.cuda.synchronize()
+    runtime.check()
+    if world > 1:
+        dist.barrier()
+    ms = torch.tensor([start.elapsed_time(end)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    if rank != 0:
+        return None
+    ms_per_step = ms / steps
+    mean_rows = sum(lengths) / BATCH + warm + (steps - 1) / 2.0 + 1
+    bytes_per_step = WEIGHT_BYTES + KV_BYTES_PER_ROW * BATCH * mean_rows
+    achieved = bytes_per_step / (ms_per_step * 1e-3) / 1e9
+    return {
+        "metric": "batched decode tokens/s (64 sequences per GPU)", "value": round(world * BATCH * steps / (ms * 1e-3), 1),
+        "unit": "tokens/s", "higher_is_better": True, "n_gpus": world, "scaling": "weak", "steps": steps,
+        "warmup": warm, "ms_per_step": round(ms_per_step, 4),
+        "tokens_per_s_per_gpu": round(BATCH * steps / (ms * 1e-3), 1),
+        "config": {"workload": "configs[3]: 64 independent sequences per GPU, ragged contexts ~U[512,4096] "
+                               "(seeded per rank), greedy steps, sequences sharded by rank, no collective",
+                   "contexts_rank0": {"min": min(lengths), "max": max(lengths), "mean": round(sum(lengths) / BATCH, 1)},
+                   "data": "seeded N(0,0.5) cache rows, seeded uniform tokens"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "algorithmic_bytes_per_step": int(bytes_per_step),
+                     "peak_source": peak_src},
+        "gpu_launches": int(runtime.kernels_per_step * steps),
+    }
+
+
+def run_attention_sweep(device, peak: float) -> dict:
+    """the compact decode attention alone through the C ABI,
+    Q/K/V ~ N(0, 1) seeded, B x L grid, L2 flushed before every launch; each
+    launch is replayed from a CUDA graph so host submission is not timed."""
+    from flux_b200 import _native
+    lib = _native.load()
+    flush = torch.empty(64 * 1024 * 1024, device=device)  # 256 MB > L2
+    stream = torch.cuda.Stream(device)
+    rows = []
+    for batch in (1, 16, 64, 256):
+        for length in (128, 1024, 8192):
+            g = torch.Generator(device=device).manual_seed(batch * 7 + length)
+            q = torch.randn(batch, 9, 1, 64, device=device, generator=g)
+            k = torch.randn(batch, 3, length, 64, device=device, generator=g)
+            v = torch.randn(batch, 3, length, 64, device=device, generator=g)
+            ln = torch.tensor(length, device=device)
+            out = torch.empty(batch, 9, 1, 64, device=device)
+            floats = lib.fx_gqa_decode_attention_workspace_floats(batch, 9, length, 64)
+            ws = torch.empty(floats, device=device)
+            args = (q.data_ptr(), _native.int64_array(q.stride()), k.data_ptr(), _native.int64_array(k.stride()),
+                    v.data_ptr(), _native.int64_array(v.stride()), None, None, None, ln.data_ptr(), out.data_ptr(),
+                    ws.data_ptr(), floats, 0.125, batch, 9, 3, length, 64)
+            with torch.cuda.stream(stream):
+                _native.check(lib.fx_gqa_decode_attention_f32(*args, stream.cuda_stream))  # loads the kernels
+                stream.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    _native.check(lib.fx_gqa_decode_attention_f32(*args, stream.cuda_stream))
+                times = []
+                for it in range(13):
+                    flush.fill_(float(it))
+                    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s.record(stream)
+                    graph.replay()
+                    e.record(stream)
+                    stream.synchronize()
+                    if it >= 3:
+                        times.append(s.elapsed_time(e))
+            t = statistics.median(times) * 1e-3
+            nbytes = batch * (1536 * length + 4608)
+            rows.append({"B": batch, "L": length, "us": round(t * 1e6, 2), "GBps": round(nbytes / t / 1e9, 1),
+                         "frac": round(nbytes / t / 1e9 / peak, 3)})
+            del graph, q, k, v, out, ws
+    return {"metric": "isolated decode attention GB/s (configs[4])", "unit": "GB/s", "peak": peak,
+            "algorithmic_bytes": "B*(1536*L + 4608)", "l2": "flushed (256 MB write) before every launch",
+            "rows": rows}
 
 
 def cpu_baseline(cpu_model, config, ctx: int, budget_s: float = 15.0) -> dict:
