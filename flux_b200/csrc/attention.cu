@@ -26,19 +26,24 @@ constexpr int kSplits = 5;                     // P.V row splits (5 x 3 heads x 
 constexpr float kLog2e = 1.4426950408889634f;  // log2(e)
 constexpr float kLn2 = 0.6931471805599453f;    // ln(2)
 constexpr unsigned long long kWaitNs = 2000000000ull;
+constexpr int kMergeMaxChunks = 2048;          // 131072 rows / 64
 
+template <int kRows>
 struct ChunkShared {
     uint64_t bar[2];
-    alignas(16) float p[kGroup][kCompactChunk];
+    alignas(16) float p[kGroup][kRows];
     float wmax[kWarps][kGroup];
     float wsum[kWarps][kGroup];
     alignas(16) float o[kSplits][kGroup][kHeadDim];
     float l[kSplits][kGroup];
     int failed;
 };
-constexpr size_t kTileBytes = static_cast<size_t>(kCompactChunk) * kHeadDim * sizeof(float);  // 32 KB
-constexpr size_t kSharedHead = (sizeof(ChunkShared) + 127) / 128 * 128;
-constexpr size_t kChunkSmem = kSharedHead + 2 * kTileBytes;
+template <int kRows>
+constexpr size_t tile_bytes() { return static_cast<size_t>(kRows) * kHeadDim * sizeof(float); }
+template <int kRows>
+constexpr size_t shared_head() { return (sizeof(ChunkShared<kRows>) + 127) / 128 * 128; }
+template <int kRows>
+constexpr size_t chunk_smem() { return shared_head<kRows>() + 2 * tile_bytes<kRows>(); }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -76,16 +81,17 @@ __device__ __forceinline__ int64_t sequence_length(const CompactAttention& a, in
     return requested < 1 ? 1 : (requested > a.cap ? a.cap : requested);
 }
 
+template <int kRows>
 __global__ void __launch_bounds__(kThreads) compact_chunk_kernel(const __grid_constant__ CompactAttention a) {
     extern __shared__ __align__(128) unsigned char smem[];
-    ChunkShared& sh = *reinterpret_cast<ChunkShared*>(smem);
-    float* ktile = reinterpret_cast<float*>(smem + kSharedHead);
-    float* vtile = ktile + kCompactChunk * kHeadDim;
+    ChunkShared<kRows>& sh = *reinterpret_cast<ChunkShared<kRows>*>(smem);
+    float* ktile = reinterpret_cast<float*>(smem + shared_head<kRows>());
+    float* vtile = ktile + kRows * kHeadDim;
     const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int64_t len = sequence_length(a, b);
-    const int64_t start = c * kCompactChunk;
+    const int64_t start = c * kRows;
     if (start >= len) return;
-    const int n = static_cast<int>(len - start < kCompactChunk ? len - start : kCompactChunk);
+    const int n = static_cast<int>(len - start < kRows ? len - start : kRows);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const size_t row0 = ((static_cast<size_t>(b) * kKVHeads + g) * a.cap + start) * kHeadDim;
     if (tid == 0) {
@@ -226,21 +232,42 @@ __global__ void __launch_bounds__(kThreads) compact_chunk_kernel(const __grid_co
     if (tid == 0 && sh.failed && a.error != nullptr) atomicOr(a.error, 1u);
 }
 
-// grid (B * 9), 64 threads: combine the active chunks of one (sequence, q head).
+// grid (B * 9), 64 threads: combine the active chunks of one (sequence, q
+// head).  The chunk weights exp(m_c - max) / sum are computed once per chunk
+// (cooperatively) into shared memory, then thread d sums o_c[d] over chunks.
 __global__ void __launch_bounds__(kHeadDim) compact_merge_kernel(const __grid_constant__ CompactAttention a) {
+    __shared__ float weight[kMergeMaxChunks];
+    __shared__ float scratch[2];
     const int64_t bh = blockIdx.x, b = bh / kQHeads;
-    const int64_t active = (sequence_length(a, b) + kCompactChunk - 1) / kCompactChunk;
+    const int rows = a.chunk_rows;
+    const int active = static_cast<int>((sequence_length(a, b) + rows - 1) / rows);
     const float* w = a.ws + bh * a.chunks * kPart;
+    const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
     float m = -INFINITY;
-    for (int64_t c = 0; c < active; ++c) m = fmaxf(m, w[c * kPart]);
-    float total = 0.0f, acc = 0.0f;
-    const int d = threadIdx.x;
-    for (int64_t c = 0; c < active; ++c) {
-        const float f = expf(w[c * kPart] - m);
-        total = fmaf(w[c * kPart + 1], f, total);
-        acc = fmaf(w[c * kPart + 2 + d], f, acc);
+    for (int c = d; c < active; c += kHeadDim) m = fmaxf(m, w[static_cast<size_t>(c) * kPart]);
+    m = warp_max(m);
+    if (lane == 0) scratch[warp] = m;
+    __syncthreads();
+    m = fmaxf(scratch[0], scratch[1]);
+    __syncthreads();
+    float total = 0.0f;
+    for (int c = d; c < active; c += kHeadDim) {
+        const float f = expf(w[static_cast<size_t>(c) * kPart] - m);
+        weight[c] = f;
+        total = fmaf(w[static_cast<size_t>(c) * kPart + 1], f, total);
     }
-    a.out[bh * kHeadDim + d] = acc / total;
+    total = warp_sum(total);
+    if (lane == 0) scratch[warp] = total;
+    __syncthreads();
+    total = scratch[0] + scratch[1];
+    float acc = 0.0f, acc2 = 0.0f;
+    int c = 0;
+    for (; c + 1 < active; c += 2) {
+        acc = fmaf(w[static_cast<size_t>(c) * kPart + 2 + d], weight[c], acc);
+        acc2 = fmaf(w[static_cast<size_t>(c + 1) * kPart + 2 + d], weight[c + 1], acc2);
+    }
+    if (c < active) acc = fmaf(w[static_cast<size_t>(c) * kPart + 2 + d], weight[c], acc);
+    a.out[bh * kHeadDim + d] = (acc + acc2) / total;
 }
 
 }  // namespace
@@ -248,15 +275,23 @@ __global__ void __launch_bounds__(kHeadDim) compact_merge_kernel(const __grid_co
 fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream) {
     static bool configured = false;
     if (!configured) {
-        FX_CUDA_TRY(cudaFuncSetAttribute(compact_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kChunkSmem)),
+        FX_CUDA_TRY(cudaFuncSetAttribute(compact_chunk_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(chunk_smem<128>())),
+                    "raising attention shared memory");
+        FX_CUDA_TRY(cudaFuncSetAttribute(compact_chunk_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(chunk_smem<64>())),
                     "raising attention shared memory");
         configured = true;
     }
-    FX_REQUIRE(a.batch >= 1 && a.batch <= 65535 && a.chunks >= 1 && a.chunks <= 0x7fffffff,
+    FX_REQUIRE(a.chunk_rows == 64 || a.chunk_rows == 128, "flux attention: chunks are 64 or 128 rows");
+    FX_REQUIRE(a.batch >= 1 && a.batch <= 65535 && a.chunks >= 1 && a.chunks <= kMergeMaxChunks &&
+                   a.chunks * a.chunk_rows >= a.cap,
                "flux attention: batch or capacity out of range");
     const dim3 grid(static_cast<unsigned>(a.chunks), kKVHeads, static_cast<unsigned>(a.batch));
-    compact_chunk_kernel<<<grid, kThreads, kChunkSmem, stream>>>(a);
+    if (a.chunk_rows == 128)
+        compact_chunk_kernel<128><<<grid, kThreads, chunk_smem<128>(), stream>>>(a);
+    else
+        compact_chunk_kernel<64><<<grid, kThreads, chunk_smem<64>(), stream>>>(a);
     FX_CUDA_TRY(cudaGetLastError(), "launching compact attention chunks");
     compact_merge_kernel<<<static_cast<unsigned>(a.batch * kQHeads), kHeadDim, 0, stream>>>(a);
     FX_CUDA_TRY(cudaGetLastError(), "launching compact attention merge");

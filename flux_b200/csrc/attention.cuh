@@ -7,7 +7,7 @@
 
 namespace fx {
 
-constexpr int kCompactChunk = 128;  // cache rows per CTA; workspace [B][9][chunks][66] as the generic op
+constexpr int kCompactChunk = 128;  // cache rows per CTA of the op path; workspace [B][9][chunks][66] as the generic op
 
 struct CompactAttention {
     const float* q;              // [B][9][64]
@@ -19,12 +19,13 @@ struct CompactAttention {
     float* ws;                   // [B][9][chunks][66]
     unsigned* error;             // optional: bit 1 set if a bounded wait gave up
     float scale;
-    int64_t batch, cap, chunks;
+    int64_t batch, cap, chunks;  // chunks = ceil(cap / chunk_rows)
+    int chunk_rows;              // 128 (the op's workspace format) or 64
 };
 
-// Workspace floats for `batch` sequences of capacity `cap`.
-inline int64_t compact_attention_workspace(int64_t batch, int64_t cap) {
-    return batch * kQHeads * ((cap + kCompactChunk - 1) / kCompactChunk) * (kHeadDim + 2);
+// Workspace floats for `batch` sequences of capacity `cap` in chunks of `rows`.
+inline int64_t compact_attention_workspace(int64_t batch, int64_t cap, int rows = kCompactChunk) {
+    return batch * kQHeads * ((cap + rows - 1) / rows) * (kHeadDim + 2);
 }
 
 // Enqueue the chunk and merge kernels on `stream`.

@@ -4,17 +4,20 @@
 // configuration, where each GPU owns its own sequences and replicas of the
 // weights and nothing crosses GPUs.
 //
-// Per layer (10 launches): RMSNorm rows -> QKV split-K GEMM -> RoPE + cache
-// write at each sequence's own position -> compact split-K attention over
-// each sequence's valid length (attention.cu) -> o_proj GEMM + residual ->
-// RMSNorm -> gate/up GEMM + SwiGLU -> down GEMM + residual; then the final
-// norm, the tied LM head GEMM and a per-row greedy argmax that advances each
-// sequence's token and position.
+// Per layer (12-13 launches): RMSNorm rows -> QKV split-K GEMM (+ its
+// reduction) -> RoPE + cache write at each sequence's own position ->
+// compact split-K attention over each sequence's valid length (attention.cu,
+// chunks + merge) -> o_proj GEMM -> reduction + residual -> RMSNorm ->
+// gate/up GEMM -> reduction + SwiGLU -> down GEMM -> reduction + residual;
+// then the final norm, the tied LM head GEMM and a per-row greedy argmax that
+// advances each sequence's token and position.
 //
 // The projections are skinny GEMMs (M = B <= 64 rows of activations against
 // the weight rows): 64 x 64 output tiles over a slice of K, so that small N
-// still spreads over every SM, then a fixed-order reduction of the K slices
-// that also applies the residual add or the SwiGLU -- deterministic, FP32.
+// still spreads over every SM, then a reduction of the K slices in a fixed
+// order (one thread per output, four loads in flight) that also applies the
+// residual add or the SwiGLU -- deterministic, FP32, and a row's result does
+// not depend on the other rows of the batch.
 #include "attention.cuh"
 #include "common.cuh"
 
@@ -110,13 +113,27 @@ __global__ void __launch_bounds__(kGemmThreads) skinny_gemm_kernel(const float* 
     }
 }
 
-// out[m][n] = sum_s P[s][m][n] (+ residual[m][n]), splits in order.
+// Sum of the split-K partials of element i, splits in a fixed order with
+// four loads in flight.
+__device__ __forceinline__ float split_sum(const float* __restrict__ P, int splits, size_t stride, size_t i) {
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    int s = 0;
+    for (; s + 3 < splits; s += 4) {
+        a0 += P[(s + 0) * stride + i];
+        a1 += P[(s + 1) * stride + i];
+        a2 += P[(s + 2) * stride + i];
+        a3 += P[(s + 3) * stride + i];
+    }
+    for (; s < splits; ++s) a0 += P[s * stride + i];
+    return (a0 + a1) + (a2 + a3);
+}
+
+// out[m][n] = sum_s P[s][m][n] (+ residual[m][n]).
 __global__ void reduce_splits_kernel(const float* __restrict__ P, int splits, int M, int N,
                                      const float* __restrict__ residual, float* __restrict__ out) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= static_cast<int64_t>(M) * N) return;
-    float v = 0.0f;
-    for (int s = 0; s < splits; ++s) v += P[static_cast<size_t>(s) * M * N + i];
+    const float v = split_sum(P, splits, static_cast<size_t>(M) * N, i);
     out[i] = residual != nullptr ? residual[i] + v : v;
 }
 
@@ -125,12 +142,9 @@ __global__ void reduce_swiglu_kernel(const float* __restrict__ P, int splits, in
     const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (e >= static_cast<int64_t>(M) * kInter) return;
     const int64_t m = e / kInter, i = e % kInter;
-    float g = 0.0f, u = 0.0f;
-    for (int s = 0; s < splits; ++s) {
-        const float* row = P + (static_cast<size_t>(s) * M + m) * kGateUp;
-        g += row[i];
-        u += row[kInter + i];
-    }
+    const size_t stride = static_cast<size_t>(M) * kGateUp;
+    const float g = split_sum(P, splits, stride, m * kGateUp + i);
+    const float u = split_sum(P, splits, stride, m * kGateUp + kInter + i);
     out[e] = swiglu(g, u);
 }
 
@@ -329,6 +343,7 @@ fx_status run_step(fx_batch* r, cudaStream_t s) {
         a.batch = B;
         a.cap = r->capacity;
         a.chunks = (r->capacity + kCompactChunk - 1) / kCompactChunk;
+        a.chunk_rows = kCompactChunk;
         if ((st = launch_compact_attention(a, s)) != FX_OK) return st;
         if ((st = gemm(r, r->attn, m.o_proj[l], kHidden, kHidden, r->o_plan, nullptr, s)) != FX_OK) return st;
         if ((st = reduce(r, r->o_plan, kHidden, r->h, r->h2, s)) != FX_OK) return st;
@@ -588,8 +603,7 @@ extern "C" fx_status fx_batch_get_buffers(const fx_batch* r, fx_batch_buffers* o
     out->batch = r->batch;
     out->capacity = r->capacity;
     out->generated_capacity = r->gen_cap;
-    out->kernels_per_step = 2 + kLayers * 10 + 3 + (r->qkv_plan.splits > 1 ? kLayers : 0) +
-                            (r->lm_plan.splits > 1 ? 1 : 0);
+    out->kernels_per_step = 1 + kLayers * (12 + (r->qkv_plan.splits > 1 ? 1 : 0)) + 4 + (r->lm_plan.splits > 1 ? 1 : 0);
     return FX_OK;
 }
 

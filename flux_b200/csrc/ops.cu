@@ -538,7 +538,7 @@ extern "C" fx_status fx_gqa_decode_attention_f32(const float* query, const int64
         c.q = query; c.k = key_cache; c.v = value_cache;
         c.lengths = cache_length; c.length_stride = 0;
         c.out = output; c.ws = workspace; c.error = nullptr; c.scale = scale;
-        c.batch = batch; c.cap = capacity; c.chunks = chunks;
+        c.batch = batch; c.cap = capacity; c.chunks = chunks; c.chunk_rows = kCompactChunk;
         return launch_compact_attention(c, as_stream(stream));
     }
     a.mask = mask; a.length = cache_length; a.out = output; a.ws = workspace; a.scale = scale;
