@@ -4,7 +4,7 @@
 // Chunk kernel, grid (chunks, 3 kv heads, B), 256 threads: one CTA owns 128
 // cache rows of one (sequence, kv head).  Thread 0 starts two 1-D TMA bulk
 // copies (K rows, V rows; no multicast) into shared memory on separate
-// mbarriers, so scoring starts as soon as K has landed.  Scores: 16-lane
+// mbarriers, so scoring starts as soon as K has landed.  Scores: 4-lane
 // groups, one row each, 3 heads from one K load; softmax in base 2 over the
 // chunk; P.V with one thread per (4-dim quad, head, row split).  Each CTA
 // writes (max, sum, unnormalised o[64]) per q head -- the workspace format of
@@ -113,44 +113,54 @@ __global__ void __launch_bounds__(kThreads) compact_chunk_kernel(const __grid_co
                 : "memory");
         }
     }
-    // q chunk l16 (4 dims) of the 3 q heads, pre-scaled to base-2 units.
-    const int l16 = lane & 15, grp = warp * 2 + (lane >> 4);
+    // Scores: 4-lane groups (8 per warp), one row each; lane (gl, l4) covers
+    // the 16-byte chunks l4 + 4 m of a row, visiting m = (j + gl) % 4 at step
+    // j so the 32 lanes of one load hit 8 distinct bank groups.  q (pre-scaled
+    // to base-2 units) is loaded in the same rotated order.
+    const int l4 = lane & 3, gl = lane >> 2;
     const float scale2 = a.scale * kLog2e;
-    float4 q[kGroup];
+    float4 q[kGroup][4];
 #pragma unroll
     for (int h = 0; h < kGroup; ++h) {
-        q[h] = reinterpret_cast<const float4*>(a.q + (static_cast<size_t>(b) * kQHeads + g * kGroup + h) * kHeadDim)[l16];
-        q[h].x *= scale2;
-        q[h].y *= scale2;
-        q[h].z *= scale2;
-        q[h].w *= scale2;
+        const float4* qh = reinterpret_cast<const float4*>(a.q + (static_cast<size_t>(b) * kQHeads + g * kGroup + h) * kHeadDim);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float4 v = qh[l4 + 4 * ((j + gl) & 3)];
+            v.x *= scale2;
+            v.y *= scale2;
+            v.z *= scale2;
+            v.w *= scale2;
+            q[h][j] = v;
+        }
     }
     __syncthreads();  // barriers initialised
     if (!wait_landed(&sh.bar[0])) sh.failed = 1;
-    // Scores: 16 groups of 16 lanes, rows grp, grp + 16, ...
     float mloc[kGroup] = {-INFINITY, -INFINITY, -INFINITY};
-    for (int r0 = warp * 2; r0 < n; r0 += 2 * kWarps) {  // warp-uniform: full-mask shuffles
-        const int r = r0 + (lane >> 4);
-        const float4 kv = reinterpret_cast<const float4*>(ktile + (r < n ? r : r0) * kHeadDim)[l16];
-        float d[kGroup];
+    for (int r0 = warp * 8; r0 < n; r0 += 8 * kWarps) {  // warp-uniform: full-mask shuffles
+        const int r = r0 + gl;
+        const float4* k4 = reinterpret_cast<const float4*>(ktile + (r < n ? r : r0) * kHeadDim);
+        float d[kGroup] = {0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int h = 0; h < kGroup; ++h) {
-            d[h] = q[h].x * kv.x;
-            d[h] = fmaf(q[h].y, kv.y, d[h]);
-            d[h] = fmaf(q[h].z, kv.z, d[h]);
-            d[h] = fmaf(q[h].w, kv.w, d[h]);
+        for (int j = 0; j < 4; ++j) {
+            const float4 kv = k4[l4 + 4 * ((j + gl) & 3)];
+#pragma unroll
+            for (int h = 0; h < kGroup; ++h) {
+                d[h] = fmaf(q[h][j].x, kv.x, d[h]);
+                d[h] = fmaf(q[h][j].y, kv.y, d[h]);
+                d[h] = fmaf(q[h][j].z, kv.z, d[h]);
+                d[h] = fmaf(q[h][j].w, kv.w, d[h]);
+            }
         }
 #pragma unroll
-        for (int off = 8; off > 0; off >>= 1)
+        for (int off = 1; off < 4; off <<= 1)
 #pragma unroll
             for (int h = 0; h < kGroup; ++h) d[h] += __shfl_xor_sync(0xffffffffu, d[h], off);
         if (r < n) {
 #pragma unroll
             for (int h = 0; h < kGroup; ++h) mloc[h] = fmaxf(mloc[h], d[h]);
-            if (l16 < kGroup) sh.p[l16][r] = l16 == 0 ? d[0] : (l16 == 1 ? d[1] : d[2]);
+            if (l4 < kGroup) sh.p[l4][r] = l4 == 0 ? d[0] : (l4 == 1 ? d[1] : d[2]);
         }
     }
-    (void)grp;
 #pragma unroll
     for (int h = 0; h < kGroup; ++h) {
         mloc[h] = warp_max(mloc[h]);
