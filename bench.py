@@ -59,6 +59,7 @@ def parse_args(argv=None):
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--batched-steps", type=int, default=256, help="greedy steps of the batched configuration")
+    p.add_argument("--batch", type=int, default=64, help="sequences per GPU of the batched configuration")
     p.add_argument("--no-batched", action="store_true", help="skip the batched configuration")
     p.add_argument("--no-attention", action="store_true", help="skip the isolated-attention sweep")
     return p.parse_args(argv)
@@ -79,6 +80,22 @@ def measured_peaks() -> dict:
         except ValueError:
             pass
     return {}
+
+
+def measured_traffic(bytes_per_step: float) -> dict | None:
+    """DRAM bytes per step-kernel launch from the committed ncu capture of
+    this workload (profiles/decode_step_traffic.json), scaled from the
+    captured step's algorithmic bytes to the timed steps' (traffic grows with
+    the K/V rows read)."""
+    path = ROOT / "profiles" / "decode_step_traffic.json"
+    try:
+        rec = json.loads(path.read_text())
+    except (OSError, ValueError):
+        return None
+    captured = rec["dram_read_bytes"] + rec["dram_write_bytes"]
+    scaled = captured * bytes_per_step / rec["algorithmic_bytes"]
+    return {"bytes_per_launch": int(scaled), "ratio_to_algorithmic": round(captured / rec["algorithmic_bytes"], 4),
+            "captured_context_rows": rec["context_rows"], "source": rec["source"]}
 
 
 # ----------------------------------------------------------- clock sampling
@@ -273,7 +290,9 @@ def run_native(args) -> dict | None:
         },
         "roofline": {
             "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": None,
+            "frac": round(achieved / peak, 4),
+            "traffic": (measured_traffic(bytes_per_step) or {}).get("bytes_per_launch"),
+            "traffic_source": measured_traffic(bytes_per_step),
             "kernel": "decode step (one CUDA graph replay)",
             "algorithmic_bytes_per_launch": int(bytes_per_step), "peak_source": peak_src,
         },
@@ -292,7 +311,6 @@ def run_native(args) -> dict | None:
     return line
 
 
-BATCH = 64                      # sequences per GPU
 BATCH_CONTEXT = (512, 4096)     # ragged contexts drawn uniformly (seeded)
 
 
@@ -306,10 +324,11 @@ def run_batched(args, model, device, world: int, rank: int, peak: float, peak_sr
     from flux_b200.runtime import NativeSmolLM2BatchedDecode
     steps, warm = args.batched_steps, max(3, args.warmup)
     gen = torch.Generator().manual_seed(args.seed * 1000 + 17 + rank)
-    lengths = torch.randint(BATCH_CONTEXT[0], BATCH_CONTEXT[1] + 1, (BATCH,), generator=gen).tolist()
-    tokens = torch.randint(0, 49152, (BATCH,), generator=gen).tolist()
+    batch = args.batch
+    lengths = torch.randint(BATCH_CONTEXT[0], BATCH_CONTEXT[1] + 1, (batch,), generator=gen).tolist()
+    tokens = torch.randint(0, 49152, (batch,), generator=gen).tolist()
     capacity = BATCH_CONTEXT[1] + warm + steps + 1
-    runtime = NativeSmolLM2BatchedDecode(model, BATCH, capacity)
+    runtime = NativeSmolLM2BatchedDecode(model, batch, capacity)
     dgen = torch.Generator(device=device).manual_seed(args.seed * 1000 + 29 + rank)
     for i, n in enumerate(lengths):
         keys = torch.randn(30, 3, n, 64, device=device, generator=dgen) * 0.5
@@ -338,17 +357,17 @@ def run_batched(args, model, device, world: int, rank: int, peak: float, peak_sr
     if rank != 0:
         return None
     ms_per_step = ms / steps
-    mean_rows = sum(lengths) / BATCH + warm + (steps - 1) / 2.0 + 1
-    bytes_per_step = WEIGHT_BYTES + KV_BYTES_PER_ROW * BATCH * mean_rows
+    mean_rows = sum(lengths) / batch + warm + (steps - 1) / 2.0 + 1
+    bytes_per_step = WEIGHT_BYTES + KV_BYTES_PER_ROW * batch * mean_rows
     achieved = bytes_per_step / (ms_per_step * 1e-3) / 1e9
     return {
-        "metric": "batched decode tokens/s (64 sequences per GPU)", "value": round(world * BATCH * steps / (ms * 1e-3), 1),
+        "metric": f"batched decode tokens/s ({batch} sequences per GPU)", "value": round(world * batch * steps / (ms * 1e-3), 1),
         "unit": "tokens/s", "higher_is_better": True, "n_gpus": world, "scaling": "weak", "steps": steps,
         "warmup": warm, "ms_per_step": round(ms_per_step, 4),
-        "tokens_per_s_per_gpu": round(BATCH * steps / (ms * 1e-3), 1),
-        "config": {"workload": "configs[3]: 64 independent sequences per GPU, ragged contexts ~U[512,4096] "
+        "tokens_per_s_per_gpu": round(batch * steps / (ms * 1e-3), 1),
+        "config": {"workload": f"configs[3]: {batch} independent sequences per GPU, ragged contexts ~U[512,4096] "
                                "(seeded per rank), greedy steps, sequences sharded by rank, no collective",
-                   "contexts_rank0": {"min": min(lengths), "max": max(lengths), "mean": round(sum(lengths) / BATCH, 1)},
+                   "contexts_rank0": {"min": min(lengths), "max": max(lengths), "mean": round(sum(lengths) / batch, 1)},
                    "data": "seeded N(0,0.5) cache rows, seeded uniform tokens"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "algorithmic_bytes_per_step": int(bytes_per_step),
