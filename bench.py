@@ -321,16 +321,17 @@ def run_batched(args, model, device, world: int, rank: int, peak: float, peak_sr
     are seeded N(0, 0.5) rows (no prefill; the step does not depend on how the
     rows were produced)."""
     import torch.distributed as dist
+    from flux_b200 import sharding
     from flux_b200.runtime import NativeSmolLM2BatchedDecode
     steps, warm = args.batched_steps, max(3, args.warmup)
-    gen = torch.Generator().manual_seed(args.seed * 1000 + 17 + rank)
     batch = args.batch
-    lengths = torch.randint(BATCH_CONTEXT[0], BATCH_CONTEXT[1] + 1, (batch,), generator=gen).tolist()
-    tokens = torch.randint(0, 49152, (batch,), generator=gen).tolist()
+    shard = sharding.sequence_shard(world * batch, world, rank)
+    lengths, tokens = sharding.shard_contexts(args.seed, shard, *BATCH_CONTEXT)
     capacity = BATCH_CONTEXT[1] + warm + steps + 1
     runtime = NativeSmolLM2BatchedDecode(model, batch, capacity)
-    dgen = torch.Generator(device=device).manual_seed(args.seed * 1000 + 29 + rank)
+    dgen = torch.Generator(device=device)
     for i, n in enumerate(lengths):
+        dgen.manual_seed(args.seed * 1_000_003 + 29 + shard[i])  # cache rows depend on the global sequence only
         keys = torch.randn(30, 3, n, 64, device=device, generator=dgen) * 0.5
         values = torch.randn(30, 3, n, 64, device=device, generator=dgen) * 0.5
         runtime.load(i, tokens[i], list(keys), list(values), n)
@@ -350,10 +351,7 @@ def run_batched(args, model, device, world: int, rank: int, peak: float, peak_sr
     runtime.check()
     if world > 1:
         dist.barrier()
-    ms = torch.tensor([start.elapsed_time(end)], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms.item())
+    ms = sharding.max_over_ranks([start.elapsed_time(end)], device)[0]
     if rank != 0:
         return None
     ms_per_step = ms / steps
@@ -361,12 +359,14 @@ def run_batched(args, model, device, world: int, rank: int, peak: float, peak_sr
     bytes_per_step = WEIGHT_BYTES + KV_BYTES_PER_ROW * batch * mean_rows
     achieved = bytes_per_step / (ms_per_step * 1e-3) / 1e9
     return {
-        "metric": f"batched decode tokens/s ({batch} sequences per GPU)", "value": round(world * batch * steps / (ms * 1e-3), 1),
+        "metric": f"batched decode tokens/s ({batch} sequences per GPU)",
+        "value": round(sharding.aggregate_tokens_per_s(batch * steps, world, ms), 1),
         "unit": "tokens/s", "higher_is_better": True, "n_gpus": world, "scaling": "weak", "steps": steps,
         "warmup": warm, "ms_per_step": round(ms_per_step, 4),
         "tokens_per_s_per_gpu": round(batch * steps / (ms * 1e-3), 1),
         "config": {"workload": f"configs[3]: {batch} independent sequences per GPU, ragged contexts ~U[512,4096] "
-                               "(seeded per rank), greedy steps, sequences sharded by rank, no collective",
+                               "(seeded per global sequence), greedy steps, contiguous sequence blocks per rank, "
+                               "no collective",
                    "contexts_rank0": {"min": min(lengths), "max": max(lengths), "mean": round(sum(lengths) / batch, 1)},
                    "data": "seeded N(0,0.5) cache rows, seeded uniform tokens"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
