@@ -478,7 +478,7 @@ def main(argv=None) -> int:
     if world > 1:
         from datetime import timedelta
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
     try:
         line = run_native(args)
     finally:
