@@ -389,6 +389,18 @@ __device__ const float* acquire(const StepArgs& a, Shared& sh, unsigned char* ri
     return reinterpret_cast<const float*>(ring + static_cast<size_t>(slot) * kStepSlotBytes);
 }
 
+// Every consumer thread waits (bounded) until tiles k .. k + n - 1 landed,
+// without a consumer barrier: the caller's next barrier makes an abort
+// visible (sh.abort), and the caller reads sh.abort after it.
+__device__ void wait_tiles(const StepArgs& a, Shared& sh, int k, int n) {
+    for (int b = 0; b < n; ++b)
+        if (!wait_bar(a, sh, &sh.full[(k + b) % kStepSlots], static_cast<uint32_t>((k + b) / kStepSlots) & 1u)) break;
+}
+
+__device__ __forceinline__ const float* slot_ptr(unsigned char* ring, int k) {
+    return reinterpret_cast<const float*>(ring + static_cast<size_t>(k % kStepSlots) * kStepSlotBytes);
+}
+
 // Tiles k .. k + n - 1 (one attention batch): wait until all landed; false (uniformly) on abort.
 __device__ bool acquire_batch(const StepArgs& a, Shared& sh, int k, int n) {
     for (int b = 0; b < n; ++b)
@@ -645,9 +657,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             }
             LAYER_MARK(0);
             {
-                const float* t = acquire(a, sh, ring, k);
-                if (t == nullptr) goto done;
-                normalise(sh, sh.hraw, t, a.eps);
+                wait_tiles(a, sh, k, 1);
+                const float* t = slot_ptr(ring, k);
+                normalise(sh, sh.hraw, t, a.eps);  // its barrier also publishes the tile wait
+                if (sh.abort) goto done;
                 if (warp < s.t1 - s.t0) {
                     int ra, rb, kind;
                     task_rows(s.t0 + warp, ra, rb, kind);
@@ -714,7 +727,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 // Batches of up to 4 cache tiles (every tile but the chunk's last
                 // holds 54 rows); the last batch also takes the new row from the
                 // exchange.  A running max rescales the earlier batches.
-                int j = 0;
+                int j = 0, last_batch = 0;
                 do {
                     const int nb = min(kBatchTiles, s.n_att - j);
                     const int64_t r0 = s.a0 + static_cast<int64_t>(j) * kStepAttnRows;
@@ -849,15 +862,24 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                         pacc.z += acc2.z;
                         pacc.w += acc2.w;
                     }
-                    release_batch(sh, k, nb);
-                    k += nb;
+                    if (j + nb < s.n_att) {
+                        release_batch(sh, k, nb);  // the next batch needs the producer to move on
+                        k += nb;
+                    } else {
+                        last_batch = nb;  // released at the combine barrier below
+                    }
                     j += nb;
                 } while (j < s.n_att);
                 LAYER_MARK(3);
                 // Sum the row splits.
                 reinterpret_cast<float4*>(sh.att.o[psplit][ph])[pq] = pacc;
                 if (pq == 0) sh.att.l[psplit][ph] = plsum;
-                consumer_sync();
+                consumer_sync();  // every thread is done with the last batch's tiles
+                if (tid == 0) {
+                    for (int b = 0; b < last_batch; ++b) mbar_arrive(&sh.empty[(k + b) % kStepSlots]);
+                    sh.consumed = k + last_batch;
+                }
+                k += last_batch;
                 if (tid < kGroup * kHeadDim) {
                     const int h = tid / kHeadDim, d = tid % kHeadDim;
                     const float mx = (h == 0 ? mrun[0] : (h == 1 ? mrun[1] : mrun[2])) * kLn2;  // natural-log units
@@ -875,7 +897,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                         st_word(pw + 1, tag, total);
                     }
                 }
-                consumer_sync();
+                // no barrier: phase M uses other shared arrays, and the next writes of
+                // sh.att come after many barriers (next layer)
             }
             LAYER_MARK(4);
 
@@ -933,27 +956,19 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             LAYER_MARK(7);
             {
                 const int nf = (s.f1 - s.f0) * kStepBlock;
+                // gate, up and down tiles together; the norm's barrier also publishes the waits.
+                wait_tiles(a, sh, k, 3);
                 normalise(sh, sh.mid, sh.wpost, a.eps);
-                // gate, up and down tiles together: gate rows on warps 0-5, up rows on 6-11.
-                if (!acquire_batch(a, sh, k, 3)) goto done;
-                auto slot = [&](int i) {
-                    return reinterpret_cast<const float*>(ring + static_cast<size_t>((k + i) % kStepSlots) * kStepSlotBytes);
-                };
-                {
-                    const bool is_up = warp >= kMaxFeatures / 2;
-                    const int wr = is_up ? warp - kMaxFeatures / 2 : warp;
-                    const int w2 = wr * 2 + half;
-                    if (warp < kMaxFeatures && wr * 2 < nf) {  // whole warps enter the half-warp shuffles
-                        const int rr = w2 < nf ? w2 : 0;
-                        const float y = row_dot(slot(is_up ? 1 : 0) + rr * kHidden, sh.xs, l16);
-                        if (l16 == 0 && w2 < nf) (is_up ? sh.up : sh.gate)[w2] = y;
-                    }
+                if (sh.abort) goto done;
+                // warp f: gate row f on lanes 0-15, up row f on lanes 16-31, SwiGLU on lane 0.
+                if (warp < nf) {
+                    const float y = row_dot(slot_ptr(ring, k + half) + warp * kHidden, sh.xs, l16);
+                    const float up = __shfl_sync(0xffffffffu, y, 16);
+                    if (lane == 0) sh.act[warp] = swiglu(y, up);
                 }
                 consumer_sync();
-                if (tid < nf) sh.act[tid] = swiglu(sh.gate[tid], sh.up[tid]);
-                consumer_sync();
                 LAYER_MARK(8);
-                tally_products(slot(2), sh.act, s.f1 - s.f0, down_tally(l) + s.replica);
+                tally_products(slot_ptr(ring, k + 2), sh.act, s.f1 - s.f0, down_tally(l) + s.replica);
                 release_batch(sh, k, 3);
                 k += 3;
             }
@@ -967,9 +982,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             long long bi = -1;
             if (s.n_lm > 0) {
                 if (!tally_read(a, sh, down_tally(kLayers - 1), sh.mid, sh.hraw, G)) goto done;
-                const float* t = acquire(a, sh, ring, k);
-                if (t == nullptr) goto done;
+                wait_tiles(a, sh, k, 1);
+                const float* t = slot_ptr(ring, k);
                 normalise(sh, sh.hraw, t, a.eps);
+                if (sh.abort) goto done;
                 if (s.v0 == 0)
                     for (int i = tid; i < kHidden; i += kStepConsumers) a.final_norm_out[i] = sh.xs[i];
                 release(sh, k++);
