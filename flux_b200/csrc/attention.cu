@@ -83,6 +83,8 @@ __device__ __forceinline__ int64_t sequence_length(const CompactAttention& a, in
 
 template <int kRows>
 __global__ void __launch_bounds__(kThreads) compact_chunk_kernel(const __grid_constant__ CompactAttention a) {
+    grid_dependency_wait();
+
     extern __shared__ __align__(128) unsigned char smem[];
     ChunkShared<kRows>& sh = *reinterpret_cast<ChunkShared<kRows>*>(smem);
     float* ktile = reinterpret_cast<float*>(smem + shared_head<kRows>());
@@ -246,6 +248,8 @@ __global__ void __launch_bounds__(kThreads) compact_chunk_kernel(const __grid_co
 // head).  The chunk weights exp(m_c - max) / sum are computed once per chunk
 // (cooperatively) into shared memory, then thread d sums o_c[d] over chunks.
 __global__ void __launch_bounds__(kHeadDim) compact_merge_kernel(const __grid_constant__ CompactAttention a) {
+    grid_dependency_wait();
+
     __shared__ float weight[kMergeMaxChunks];
     __shared__ float scratch[2];
     const int64_t bh = blockIdx.x, b = bh / kQHeads;
@@ -282,7 +286,7 @@ __global__ void __launch_bounds__(kHeadDim) compact_merge_kernel(const __grid_co
 
 }  // namespace
 
-fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream) {
+fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream, bool dependent) {
     static bool configured = false;
     if (!configured) {
         FX_CUDA_TRY(cudaFuncSetAttribute(compact_chunk_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -298,12 +302,23 @@ fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t strea
                    a.chunks * a.chunk_rows >= a.cap,
                "flux attention: batch or capacity out of range");
     const dim3 grid(static_cast<unsigned>(a.chunks), kKVHeads, static_cast<unsigned>(a.batch));
+    const dim3 merge_grid(static_cast<unsigned>(a.batch * kQHeads));
+    if (dependent) {
+        fx_status st = a.chunk_rows == 128
+                           ? launch_dependent(compact_chunk_kernel<128>, grid, dim3(kThreads), chunk_smem<128>(), stream,
+                                              "launching compact attention chunks", a)
+                           : launch_dependent(compact_chunk_kernel<64>, grid, dim3(kThreads), chunk_smem<64>(), stream,
+                                              "launching compact attention chunks", a);
+        if (st != FX_OK) return st;
+        return launch_dependent(compact_merge_kernel, merge_grid, dim3(kHeadDim), 0, stream,
+                                "launching compact attention merge", a);
+    }
     if (a.chunk_rows == 128)
         compact_chunk_kernel<128><<<grid, kThreads, chunk_smem<128>(), stream>>>(a);
     else
         compact_chunk_kernel<64><<<grid, kThreads, chunk_smem<64>(), stream>>>(a);
     FX_CUDA_TRY(cudaGetLastError(), "launching compact attention chunks");
-    compact_merge_kernel<<<static_cast<unsigned>(a.batch * kQHeads), kHeadDim, 0, stream>>>(a);
+    compact_merge_kernel<<<merge_grid, kHeadDim, 0, stream>>>(a);
     FX_CUDA_TRY(cudaGetLastError(), "launching compact attention merge");
     return FX_OK;
 }

@@ -28,7 +28,8 @@ inline int64_t compact_attention_workspace(int64_t batch, int64_t cap, int rows 
     return batch * kQHeads * ((cap + rows - 1) / rows) * (kHeadDim + 2);
 }
 
-// Enqueue the chunk and merge kernels on `stream`.
-fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream);
+// Enqueue the chunk and merge kernels on `stream` (`dependent`: as
+// programmatic dependent launches of the preceding kernel).
+fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream, bool dependent = false);
 
 }  // namespace fx

@@ -38,6 +38,8 @@ constexpr int64_t kMaxCapacity = 131072;
 // h[b] = embedding[tokens[b]] (zeros for an out-of-range token).
 __global__ void embed_rows_kernel(const int64_t* __restrict__ tokens, const float* __restrict__ embedding,
                                   int64_t vocab, float* __restrict__ h) {
+    grid_dependency_wait();
+
     const int b = blockIdx.x;
     const int64_t t = tokens[b];
     const bool valid = t >= 0 && t < vocab;
@@ -47,6 +49,8 @@ __global__ void embed_rows_kernel(const int64_t* __restrict__ tokens, const floa
 // out[b] = x[b] * rsqrt(mean(x[b]^2) + eps) * w; one CTA per row.
 __global__ void __launch_bounds__(192) norm_rows_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                         float* __restrict__ out, float eps) {
+    grid_dependency_wait();
+
     __shared__ float scratch[32];
     const int b = blockIdx.x;
     const float* row = x + static_cast<size_t>(b) * kHidden;
@@ -64,6 +68,8 @@ __global__ void __launch_bounds__(kGemmThreads) skinny_gemm_kernel(const float* 
                                                                    const float* __restrict__ W,
                                                                    float* __restrict__ P, int M, int N, int K,
                                                                    int k_per_split) {
+    grid_dependency_wait();
+
     __shared__ __align__(16) float As[kTileK][kTileM + 4];
     __shared__ __align__(16) float Bs[kTileK][kTileN + 4];
     const int n0 = blockIdx.x * kTileN;
@@ -131,6 +137,8 @@ __device__ __forceinline__ float split_sum(const float* __restrict__ P, int spli
 // out[m][n] = sum_s P[s][m][n] (+ residual[m][n]).
 __global__ void reduce_splits_kernel(const float* __restrict__ P, int splits, int M, int N,
                                      const float* __restrict__ residual, float* __restrict__ out) {
+    grid_dependency_wait();
+
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= static_cast<int64_t>(M) * N) return;
     const float v = split_sum(P, splits, static_cast<size_t>(M) * N, i);
@@ -139,6 +147,8 @@ __global__ void reduce_splits_kernel(const float* __restrict__ P, int splits, in
 
 // out[m][i] = swiglu(sum_s P[s][m][i], sum_s P[s][m][I + i]) for the packed gate|up columns.
 __global__ void reduce_swiglu_kernel(const float* __restrict__ P, int splits, int M, float* __restrict__ out) {
+    grid_dependency_wait();
+
     const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (e >= static_cast<int64_t>(M) * kInter) return;
     const int64_t m = e / kInter, i = e % kInter;
@@ -155,6 +165,8 @@ __global__ void rope_cache_rows_kernel(const float* __restrict__ qkv, const int6
                                        const float* __restrict__ cos_table, const float* __restrict__ sin_table,
                                        float* __restrict__ kc, float* __restrict__ vc, float* __restrict__ q,
                                        int64_t* __restrict__ lengths, int64_t cap, int B, unsigned* __restrict__ error) {
+    grid_dependency_wait();
+
     constexpr int kPairs = (kQHeads + kKVHeads) * (kHeadDim / 2) + kKVHeads * kHeadDim;  // 384 + 192
     const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (e >= static_cast<int64_t>(B) * kPairs) return;
@@ -196,6 +208,8 @@ __global__ void __launch_bounds__(1024) greedy_rows_kernel(const float* __restri
                                                            int64_t* __restrict__ tokens, int64_t* __restrict__ positions,
                                                            int64_t* __restrict__ generated, int64_t gen_cap,
                                                            const int64_t* __restrict__ step_in, int64_t* __restrict__ step_out) {
+    grid_dependency_wait();
+
     __shared__ float sv[32];
     __shared__ long long si[32];
     const int b = blockIdx.x;
@@ -237,6 +251,8 @@ __global__ void __launch_bounds__(1024) greedy_rows_kernel(const float* __restri
 }
 
 __global__ void advance_step_kernel(int64_t* step) {
+    grid_dependency_wait();
+
     if (threadIdx.x == 0 && blockIdx.x == 0) *step += 1;
 }
 
@@ -299,36 +315,40 @@ fx_status gemm(fx_batch* r, const float* x, const float* w, int N, int K, const 
     const int M = static_cast<int>(r->batch);
     float* out = p.splits == 1 && direct_out != nullptr ? direct_out : r->partials;
     const dim3 grid((N + kTileN - 1) / kTileN, p.splits);
-    skinny_gemm_kernel<<<grid, kGemmThreads, 0, s>>>(x, w, out, M, N, K, p.k_per_split);
-    FX_CUDA_TRY(cudaGetLastError(), "launching a batched projection");
-    return FX_OK;
+    return launch_dependent(skinny_gemm_kernel, grid, dim3(kGemmThreads), 0, s, "launching a batched projection", x, w,
+                            out, M, N, K, p.k_per_split);
 }
 
 fx_status reduce(fx_batch* r, const GemmPlan& p, int N, const float* residual, float* out, cudaStream_t s) {
     const int M = static_cast<int>(r->batch);
     const int64_t n = static_cast<int64_t>(M) * N;
-    reduce_splits_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(r->partials, p.splits, M, N, residual, out);
-    FX_CUDA_TRY(cudaGetLastError(), "launching a split-K reduction");
-    return FX_OK;
+    return launch_dependent(reduce_splits_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s,
+                            "launching a split-K reduction", static_cast<const float*>(r->partials), p.splits, M, N,
+                            residual, out);
 }
 
 fx_status run_step(fx_batch* r, cudaStream_t s) {
     const fx_model_desc& m = r->model;
     const int B = static_cast<int>(r->batch);
     fx_status st;
-    embed_rows_kernel<<<B, 192, 0, s>>>(r->tokens, m.embedding, r->vocab, r->h);
-    FX_CUDA_TRY(cudaGetLastError(), "launching the embedding gather");
+    if ((st = launch_dependent(embed_rows_kernel, dim3(B), dim3(192), 0, s, "launching the embedding gather",
+                               static_cast<const int64_t*>(r->tokens), m.embedding, r->vocab, r->h)) != FX_OK)
+        return st;
     for (int l = 0; l < kLayers; ++l) {
         float* kc = r->key_cache + l * r->layer_stride();
         float* vc = r->value_cache + l * r->layer_stride();
-        norm_rows_kernel<<<B, 192, 0, s>>>(r->h, m.input_norm[l], r->norm, m.epsilon);
+        if ((st = launch_dependent(norm_rows_kernel, dim3(B), dim3(192), 0, s, "launching RMSNorm rows",
+                                   static_cast<const float*>(r->h), m.input_norm[l], r->norm, m.epsilon)) != FX_OK)
+            return st;
         if ((st = gemm(r, r->norm, m.packed_qkv[l], kQKV, kHidden, r->qkv_plan, r->qkv, s)) != FX_OK) return st;
         if (r->qkv_plan.splits > 1 && (st = reduce(r, r->qkv_plan, kQKV, nullptr, r->qkv, s)) != FX_OK) return st;
         {
             const int64_t n = static_cast<int64_t>(B) * ((kQHeads + kKVHeads) * (kHeadDim / 2) + kKVHeads * kHeadDim);
-            rope_cache_rows_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
-                r->qkv, r->positions, m.rope_cos, m.rope_sin, kc, vc, r->q, r->lengths, r->capacity, B, r->error);
-            FX_CUDA_TRY(cudaGetLastError(), "launching the batched RoPE / cache write");
+            if ((st = launch_dependent(rope_cache_rows_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s,
+                                       "launching the batched RoPE / cache write", static_cast<const float*>(r->qkv),
+                                       static_cast<const int64_t*>(r->positions), m.rope_cos, m.rope_sin, kc, vc, r->q,
+                                       r->lengths, r->capacity, B, r->error)) != FX_OK)
+                return st;
         }
         CompactAttention a{};
         a.q = r->q;
@@ -344,31 +364,35 @@ fx_status run_step(fx_batch* r, cudaStream_t s) {
         a.cap = r->capacity;
         a.chunks = (r->capacity + kCompactChunk - 1) / kCompactChunk;
         a.chunk_rows = kCompactChunk;
-        if ((st = launch_compact_attention(a, s)) != FX_OK) return st;
+        if ((st = launch_compact_attention(a, s, true)) != FX_OK) return st;
         if ((st = gemm(r, r->attn, m.o_proj[l], kHidden, kHidden, r->o_plan, nullptr, s)) != FX_OK) return st;
         if ((st = reduce(r, r->o_plan, kHidden, r->h, r->h2, s)) != FX_OK) return st;
-        norm_rows_kernel<<<B, 192, 0, s>>>(r->h2, m.post_norm[l], r->norm, m.epsilon);
+        if ((st = launch_dependent(norm_rows_kernel, dim3(B), dim3(192), 0, s, "launching RMSNorm rows",
+                                   static_cast<const float*>(r->h2), m.post_norm[l], r->norm, m.epsilon)) != FX_OK)
+            return st;
         if ((st = gemm(r, r->norm, m.gate_up[l], kGateUp, kHidden, r->gu_plan, nullptr, s)) != FX_OK) return st;
         {
             const int64_t n = static_cast<int64_t>(B) * kInter;
-            reduce_swiglu_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(r->partials, r->gu_plan.splits, B,
-                                                                                        r->act);
-            FX_CUDA_TRY(cudaGetLastError(), "launching the batched SwiGLU");
+            if ((st = launch_dependent(reduce_swiglu_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s,
+                                       "launching the batched SwiGLU", static_cast<const float*>(r->partials),
+                                       r->gu_plan.splits, B, r->act)) != FX_OK)
+                return st;
         }
         if ((st = gemm(r, r->act, m.down[l], kHidden, kInter, r->down_plan, nullptr, s)) != FX_OK) return st;
         if ((st = reduce(r, r->down_plan, kHidden, r->h2, r->h, s)) != FX_OK) return st;
     }
-    norm_rows_kernel<<<B, 192, 0, s>>>(r->h, m.final_norm, r->norm, m.epsilon);
+    if ((st = launch_dependent(norm_rows_kernel, dim3(B), dim3(192), 0, s, "launching the final RMSNorm",
+                               static_cast<const float*>(r->h), m.final_norm, r->norm, m.epsilon)) != FX_OK)
+        return st;
     if ((st = gemm(r, r->norm, m.lm_head, static_cast<int>(r->vocab), kHidden, r->lm_plan, r->logits, s)) != FX_OK)
         return st;
     if (r->lm_plan.splits > 1 && (st = reduce(r, r->lm_plan, static_cast<int>(r->vocab), nullptr, r->logits, s)) != FX_OK)
         return st;
-    greedy_rows_kernel<<<B, 1024, 0, s>>>(r->logits, r->vocab, r->tokens, r->positions, r->generated, r->gen_cap,
-                                          r->step, r->step);
-    FX_CUDA_TRY(cudaGetLastError(), "launching the batched greedy update");
-    advance_step_kernel<<<1, 32, 0, s>>>(r->step);
-    FX_CUDA_TRY(cudaGetLastError(), "advancing the batched step");
-    return FX_OK;
+    if ((st = launch_dependent(greedy_rows_kernel, dim3(B), dim3(1024), 0, s, "launching the batched greedy update",
+                               static_cast<const float*>(r->logits), r->vocab, r->tokens, r->positions, r->generated,
+                               r->gen_cap, static_cast<const int64_t*>(r->step), r->step)) != FX_OK)
+        return st;
+    return launch_dependent(advance_step_kernel, dim3(1), dim3(32), 0, s, "advancing the batched step", r->step);
 }
 
 struct DeviceScope {
