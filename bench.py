@@ -14,7 +14,8 @@ Under torchrun with N > 1 every rank runs an independent replica (the batch-1
 path does not shard; no collective is on the data path) and the value is the
 max over ranks.
 
-The line also carries ``batched`` (configs[3]: 64 ragged sequences per GPU,
+The line also carries ``sweep`` (configs[2]: the batch-1 step after a
+native prefill at each context 128 ... 8192, N = 1), ``batched`` (configs[3]: 64 ragged sequences per GPU,
 greedy steps through the batched runtime, sequences sharded by rank with no
 collective; aggregate tokens/s over all ranks, max-over-ranks time) and, at
 N = 1, ``attention`` (configs[4]: the isolated decode attention GB/s over
@@ -62,6 +63,7 @@ def parse_args(argv=None):
     p.add_argument("--batch", type=int, default=64, help="sequences per GPU of the batched configuration")
     p.add_argument("--no-batched", action="store_true", help="skip the batched configuration")
     p.add_argument("--no-attention", action="store_true", help="skip the isolated-attention sweep")
+    p.add_argument("--no-sweep", action="store_true", help="skip the context sweep of the batch-1 decode")
     return p.parse_args(argv)
 
 
@@ -306,6 +308,8 @@ def run_native(args) -> dict | None:
         line["batched"] = batched
     if world == 1 and not args.no_attention:
         line["attention"] = run_attention_sweep(device, peak)
+    if world == 1 and not args.no_sweep:
+        line["sweep"] = run_context_sweep(model, device, args.seed, peak)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cpu_model, config, ctx)
     return line
@@ -374,6 +378,40 @@ def run_batched(args, model, device, world: int, rank: int, peak: float, peak_sr
                      "peak_source": peak_src},
         "gpu_launches": int(runtime.kernels_per_step * steps),
     }
+
+
+SWEEP_CONTEXTS = (128, 512, 1024, 2048, 4096, 8192)
+
+
+def run_context_sweep(model, device, seed: int, peak: float, steps: int = 32, warm: int = 4) -> dict:
+    """the batch-1 decode step after a native prefill of a seeded
+    prompt of each context length; ms/token over ``steps`` graph replays and
+    the fraction of the HBM roofline of those steps' algorithmic bytes."""
+    from flux_b200.runtime import NativeSmolLM2Prefill
+    from tests.golden.inputs import uniform_prompt
+    rows = []
+    for ctx in SWEEP_CONTEXTS:
+        prompt = uniform_prompt(ctx, seed=seed + ctx).to(device)
+        with torch.inference_mode():
+            runtime = NativeSmolLM2Prefill.capture(model, prompt, max_decode_steps=warm + steps + 1)
+            for _ in range(warm):
+                runtime.replay()
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(steps):
+                runtime.replay()
+            e.record()
+            torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / steps
+        mean_len = ctx + warm + 1 + (steps - 1) / 2.0
+        nbytes = WEIGHT_BYTES + KV_BYTES_PER_ROW * (mean_len + 1)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        rows.append({"context": ctx, "ms_per_token": round(ms, 4), "GBps": round(gbs, 1), "frac": round(gbs / peak, 4)})
+        del runtime
+        torch.cuda.empty_cache()
+    return {"metric": "bs1 decode ms/token by context (configs[2])", "unit": "ms/token", "steps": steps,
+            "warmup": warm, "rows": rows}
 
 
 def run_attention_sweep(device, peak: float) -> dict:
