@@ -165,96 +165,130 @@ __global__ void prefill_rope_cache_kernel(const float* __restrict__ packed, cons
     }
 }
 
-constexpr int kAttnRows = 128;  // query rows per CTA (one per thread)
-constexpr int kAttnKeys = 64;   // keys per shared-memory tile
-constexpr int kAttnSub = 16;    // keys per online-softmax update
+// Causal attention over the cache rows [0, S), flash style: grid
+// (ceil(S/64), 9), one CTA per 64 queries of one q head, 256 threads.  Key
+// tiles of 64 rows stream through shared memory (K transposed, V as is); each
+// thread owns a 4 x 4 block of the score tile (rows 4 tr.., keys 4 tc..) and
+// a 4 x 4 block of the output (rows 4 tr.., dims 4 tc..), so both products
+// are register-blocked (16 FMAs per two 16-byte shared loads).  Online
+// softmax per row across the tiles, reduced over the 16 lanes that share the
+// rows.  Heaviest query blocks (most key tiles) are scheduled first.
+constexpr int kFlash = 64;          // queries and keys per tile
+constexpr int kFlashPad = kFlash + 4;
+constexpr int kFlashThreads = 256;
+constexpr size_t kFlashSmem = 4ull * kFlash * kFlashPad * sizeof(float);
 
-// Causal attention over the cache rows [0, S): grid (ceil(S/128), 9).
-// out is row-major [S, 576] (head h at columns [64 h, 64 h + 64)).
-__global__ void __launch_bounds__(kAttnRows) prefill_attention_kernel(const float* __restrict__ q,
+__global__ void __launch_bounds__(kFlashThreads) prefill_flash_kernel(const float* __restrict__ q,
                                                                       const float* __restrict__ key_cache,
                                                                       const float* __restrict__ value_cache,
                                                                       float* __restrict__ out, int64_t rows,
                                                                       int64_t capacity, float scale) {
-    __shared__ __align__(16) float ks[kAttnKeys][kHeadDim];
-    __shared__ __align__(16) float vs[kAttnKeys][kHeadDim];
+    extern __shared__ __align__(16) float flash_smem[];
+    float (*Qt)[kFlashPad] = reinterpret_cast<float (*)[kFlashPad]>(flash_smem);           // [dim][query]
+    float (*Kt)[kFlashPad] = reinterpret_cast<float (*)[kFlashPad]>(flash_smem + kFlash * kFlashPad);  // [dim][key]
+    float (*Vs)[kFlashPad] = reinterpret_cast<float (*)[kFlashPad]>(flash_smem + 2 * kFlash * kFlashPad);  // [key][dim]
+    float (*Pt)[kFlashPad] = reinterpret_cast<float (*)[kFlashPad]>(flash_smem + 3 * kFlash * kFlashPad);  // [key][query]
+    const int qb = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);
     const int h = blockIdx.y, g = h / kGroup;
-    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kAttnRows;
-    const int64_t r = r0 + threadIdx.x;
-    const bool valid = r < rows;
-    float qv[kHeadDim], o[kHeadDim];
-    {
-        const float4* q4 = reinterpret_cast<const float4*>(q + (static_cast<int64_t>(h) * rows + (valid ? r : 0)) * kHeadDim);
-#pragma unroll
-        for (int j = 0; j < kHeadDim / 4; ++j) {
-            const float4 v = q4[j];
-            qv[4 * j] = v.x; qv[4 * j + 1] = v.y; qv[4 * j + 2] = v.z; qv[4 * j + 3] = v.w;
-        }
+    const int64_t r0 = static_cast<int64_t>(qb) * kFlash;
+    const int tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+    // Q tile (scaled), transposed.
+    for (int idx = tid; idx < kFlash * kHeadDim / 4; idx += kFlashThreads) {
+        const int r = idx >> 4, d4 = idx & 15;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r0 + r < rows) v = *reinterpret_cast<const float4*>(q + (static_cast<int64_t>(h) * rows + r0 + r) * kHeadDim + 4 * d4);
+        Qt[4 * d4 + 0][r] = v.x * scale;
+        Qt[4 * d4 + 1][r] = v.y * scale;
+        Qt[4 * d4 + 2][r] = v.z * scale;
+        Qt[4 * d4 + 3][r] = v.w * scale;
     }
-#pragma unroll
-    for (int d = 0; d < kHeadDim; ++d) o[d] = 0.0f;
-    float m = -INFINITY, l = 0.0f;
-    const int64_t last_key = std::min<int64_t>(rows, r0 + kAttnRows);  // exclusive
     const float* kb = key_cache + static_cast<int64_t>(g) * capacity * kHeadDim;
     const float* vb = value_cache + static_cast<int64_t>(g) * capacity * kHeadDim;
-    for (int64_t t0 = 0; t0 < last_key; t0 += kAttnKeys) {
-        __syncthreads();
-        for (int f = threadIdx.x; f < kAttnKeys * kHeadDim / 4; f += kAttnRows) {
-            const int key = f / (kHeadDim / 4), c4 = f % (kHeadDim / 4);
-            const bool in = t0 + key < last_key;
-            const float4 kv = in ? __ldg(reinterpret_cast<const float4*>(kb + (t0 + key) * kHeadDim) + c4)
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float4 vv = in ? __ldg(reinterpret_cast<const float4*>(vb + (t0 + key) * kHeadDim) + c4)
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-            *reinterpret_cast<float4*>(&ks[key][4 * c4]) = kv;
-            *reinterpret_cast<float4*>(&vs[key][4 * c4]) = vv;
+    float o[4][4] = {}, m[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
+    }
+    for (int kt = 0; kt <= qb; ++kt) {
+        const int64_t k0 = static_cast<int64_t>(kt) * kFlash;
+        __syncthreads();  // the previous tile's K / V / P are consumed
+        for (int idx = tid; idx < kFlash * kHeadDim / 4; idx += kFlashThreads) {
+            const int key = idx >> 4, d4 = idx & 15;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (k0 + key < rows) {
+                kv = __ldg(reinterpret_cast<const float4*>(kb + (k0 + key) * kHeadDim) + d4);
+                vv = __ldg(reinterpret_cast<const float4*>(vb + (k0 + key) * kHeadDim) + d4);
+            }
+            Kt[4 * d4 + 0][key] = kv.x;
+            Kt[4 * d4 + 1][key] = kv.y;
+            Kt[4 * d4 + 2][key] = kv.z;
+            Kt[4 * d4 + 3][key] = kv.w;
+            *reinterpret_cast<float4*>(&Vs[key][4 * d4]) = vv;
         }
         __syncthreads();
-        for (int j0 = 0; j0 < kAttnKeys; j0 += kAttnSub) {
-            if (t0 + j0 > r) break;  // every key of this sub-block is in the future
-            float s[kAttnSub];
-            float smax = -INFINITY;
+        float sc[4][4] = {};
+#pragma unroll 8
+        for (int d = 0; d < kHeadDim; ++d) {
+            const float4 a = *reinterpret_cast<const float4*>(&Qt[d][4 * tr]);
+            const float4 b = *reinterpret_cast<const float4*>(&Kt[d][4 * tc]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-            for (int jj = 0; jj < kAttnSub; ++jj) {
-                const int key = j0 + jj;
-                float dot = 0.0f;
+            for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int d = 0; d < kHeadDim; d += 4) {
-                    const float4 k4 = *reinterpret_cast<const float4*>(&ks[key][d]);
-                    dot = fmaf(qv[d], k4.x, dot);
-                    dot = fmaf(qv[d + 1], k4.y, dot);
-                    dot = fmaf(qv[d + 2], k4.z, dot);
-                    dot = fmaf(qv[d + 3], k4.w, dot);
-                }
-                s[jj] = (t0 + key <= r) ? dot * scale : -INFINITY;
-                smax = fmaxf(smax, s[jj]);
+                for (int j = 0; j < 4; ++j) sc[i][j] = fmaf(av[i], bv[j], sc[i][j]);
+        }
+        // causal / length mask, online softmax per row (16 lanes share a row)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int64_t row = r0 + 4 * tr + i;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int64_t key = k0 + 4 * tc + j;
+                if (key > row || key >= rows) sc[i][j] = -INFINITY;
+                mx = fmaxf(mx, sc[i][j]);
             }
-            const float m_new = fmaxf(m, smax);
-            const float corr = expf(m - m_new);
-            l *= corr;
 #pragma unroll
-            for (int d = 0; d < kHeadDim; ++d) o[d] *= corr;
+            for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mn = fmaxf(m[i], mx);
+            const float corr = expf(m[i] - mn);  // first tile: m = -inf -> 0
+            float sum = 0.0f;
 #pragma unroll
-            for (int jj = 0; jj < kAttnSub; ++jj) {
-                const float p = expf(s[jj] - m_new);
-                l += p;
-#pragma unroll
-                for (int d = 0; d < kHeadDim; d += 4) {
-                    const float4 v4 = *reinterpret_cast<const float4*>(&vs[j0 + jj][d]);
-                    o[d] = fmaf(p, v4.x, o[d]);
-                    o[d + 1] = fmaf(p, v4.y, o[d + 1]);
-                    o[d + 2] = fmaf(p, v4.z, o[d + 2]);
-                    o[d + 3] = fmaf(p, v4.w, o[d + 3]);
-                }
+            for (int j = 0; j < 4; ++j) {
+                sc[i][j] = expf(sc[i][j] - mn);  // masked: exp(-inf) = 0
+                sum += sc[i][j];
             }
-            m = m_new;
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            l[i] = l[i] * corr + sum;
+            m[i] = mn;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) o[i][c] *= corr;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<float4*>(&Pt[4 * tc + j][4 * tr]) = make_float4(sc[0][j], sc[1][j], sc[2][j], sc[3][j]);
+        __syncthreads();
+#pragma unroll 8
+        for (int key = 0; key < kFlash; ++key) {
+            const float4 a = *reinterpret_cast<const float4*>(&Pt[key][4 * tr]);
+            const float4 b = *reinterpret_cast<const float4*>(&Vs[key][4 * tc]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) o[i][c] = fmaf(av[i], bv[c], o[i][c]);
         }
     }
-    if (!valid) return;
-    float4* o4 = reinterpret_cast<float4*>(out + r * kHidden + h * kHeadDim);
-    const float inv = 1.0f / l;
 #pragma unroll
-    for (int j = 0; j < kHeadDim / 4; ++j) o4[j] = make_float4(o[4 * j] * inv, o[4 * j + 1] * inv, o[4 * j + 2] * inv, o[4 * j + 3] * inv);
+    for (int i = 0; i < 4; ++i) {
+        const int64_t row = r0 + 4 * tr + i;
+        if (row >= rows) continue;
+        const float inv = 1.0f / l[i];
+        *reinterpret_cast<float4*>(out + row * kHidden + h * kHeadDim + 4 * tc) =
+            make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
+    }
 }
 
 unsigned blocks_for(int64_t work) {
@@ -301,6 +335,13 @@ namespace fx {
 namespace {
 
 fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
+    static bool configured = false;  // the flash tiles need more than the default 48 KB of shared memory
+    if (!configured) {
+        FX_CUDA_TRY(cudaFuncSetAttribute(prefill_flash_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kFlashSmem)),
+                    "raising prefill attention shared memory");
+        configured = true;
+    }
     const fx_model_desc& m = p->model;
     fx_decode_buffers db{};
     fx_status st = fx_decode_get_buffers(p->decode, &db);
@@ -322,8 +363,8 @@ fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
         prefill_rope_cache_kernel<<<blocks_for(S * kQKV), 256, 0, s>>>(p->qkv, m.rope_cos, m.rope_sin, p->q, kc, vc,
                                                                        S, cap);
         FX_CUDA_TRY(cudaGetLastError(), "launching prefill RoPE/cache fill");
-        const dim3 agrid(static_cast<unsigned>((S + kAttnRows - 1) / kAttnRows), kQHeads);
-        prefill_attention_kernel<<<agrid, kAttnRows, 0, s>>>(p->q, kc, vc, p->attn, S, cap, m.attention_scale[l]);
+        prefill_flash_kernel<<<dim3(static_cast<unsigned>((S + kFlash - 1) / kFlash), kQHeads), kFlashThreads,
+                               kFlashSmem, s>>>(p->q, kc, vc, p->attn, S, cap, m.attention_scale[l]);
         FX_CUDA_TRY(cudaGetLastError(), "launching prefill attention");
         // residual = attn . Wo^T + in; norm = rmsnorm(residual)
         if ((st = launch_gemm_nt_residual(p->attn, m.o_proj[l], p->residual, in, S, kHidden, kHidden, s)) != FX_OK)

@@ -223,3 +223,26 @@ def test_replay_on_non_default_stream_and_memory(tiny_flux):
     memory = native.memory
     assert memory.cache_bytes == 2 * 30 * 3 * 9 * 64 * 4
     assert memory.owned_tensor_bytes > memory.cache_bytes
+
+
+@pytest.mark.parametrize("prompt_length", [64, 65, 200, 777])
+def test_prefill_long_prompt_vs_oracle(smollm2_model, smollm2_flux, prompt_length):
+    """The native prefill (flash-style causal attention over 64-row key tiles,
+    partial last tile, causal diagonal) against the oracle: prefill logits,
+    every cache row, and the first decode step after it."""
+    from flux_b200.runtime import NativeSmolLM2Prefill
+    ids = gi.uniform_prompt(prompt_length, seed=prompt_length).cuda()
+    with torch.inference_mode():
+        native = NativeSmolLM2Prefill.capture(smollm2_flux, ids, max_decode_steps=2)
+    capacity = prompt_length + 2
+    cos, sin = hf.rope_tables(smollm2_model, capacity)
+    oracle = o.Decoder(hf.oracle_weights(smollm2_model), capacity, cos.numpy(), sin.numpy())
+    expected = oracle.prefill(ids[0].cpu().numpy())
+    np.testing.assert_allclose(np32(native.logits), expected, rtol=LOGIT_TOL, atol=LOGIT_TOL)
+    np.testing.assert_allclose(native.key_cache[:, 0, :, :prompt_length].cpu().numpy(),
+                               oracle.key_cache[:, :, :prompt_length], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(native.value_cache[:, 0, :, :prompt_length].cpu().numpy(),
+                               oracle.value_cache[:, :, :prompt_length], rtol=1e-4, atol=1e-5)
+    token = int(np.argmax(expected))
+    logits = native.replay(torch.tensor([[token]], device="cuda"))
+    np.testing.assert_allclose(np32(logits), oracle.step(token), rtol=LOGIT_TOL, atol=LOGIT_TOL)
