@@ -210,23 +210,35 @@ __global__ void __launch_bounds__(kFlashThreads) prefill_flash_kernel(const floa
         m[i] = -INFINITY;
         l[i] = 0.0f;
     }
+    // K / V tile kt is fetched into registers while tile kt - 1 is computed.
+    constexpr int kPer = kFlash * kHeadDim / 4 / kFlashThreads;  // float4s per thread per tile (4)
+    float4 kreg[kPer], vreg[kPer];
+    auto fetch = [&](int64_t k0) {
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int idx = tid + j * kFlashThreads, key = idx >> 4, d4 = idx & 15;
+            kreg[j] = vreg[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k0 + key < rows) {
+                kreg[j] = __ldg(reinterpret_cast<const float4*>(kb + (k0 + key) * kHeadDim) + d4);
+                vreg[j] = __ldg(reinterpret_cast<const float4*>(vb + (k0 + key) * kHeadDim) + d4);
+            }
+        }
+    };
+    fetch(0);
     for (int kt = 0; kt <= qb; ++kt) {
         const int64_t k0 = static_cast<int64_t>(kt) * kFlash;
         __syncthreads();  // the previous tile's K / V / P are consumed
-        for (int idx = tid; idx < kFlash * kHeadDim / 4; idx += kFlashThreads) {
-            const int key = idx >> 4, d4 = idx & 15;
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (k0 + key < rows) {
-                kv = __ldg(reinterpret_cast<const float4*>(kb + (k0 + key) * kHeadDim) + d4);
-                vv = __ldg(reinterpret_cast<const float4*>(vb + (k0 + key) * kHeadDim) + d4);
-            }
-            Kt[4 * d4 + 0][key] = kv.x;
-            Kt[4 * d4 + 1][key] = kv.y;
-            Kt[4 * d4 + 2][key] = kv.z;
-            Kt[4 * d4 + 3][key] = kv.w;
-            *reinterpret_cast<float4*>(&Vs[key][4 * d4]) = vv;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int idx = tid + j * kFlashThreads, key = idx >> 4, d4 = idx & 15;
+            Kt[4 * d4 + 0][key] = kreg[j].x;
+            Kt[4 * d4 + 1][key] = kreg[j].y;
+            Kt[4 * d4 + 2][key] = kreg[j].z;
+            Kt[4 * d4 + 3][key] = kreg[j].w;
+            *reinterpret_cast<float4*>(&Vs[key][4 * d4]) = vreg[j];
         }
         __syncthreads();
+        if (kt < qb) fetch(k0 + kFlash);
         float sc[4][4] = {};
 #pragma unroll 8
         for (int d = 0; d < kHeadDim; ++d) {
