@@ -30,7 +30,7 @@ namespace fx {
 namespace {
 
 constexpr int kMaxBatch = 64;
-constexpr int kTileM = 64, kTileN = 64, kTileK = 16, kGemmThreads = 256;
+constexpr int kTileM = 64, kTileN = 64, kTileK = 32, kGemmThreads = 256;
 constexpr int64_t kMaxCapacity = 131072;
 
 // ------------------------------------------------------------- kernels
@@ -62,59 +62,85 @@ __global__ void __launch_bounds__(192) norm_rows_kernel(const float* __restrict_
 }
 
 // P[split][m][n] = sum over k in the split's slice of X[m][k] * W[n][k]
-// (M <= 64).  256 threads, 4 x 4 outputs each, K staged through shared
-// memory 16 columns at a time (transposed so the inner loop reads float4s).
+// (M <= 64).  256 threads, 4 x 4 outputs each; K staged through two
+// shared-memory buffers 32 columns at a time (transposed so the inner loop
+// reads float4s), the next slice fetched into registers while the current
+// one is multiplied: one barrier per slice.
 __global__ void __launch_bounds__(kGemmThreads) skinny_gemm_kernel(const float* __restrict__ X,
                                                                    const float* __restrict__ W,
                                                                    float* __restrict__ P, int M, int N, int K,
                                                                    int k_per_split) {
     grid_dependency_wait();
-
-    __shared__ __align__(16) float As[kTileK][kTileM + 4];
-    __shared__ __align__(16) float Bs[kTileK][kTileN + 4];
+    __shared__ __align__(16) float As[2][kTileK][kTileM + 4];
+    __shared__ __align__(16) float Bs[2][kTileK][kTileN + 4];
     const int n0 = blockIdx.x * kTileN;
     const int split = blockIdx.y;
     const int k0 = split * k_per_split;
     const int k1 = min(K, k0 + k_per_split);
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    // loader: row lr (0..63), 4 consecutive k at lk
-    const int lr = tid >> 2, lk = (tid & 3) * 4;
-    float acc[4][4] = {};
-    for (int kk = k0; kk < k1; kk += kTileK) {
-        {
-            float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f), w = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (lr < M && kk + lk < k1) a = *reinterpret_cast<const float4*>(X + static_cast<size_t>(lr) * K + kk + lk);
-            if (n0 + lr < N && kk + lk < k1) w = *reinterpret_cast<const float4*>(W + static_cast<size_t>(n0 + lr) * K + kk + lk);
-            As[lk + 0][lr] = a.x;
-            As[lk + 1][lr] = a.y;
-            As[lk + 2][lr] = a.z;
-            As[lk + 3][lr] = a.w;
-            Bs[lk + 0][lr] = w.x;
-            Bs[lk + 1][lr] = w.y;
-            Bs[lk + 2][lr] = w.z;
-            Bs[lk + 3][lr] = w.w;
+    // loader: float4 j covers row (tid + 256 j) / 8, k quad (tid + 256 j) % 8
+    float4 ar[2], br[2];
+    auto fetch = [&](int kk) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int idx = tid + kGemmThreads * j, r = idx >> 3, kq = (idx & 7) * 4;
+            ar[j] = r < M && kk + kq < k1 ? *reinterpret_cast<const float4*>(X + static_cast<size_t>(r) * K + kk + kq)
+                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            br[j] = n0 + r < N && kk + kq < k1
+                        ? *reinterpret_cast<const float4*>(W + static_cast<size_t>(n0 + r) * K + kk + kq)
+                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
-        __syncthreads();
+    };
+    auto stage = [&](int buf) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int idx = tid + kGemmThreads * j, r = idx >> 3, kq = (idx & 7) * 4;
+            As[buf][kq + 0][r] = ar[j].x;
+            As[buf][kq + 1][r] = ar[j].y;
+            As[buf][kq + 2][r] = ar[j].z;
+            As[buf][kq + 3][r] = ar[j].w;
+            Bs[buf][kq + 0][r] = br[j].x;
+            Bs[buf][kq + 1][r] = br[j].y;
+            Bs[buf][kq + 2][r] = br[j].z;
+            Bs[buf][kq + 3][r] = br[j].w;
+        }
+    };
+    float acc[4][4] = {};
+    int buf = 0;
+    if (k0 < k1) {
+        fetch(k0);
+        stage(0);
+    }
+    __syncthreads();
+    for (int kk = k0; kk < k1; kk += kTileK) {
+        const bool more = kk + kTileK < k1;
+        if (more) fetch(kk + kTileK);
 #pragma unroll
         for (int k = 0; k < kTileK; ++k) {
-            const float4 a = *reinterpret_cast<const float4*>(&As[k][ty * 4]);
-            const float4 b = *reinterpret_cast<const float4*>(&Bs[k][tx * 4]);
+            const float4 a = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
+            const float4 b = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 4]);
             const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
         }
+        if (more) stage(buf ^ 1);
         __syncthreads();
+        buf ^= 1;
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int m = ty * 4 + i;
         if (m >= M) continue;
+        const int n = n0 + tx * 4;
+        float* dst = P + (static_cast<size_t>(split) * M + m) * N + n;
+        if (n + 3 < N) {
+            *reinterpret_cast<float4*>(dst) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int n = n0 + tx * 4 + j;
-            if (n < N) P[(static_cast<size_t>(split) * M + m) * N + n] = acc[i][j];
+            for (int j = 0; j < 4; ++j)
+                if (n + j < N) dst[j] = acc[i][j];
         }
     }
 }
@@ -271,9 +297,10 @@ struct GemmPlan {
 };
 
 GemmPlan plan_gemm(int N, int K, int sms) {
+    // About one wave of CTAs, each with at least 64 columns of K.
     const int tiles = (N + kTileN - 1) / kTileN;
-    int splits = std::max(1, (2 * sms + tiles - 1) / tiles);
-    splits = std::min(splits, std::max(1, K / 32));
+    int splits = std::max(1, (sms + tiles - 1) / tiles);
+    splits = std::min(splits, std::max(1, K / 64));
     int kps = (K + splits - 1) / splits;
     kps = (kps + kTileK - 1) / kTileK * kTileK;
     GemmPlan p;
