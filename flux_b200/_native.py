@@ -145,6 +145,8 @@ SIGNATURES: dict[str, tuple] = {
                                                          _i64, _i64, _i64, _i64, _i64, _p]),
     "fx_packed_gate_up_swiglu_f32": (_st, [_p, _p, _p, _i64, _i64, _p]),
     "fx_linear_f32": (_st, [_p, _p, _p, _i64, _i64, _i64, _p]),
+    "fx_tf32_split_f32": (_st, [_p, _p, _p, _i64, _p]),
+    "fx_linear_3xtf32_f32": (_st, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p]),
     "fx_greedy_argmax_f32": (_st, [_p, _i64, _p, _p]),
     "fx_greedy_argmax_update_f32": (_st, [_p, _i64, _p, _p, _i64, _p, _p, _p, _p]),
     "fx_decode_create": (_st, [ctypes.POINTER(ModelDesc), _p, _p, _p, _i64, _i64, _p, ctypes.POINTER(_p)]),

@@ -20,9 +20,11 @@
 // not depend on the other rows of the batch.
 #include "attention.cuh"
 #include "common.cuh"
+#include "tc_gemm.cuh"
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -296,13 +298,17 @@ struct GemmPlan {
     int splits = 1, k_per_split = 0;
 };
 
-GemmPlan plan_gemm(int N, int K, int sms) {
-    // About one wave of CTAs, each with at least 64 columns of K.
-    const int tiles = (N + kTileN - 1) / kTileN;
+GemmPlan plan_gemm(int N, int K, int sms, bool tensor_cores) {
+    // About one wave of CTAs; SIMT slices hold at least 64 columns of K,
+    // tensor-core slices at least one 32-column stage.
+    const int tile_n = tensor_cores ? kTcTileN : kTileN;
+    const int min_k = tensor_cores ? kTcTileK : 64;
+    const int tiles = (N + tile_n - 1) / tile_n;
     int splits = std::max(1, (sms + tiles - 1) / tiles);
-    splits = std::min(splits, std::max(1, K / 64));
+    splits = std::min(splits, std::max(1, K / min_k));
     int kps = (K + splits - 1) / splits;
-    kps = (kps + kTileK - 1) / kTileK * kTileK;
+    const int round = tensor_cores ? kTcTileK : kTileK;
+    kps = (kps + round - 1) / round * round;
     GemmPlan p;
     p.k_per_split = kps;
     p.splits = (K + kps - 1) / kps;
@@ -331,6 +337,10 @@ struct fx_batch {
     float *partials = nullptr, *attn_ws = nullptr;
     unsigned* error = nullptr;
     GemmPlan qkv_plan, o_plan, gu_plan, down_plan, lm_plan;
+    // Projections on tcgen05 tensor cores (3xTF32) unless FLUX_B200_BATCH_GEMM=simt.
+    bool tensor_cores = true;
+    fx::TcModelWeights tc;
+    CUtensorMap x_norm, x_attn, x_act;  // activation maps, 64 rows (rows >= batch stay zero)
     size_t layer_stride() const { return static_cast<size_t>(batch) * kKVHeads * capacity * kHeadDim; }
 };
 
@@ -338,9 +348,13 @@ namespace fx {
 namespace {
 
 fx_status gemm(fx_batch* r, const float* x, const float* w, int N, int K, const GemmPlan& p, float* direct_out,
-               cudaStream_t s) {
+               cudaStream_t s, const TcWeight* tw = nullptr, const CUtensorMap* xmap = nullptr) {
     const int M = static_cast<int>(r->batch);
     float* out = p.splits == 1 && direct_out != nullptr ? direct_out : r->partials;
+    if (r->tensor_cores) {
+        TcGemmArgs a = tc_args(*tw, *xmap, out, nullptr, reinterpret_cast<int*>(r->error), M, p.k_per_split);
+        return launch_tc_gemm(a, 64, p.splits, s, true);
+    }
     const dim3 grid((N + kTileN - 1) / kTileN, p.splits);
     return launch_dependent(skinny_gemm_kernel, grid, dim3(kGemmThreads), 0, s, "launching a batched projection", x, w,
                             out, M, N, K, p.k_per_split);
@@ -367,7 +381,7 @@ fx_status run_step(fx_batch* r, cudaStream_t s) {
         if ((st = launch_dependent(norm_rows_kernel, dim3(B), dim3(192), 0, s, "launching RMSNorm rows",
                                    static_cast<const float*>(r->h), m.input_norm[l], r->norm, m.epsilon)) != FX_OK)
             return st;
-        if ((st = gemm(r, r->norm, m.packed_qkv[l], kQKV, kHidden, r->qkv_plan, r->qkv, s)) != FX_OK) return st;
+        if ((st = gemm(r, r->norm, m.packed_qkv[l], kQKV, kHidden, r->qkv_plan, r->qkv, s, &r->tc.qkv[l], &r->x_norm)) != FX_OK) return st;
         if (r->qkv_plan.splits > 1 && (st = reduce(r, r->qkv_plan, kQKV, nullptr, r->qkv, s)) != FX_OK) return st;
         {
             const int64_t n = static_cast<int64_t>(B) * ((kQHeads + kKVHeads) * (kHeadDim / 2) + kKVHeads * kHeadDim);
@@ -392,12 +406,12 @@ fx_status run_step(fx_batch* r, cudaStream_t s) {
         a.chunks = (r->capacity + kCompactChunk - 1) / kCompactChunk;
         a.chunk_rows = kCompactChunk;
         if ((st = launch_compact_attention(a, s, true)) != FX_OK) return st;
-        if ((st = gemm(r, r->attn, m.o_proj[l], kHidden, kHidden, r->o_plan, nullptr, s)) != FX_OK) return st;
+        if ((st = gemm(r, r->attn, m.o_proj[l], kHidden, kHidden, r->o_plan, nullptr, s, &r->tc.o[l], &r->x_attn)) != FX_OK) return st;
         if ((st = reduce(r, r->o_plan, kHidden, r->h, r->h2, s)) != FX_OK) return st;
         if ((st = launch_dependent(norm_rows_kernel, dim3(B), dim3(192), 0, s, "launching RMSNorm rows",
                                    static_cast<const float*>(r->h2), m.post_norm[l], r->norm, m.epsilon)) != FX_OK)
             return st;
-        if ((st = gemm(r, r->norm, m.gate_up[l], kGateUp, kHidden, r->gu_plan, nullptr, s)) != FX_OK) return st;
+        if ((st = gemm(r, r->norm, m.gate_up[l], kGateUp, kHidden, r->gu_plan, nullptr, s, &r->tc.gate_up[l], &r->x_norm)) != FX_OK) return st;
         {
             const int64_t n = static_cast<int64_t>(B) * kInter;
             if ((st = launch_dependent(reduce_swiglu_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s,
@@ -405,13 +419,14 @@ fx_status run_step(fx_batch* r, cudaStream_t s) {
                                        r->gu_plan.splits, B, r->act)) != FX_OK)
                 return st;
         }
-        if ((st = gemm(r, r->act, m.down[l], kHidden, kInter, r->down_plan, nullptr, s)) != FX_OK) return st;
+        if ((st = gemm(r, r->act, m.down[l], kHidden, kInter, r->down_plan, nullptr, s, &r->tc.down[l], &r->x_act)) != FX_OK) return st;
         if ((st = reduce(r, r->down_plan, kHidden, r->h2, r->h, s)) != FX_OK) return st;
     }
     if ((st = launch_dependent(norm_rows_kernel, dim3(B), dim3(192), 0, s, "launching the final RMSNorm",
                                static_cast<const float*>(r->h), m.final_norm, r->norm, m.epsilon)) != FX_OK)
         return st;
-    if ((st = gemm(r, r->norm, m.lm_head, static_cast<int>(r->vocab), kHidden, r->lm_plan, r->logits, s)) != FX_OK)
+    if ((st = gemm(r, r->norm, m.lm_head, static_cast<int>(r->vocab), kHidden, r->lm_plan, r->logits, s, &r->tc.lm_head,
+                    &r->x_norm)) != FX_OK)
         return st;
     if (r->lm_plan.splits > 1 && (st = reduce(r, r->lm_plan, static_cast<int>(r->vocab), nullptr, r->logits, s)) != FX_OK)
         return st;
@@ -445,6 +460,7 @@ void destroy_batch(fx_batch* r) {
                     static_cast<void*>(r->value_cache), static_cast<void*>(r->h), static_cast<void*>(r->partials),
                     static_cast<void*>(r->attn_ws)})
         cudaFree(p);
+    tc_weights_release(&r->tc);
     delete r;
 }
 
@@ -463,20 +479,34 @@ fx_status create_batch(fx_batch* r, cudaStream_t stream) {
     const size_t cache = static_cast<size_t>(kLayers) * r->layer_stride() * sizeof(float);
     FX_CUDA_TRY(cudaMalloc(&r->key_cache, cache), "allocating the batched K cache");
     FX_CUDA_TRY(cudaMalloc(&r->value_cache, cache), "allocating the batched V cache");
-    // activations
-    const size_t act_floats = static_cast<size_t>(B) * (3 * kHidden + kQKV + kHidden + kHidden + kInter);
+    // activations; the projection inputs (norm, attn, act) hold 64 rows so
+    // the tensor-core tiles never read past them (rows >= batch stay zero)
+    const char* mode = std::getenv("FLUX_B200_BATCH_GEMM");
+    r->tensor_cores = !(mode != nullptr && std::strcmp(mode, "simt") == 0);
+    const int64_t R = std::max<int64_t>(B, 64);
+    const size_t act_floats = static_cast<size_t>(B) * (2 * kHidden + kQKV + kHidden) +
+                              static_cast<size_t>(R) * (2 * kHidden + kInter);
     FX_CUDA_TRY(cudaMalloc(&r->h, act_floats * sizeof(float)), "allocating batched activations");
+    FX_CUDA_TRY(cudaMemsetAsync(r->h, 0, act_floats * sizeof(float), stream), "clearing batched activations");
     r->h2 = r->h + B * kHidden;
-    r->norm = r->h2 + B * kHidden;
-    r->qkv = r->norm + B * kHidden;
+    r->qkv = r->h2 + B * kHidden;
     r->q = r->qkv + B * kQKV;
-    r->attn = r->q + B * kHidden;
-    r->act = r->attn + B * kHidden;
-    r->qkv_plan = plan_gemm(kQKV, kHidden, r->sms);
-    r->o_plan = plan_gemm(kHidden, kHidden, r->sms);
-    r->gu_plan = plan_gemm(kGateUp, kHidden, r->sms);
-    r->down_plan = plan_gemm(kHidden, kInter, r->sms);
-    r->lm_plan = plan_gemm(static_cast<int>(r->vocab), kHidden, r->sms);
+    r->norm = r->q + B * kHidden;
+    r->attn = r->norm + R * kHidden;
+    r->act = r->attn + R * kHidden;
+    if (r->tensor_cores) {
+        fx_status st0 = tc_weights_create(r->model, true, &r->tc, stream);
+        if (st0 != FX_OK) return st0;
+        if ((st0 = tc_encode_map(&r->x_norm, r->norm, R, kHidden, 64, "the batched norm rows")) != FX_OK) return st0;
+        if ((st0 = tc_encode_map(&r->x_attn, r->attn, R, kHidden, 64, "the batched attention rows")) != FX_OK) return st0;
+        if ((st0 = tc_encode_map(&r->x_act, r->act, R, kInter, 64, "the batched SwiGLU rows")) != FX_OK) return st0;
+    }
+    const bool tc = r->tensor_cores;
+    r->qkv_plan = plan_gemm(kQKV, kHidden, r->sms, tc);
+    r->o_plan = plan_gemm(kHidden, kHidden, r->sms, tc);
+    r->gu_plan = plan_gemm(kGateUp, kHidden, r->sms, tc);
+    r->down_plan = plan_gemm(kHidden, kInter, r->sms, tc);
+    r->lm_plan = plan_gemm(static_cast<int>(r->vocab), kHidden, r->sms, tc);
     size_t partial_floats = 0;
     const std::pair<const GemmPlan*, int> plans[] = {{&r->qkv_plan, kQKV}, {&r->o_plan, kHidden},
                                                      {&r->gu_plan, kGateUp}, {&r->down_plan, kHidden},
@@ -637,6 +667,10 @@ extern "C" fx_status fx_batch_check(fx_batch* r) {
     }
     if (error & 1u) {
         set_error("flux batched decode: a bounded wait in the attention kernel gave up");
+        return FX_ERR_DEVICE;
+    }
+    if (error & 256u) {
+        set_error("flux batched decode: a bounded wait in a tensor-core projection gave up");
         return FX_ERR_DEVICE;
     }
     return FX_OK;

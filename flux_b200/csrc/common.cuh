@@ -51,6 +51,10 @@ fx_status cuda_failure(const char* what, cudaError_t error);
 
 inline cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
 
+// Device error word of a decode runtime; the prefill's kernels report into
+// it (bit 8: a tensor-core projection's bounded wait gave up).
+int* decode_error_word(fx_decode* runtime);
+
 // Programmatic dependent launch.  A kernel launched with launch_dependent()
 // is scheduled as the previous kernel in the stream retires its CTAs; it
 // calls grid_dependency_wait() before touching anything that kernel produced

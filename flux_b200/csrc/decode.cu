@@ -944,6 +944,10 @@ extern "C" fx_status fx_decode_install_prefill(fx_decode* r, const int64_t* toke
     return FX_OK;
 }
 
+namespace fx {
+int* decode_error_word(fx_decode* runtime) { return runtime == nullptr ? nullptr : runtime->error; }
+}  // namespace fx
+
 extern "C" fx_status fx_decode_wait(fx_decode* r, void* stream) {
     FX_REQUIRE(r != nullptr, "fx_decode_wait: runtime is null");
     DeviceGuard guard(r->model.device);
@@ -985,6 +989,10 @@ extern "C" fx_status fx_decode_read_state(fx_decode* r, int32_t which, int64_t* 
     FX_CUDA_TRY(cudaMemcpy(value, src, sizeof(int64_t), cudaMemcpyDeviceToHost), "reading decode state");
     int error = 0;
     FX_CUDA_TRY(cudaMemcpy(&error, r->error, sizeof(int), cudaMemcpyDeviceToHost), "reading decode error flag");
+    if (error & 256) {
+        set_error("flux native prefill: a bounded wait in a tensor-core projection gave up");
+        return FX_ERR_DEVICE;
+    }
     if (error != 0) {
         set_error("flux native full decode: a step ran with its position outside the cache capacity");
         return FX_ERR_DEVICE;

@@ -6,10 +6,12 @@
 // online-softmax attention, o_proj GEMM + residual, RMSNorm, gate/up GEMM,
 // SwiGLU, down GEMM + residual) -> final RMSNorm of the last row -> LM head
 // -> greedy token -> decode state handoff (position = prompt length,
-// generated[0] = token, step = 1).  Projections use an FP32 SIMT GEMM
-// (exact FP32 products, unlike TF32 tensor cores); the attention keeps one
-// query row per thread with the K/V tile in shared memory.
+// generated[0] = token, step = 1).  The four projections per layer run on
+// tcgen05 tensor cores with the 3xTF32 split (FP32-level results; weights
+// split once at create); the attention is a flash-style FP32 SIMT kernel.
+// The SIMT GEMM below serves the generic fx_linear_f32 op.
 #include "common.cuh"
+#include "tc_gemm.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -341,6 +343,9 @@ struct fx_prefill {
     float* logits = nullptr;
     int64_t* initial_token = nullptr;
     float *h_a, *h_b, *norm, *residual, *qkv, *q, *attn, *gate_up, *swiglu_out, *final_hidden;
+    fx::TcModelWeights tc;                  // split projection weights
+    CUtensorMap x_norm, x_attn, x_swiglu;   // activation maps of the projections
+    int bm = 128;                           // activation rows per tensor-core tile
 };
 
 namespace fx {
@@ -362,6 +367,10 @@ fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
     if (st != FX_OK) return st;
     const int64_t S = p->rows;
     const int64_t cap = m.capacity;
+    int* error = decode_error_word(p->decode);
+    auto project = [&](const TcWeight& w, const CUtensorMap& x, float* c, const float* residual) {
+        return launch_tc_gemm(tc_args(w, x, c, residual, error, static_cast<int>(S), w.cols), p->bm, 1, s, false);
+    };
     const size_t layer_stride = static_cast<size_t>(kKVHeads) * cap * kHeadDim;
     embedding_gather_kernel<<<blocks_for(S * kHidden), 256, 0, s>>>(ids, m.embedding, p->h_a, S, m.vocab);
     FX_CUDA_TRY(cudaGetLastError(), "launching embedding gather");
@@ -371,7 +380,7 @@ fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
         float* kc = db.key_cache + l * layer_stride;
         float* vc = db.value_cache + l * layer_stride;
         if ((st = fx_rmsnorm_f32(in, m.input_norm[l], p->norm, S, kHidden, m.epsilon, s)) != FX_OK) return st;
-        if ((st = launch_gemm_nt(p->norm, m.packed_qkv[l], p->qkv, S, kQKV, kHidden, s)) != FX_OK) return st;
+        if ((st = project(p->tc.qkv[l], p->x_norm, p->qkv, nullptr)) != FX_OK) return st;
         prefill_rope_cache_kernel<<<blocks_for(S * kQKV), 256, 0, s>>>(p->qkv, m.rope_cos, m.rope_sin, p->q, kc, vc,
                                                                        S, cap);
         FX_CUDA_TRY(cudaGetLastError(), "launching prefill RoPE/cache fill");
@@ -379,13 +388,11 @@ fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
                                kFlashSmem, s>>>(p->q, kc, vc, p->attn, S, cap, m.attention_scale[l]);
         FX_CUDA_TRY(cudaGetLastError(), "launching prefill attention");
         // residual = attn . Wo^T + in; norm = rmsnorm(residual)
-        if ((st = launch_gemm_nt_residual(p->attn, m.o_proj[l], p->residual, in, S, kHidden, kHidden, s)) != FX_OK)
-            return st;
+        if ((st = project(p->tc.o[l], p->x_attn, p->residual, in)) != FX_OK) return st;
         if ((st = fx_rmsnorm_f32(p->residual, m.post_norm[l], p->norm, S, kHidden, m.epsilon, s)) != FX_OK) return st;
-        if ((st = launch_gemm_nt(p->norm, m.gate_up[l], p->gate_up, S, kGateUp, kHidden, s)) != FX_OK) return st;
+        if ((st = project(p->tc.gate_up[l], p->x_norm, p->gate_up, nullptr)) != FX_OK) return st;
         if ((st = fx_packed_swiglu_f32(p->gate_up, p->swiglu_out, S, kInter, s)) != FX_OK) return st;
-        if ((st = launch_gemm_nt_residual(p->swiglu_out, m.down[l], out, p->residual, S, kHidden, kInter, s)) != FX_OK)
-            return st;
+        if ((st = project(p->tc.down[l], p->x_swiglu, out, p->residual)) != FX_OK) return st;
     }
     const float* last = p->h_a + (S - 1) * kHidden;  // 30 layers end in h_a
     if ((st = fx_rmsnorm_f32(last, m.final_norm, p->final_hidden, 1, kHidden, m.epsilon, s)) != FX_OK) return st;
@@ -400,6 +407,7 @@ void prefill_release(fx_prefill* p) {
     cudaGetDevice(&prev);
     cudaSetDevice(p->model.device);
     if (p->decode != nullptr) fx_decode_destroy(p->decode);  // waits for pending work
+    tc_weights_release(&p->tc);
     cudaFree(p->buffer);
     cudaFree(p->logits);
     cudaFree(p->initial_token);
@@ -409,11 +417,15 @@ void prefill_release(fx_prefill* p) {
 
 fx_status prefill_create_impl(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
     const int64_t S = p->rows;
+    p->bm = S <= 64 ? 64 : 128;
+    // The projection inputs (norm, attn, swiglu_out) hold at least one
+    // tensor-core tile of rows; rows past S stay zero.
+    const int64_t R = std::max<int64_t>(S, p->bm);
     const size_t counts[] = {static_cast<size_t>(S) * kHidden, static_cast<size_t>(S) * kHidden,
-                             static_cast<size_t>(S) * kHidden, static_cast<size_t>(S) * kHidden,
+                             static_cast<size_t>(R) * kHidden, static_cast<size_t>(S) * kHidden,
                              static_cast<size_t>(S) * kQKV,    static_cast<size_t>(S) * kHidden,
-                             static_cast<size_t>(S) * kHidden, static_cast<size_t>(S) * kGateUp,
-                             static_cast<size_t>(S) * kInter,  static_cast<size_t>(kHidden)};
+                             static_cast<size_t>(R) * kHidden, static_cast<size_t>(S) * kGateUp,
+                             static_cast<size_t>(R) * kInter,  static_cast<size_t>(kHidden)};
     size_t total = 0;
     for (size_t c : counts) total += (c + 63) / 64 * 64;
     p->buffer_bytes = total * sizeof(float);
@@ -427,6 +439,13 @@ fx_status prefill_create_impl(fx_prefill* p, const int64_t* ids, cudaStream_t s)
         *views[i] = cursor;
         cursor += (counts[i] + 63) / 64 * 64;
     }
+    FX_CUDA_TRY(cudaMemsetAsync(p->buffer, 0, p->buffer_bytes, s), "clearing the prefill workspace");
+    fx_status st0 = tc_weights_create(p->model, false, &p->tc, s);
+    if (st0 != FX_OK) return st0;
+    if ((st0 = tc_encode_map(&p->x_norm, p->norm, R, kHidden, p->bm, "the prefill norm rows")) != FX_OK) return st0;
+    if ((st0 = tc_encode_map(&p->x_attn, p->attn, R, kHidden, p->bm, "the prefill attention rows")) != FX_OK) return st0;
+    if ((st0 = tc_encode_map(&p->x_swiglu, p->swiglu_out, R, kInter, p->bm, "the prefill SwiGLU rows")) != FX_OK)
+        return st0;
     FX_CUDA_TRY(cudaMemsetAsync(p->initial_token, 0, sizeof(int64_t), s), "initializing decode token");
     fx_status st = fx_decode_create(&p->model, p->initial_token, nullptr, nullptr, 0, 0, s, &p->decode);
     if (st != FX_OK) return st;

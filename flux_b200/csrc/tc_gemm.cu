@@ -1,0 +1,559 @@
+// 3xTF32 projection GEMM on tcgen05 tensor cores (sm_100a).
+//
+// One CTA computes a 128 (weight rows) x BM (activation rows) tile of
+// C = X . W^T over its K slice.  192 threads in three roles:
+//   warp 0, lane 0  TMA producer: per 32-column stage, W_hi and W_lo boxes
+//                   (128 x 32) and the raw X box (BM x 32), 128-byte
+//                   swizzled, completing on full[stage];
+//   warp 1          allocates 4 BM TMEM columns; lane 0 issues the MMAs
+//                   (M = 128, N = BM, K = 8 per instruction, 3 products per
+//                   K step), commits each stage back to empty[stage] and its
+//                   hi.hi accumulator to acc_full[stage & 1];
+//   warps 2-5       split the staged X tile in shared memory into hi (in
+//                   place) and lo (a second buffer), publish it to the
+//                   tensor core with fence.proxy.async, arrive on
+//                   conv[stage]; they add each stage's hi.hi accumulator
+//                   into FP32 registers (warp w owns TMEM lanes 32 (w % 4)
+//                   ..), then the cross-term accumulator, and write C,
+//                   transposed so each store is 32 consecutive floats of one
+//                   output row.
+// The operands are K-major with the canonical 128-byte swizzle: 8-row groups
+// 1024 bytes apart (SBO), the 8-column K steps 32 bytes apart inside a row.
+// Every mbarrier wait is bounded by %globaltimer; a wait that gives up sets
+// bit 8 of the error word, stops the CTA's loops, lets copies and MMAs in
+// flight finish (bounded), frees TMEM and returns.
+#include "tc_gemm.cuh"
+
+#include <mutex>
+#include <string>
+
+namespace fx {
+namespace {
+
+constexpr unsigned long long kTcWaitNs = 1000000000ull;  // 1 s per wait
+constexpr int kTcThreads = 192;
+constexpr uint32_t kWBox = kTcTileN * kTcTileK * 4;  // 16 KB
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long now_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void bar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void bar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void bar_expect(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool bar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait: false when it gave up (error recorded) or another role of
+// the CTA already gave up.
+__device__ bool bar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* error) {
+    if (bar_test(bar, parity)) return true;
+    const unsigned long long t0 = now_ns();
+    while (!bar_test(bar, parity)) {
+        if (*abort) return false;
+        if (now_ns() - t0 > kTcWaitNs) {
+            *abort = 1;
+            atomicOr(error, 256);
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void tma_box(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart, descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    return static_cast<uint64_t>((addr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+           (static_cast<uint64_t>(2) << 61);
+}
+
+// Instruction descriptor: FP32 accumulate, TF32 A and B, both K-major,
+// M = 128, N = n.
+__host__ __device__ constexpr uint32_t tf32_idesc(int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(kTcTileN >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_before_sync() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_after_sync() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns of TMEM into 32 registers.
+__device__ __forceinline__ void tmem_load32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BM>
+struct TcLayout {
+    static constexpr uint32_t kX = BM * kTcTileK * 4;
+    static constexpr uint32_t kStage = 2 * kWBox + 2 * kX;  // W_hi, W_lo, X (-> X_hi), X_lo
+    static constexpr int kStages = BM == 64 ? 4 : 3;
+    static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStage + 1024 + 256;
+    // TMEM columns: [0, BM) the cross terms, [BM, 2 BM) and [2 BM, 3 BM)
+    // the per-stage hi.hi products (double-buffered); allocation 4 BM.
+    static constexpr uint32_t kTmemCols = 4 * BM;
+};
+
+template <int BM>
+__global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ TcGemmArgs a) {
+    using L = TcLayout<BM>;
+    constexpr int S = L::kStages;
+    extern __shared__ unsigned char tc_raw[];
+    unsigned char* smem = tc_raw + ((1024u - (smem_addr(tc_raw) & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * L::kStage);
+    uint64_t* conv = full + S;
+    uint64_t* empty = conv + S;
+    uint64_t* acc_full = empty + S;   // [2] a stage's hi.hi products are in TMEM
+    uint64_t* acc_empty = acc_full + 2;  // [2] the epilogue has taken them
+    uint64_t* done = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int n0 = blockIdx.x * kTcTileN, m0 = blockIdx.y * BM;
+    const int k0 = blockIdx.z * a.k_per_split;
+    const int k1 = min(a.k, k0 + a.k_per_split);
+    const int nk = k1 > k0 ? (k1 - k0 + kTcTileK - 1) / kTcTileK : 0;
+    auto w_hi = [&](int s) { return smem + s * L::kStage; };
+    auto w_lo = [&](int s) { return smem + s * L::kStage + kWBox; };
+    auto x_hi = [&](int s) { return smem + s * L::kStage + 2 * kWBox; };
+    auto x_lo = [&](int s) { return smem + s * L::kStage + 2 * kWBox + L::kX; };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            bar_init(&full[s], 1);
+            bar_init(&conv[s], 128);
+            bar_init(&empty[s], 1);
+        }
+        for (int j = 0; j < 2; ++j) {
+            bar_init(&acc_full[j], 1);
+            bar_init(&acc_empty[j], 128);
+        }
+        bar_init(done, 1);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(L::kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % S;
+                if (i >= S && !bar_wait(&empty[s], static_cast<uint32_t>(i / S - 1) & 1u, abort, a.error)) break;
+                if (*abort) break;
+                const int kx = k0 + i * kTcTileK;
+                bar_expect(&full[s], 2 * kWBox + L::kX);
+                tma_box(w_hi(s), &a.w_hi, kx, n0, &full[s]);
+                tma_box(w_lo(s), &a.w_lo, kx, n0, &full[s]);
+                if (i == 0) grid_dependency_wait();  // X comes from the previous kernel
+                tma_box(x_hi(s), &a.x, kx, m0, &full[s]);
+                issued = i + 1;
+            }
+            if (nk == 0) grid_dependency_wait();
+            // Copies still in flight land before the CTA leaves (a no-op
+            // unless a consumer gave up early).
+            for (int i = max(0, issued - S); i < issued; ++i) {
+                const unsigned long long t0 = now_ns();
+                while (!bar_test(&full[i % S], static_cast<uint32_t>(i / S) & 1u))
+                    if (now_ns() - t0 > kTcWaitNs) break;
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = tf32_idesc(BM);
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % S, j = i & 1;
+                if (!bar_wait(&conv[s], static_cast<uint32_t>(i / S) & 1u, abort, a.error)) break;
+                if (i >= 2 && !bar_wait(&acc_empty[j], static_cast<uint32_t>(i / 2 - 1) & 1u, abort, a.error)) break;
+                fence_after_sync();
+                const uint64_t ah = sw128_desc(smem_addr(w_hi(s))), al = sw128_desc(smem_addr(w_lo(s)));
+                const uint64_t bh = sw128_desc(smem_addr(x_hi(s))), bl = sw128_desc(smem_addr(x_lo(s)));
+                const uint32_t main_acc = tmem + static_cast<uint32_t>((1 + j) * BM);
+#pragma unroll
+                for (int kk = 0; kk < kTcTileK / 8; ++kk) {
+                    const uint64_t step = static_cast<uint64_t>(kk * 32 >> 4);  // 8 TF32 = 32 bytes
+                    mma_tf32(tmem, ah + step, bl + step, idesc, (i | kk) != 0 ? 1u : 0u);
+                    mma_tf32(tmem, al + step, bh + step, idesc, 1u);
+                    mma_tf32(main_acc, ah + step, bh + step, idesc, kk != 0 ? 1u : 0u);
+                }
+                mma_commit(&empty[s]);
+                mma_commit(&acc_full[j]);
+            }
+            mma_commit(done);  // arrives once every MMA issued above has completed
+        }
+        __syncwarp();
+    } else {
+        // The tensor core's accumulation truncates, so a long chain of MMAs
+        // into one accumulator drifts by about one unit in the last place
+        // per step.  Each stage's hi.hi products start a fresh accumulator
+        // and are added here in FP32 with round-to-nearest; the cross terms
+        // (2^-11 of the result) stay in one accumulator.
+        const int t = threadIdx.x - 64;  // 0..127
+        const int quarter = warp & 3;
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        float acc[BM];
+#pragma unroll
+        for (int c = 0; c < BM; ++c) acc[c] = 0.0f;
+        bool ok = true;
+        auto promote = [&](int i) {
+            const int j = i & 1;
+            ok = ok && bar_wait(&acc_full[j], static_cast<uint32_t>(i / 2) & 1u, abort, a.error);
+            __syncwarp();
+            fence_after_sync();
+#pragma unroll
+            for (int col = 0; col < BM; col += 32) {
+                float v[32];
+                tmem_load32(tmem + lane_base + static_cast<uint32_t>((1 + j) * BM + col), v);
+#pragma unroll
+                for (int c = 0; c < 32; ++c) acc[col + c] += v[c];
+            }
+            fence_before_sync();
+            bar_arrive(&acc_empty[j]);
+        };
+        for (int i = 0; i < nk && ok; ++i) {
+            const int s = i % S;
+            if (!bar_wait(&full[s], static_cast<uint32_t>(i / S) & 1u, abort, a.error)) {
+                ok = false;
+                break;
+            }
+            float4* xh = reinterpret_cast<float4*>(x_hi(s));
+            float4* xl = reinterpret_cast<float4*>(x_lo(s));
+#pragma unroll 4
+            for (int q = t; q < BM * kTcTileK / 4; q += 128) {
+                const float4 v = xh[q];
+                float4 h, r;
+                h.x = tf32_rna(v.x);
+                h.y = tf32_rna(v.y);
+                h.z = tf32_rna(v.z);
+                h.w = tf32_rna(v.w);
+                r.x = tf32_rna(v.x - h.x);
+                r.y = tf32_rna(v.y - h.y);
+                r.z = tf32_rna(v.z - h.z);
+                r.w = tf32_rna(v.w - h.w);
+                xh[q] = h;
+                xl[q] = r;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            bar_arrive(&conv[s]);
+            if (i >= 1) promote(i - 1);
+        }
+        if (ok && nk > 0) promote(nk - 1);
+        grid_dependency_wait();  // the residual and C belong to earlier kernels too
+        ok = ok && bar_wait(done, 0, abort, a.error) && !*abort;
+        __syncwarp();
+        fence_after_sync();
+        const int n = n0 + quarter * 32 + lane;
+        float* c = a.c + static_cast<long long>(blockIdx.z) * a.split_stride;
+#pragma unroll
+        for (int col = 0; col < BM; col += 32) {
+            float v[32];
+            if (nk > 0) {
+                tmem_load32(tmem + lane_base + static_cast<uint32_t>(col), v);
+            } else {
+#pragma unroll
+                for (int q = 0; q < 32; ++q) v[q] = 0.0f;
+            }
+            if (ok && n < a.n) {
+#pragma unroll
+                for (int q = 0; q < 32; ++q) {
+                    const int m = m0 + col + q;
+                    if (m < a.m) {
+                        const long long at = static_cast<long long>(m) * a.ldc + n;
+                        const float r = acc[col + q] + v[q];
+                        c[at] = a.residual != nullptr ? r + a.residual[at] : r;
+                    }
+                }
+            }
+        }
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after_sync();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::kTmemCols)
+                     : "memory");
+    }
+}
+
+__global__ void tf32_split_kernel(const float4* __restrict__ w, float4* __restrict__ hi, float4* __restrict__ lo,
+                                  size_t n4) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const float4 v = w[i];
+        float4 h, r;
+        h.x = tf32_rna(v.x);
+        h.y = tf32_rna(v.y);
+        h.z = tf32_rna(v.z);
+        h.w = tf32_rna(v.w);
+        r.x = tf32_rna(v.x - h.x);
+        r.y = tf32_rna(v.y - h.y);
+        r.z = tf32_rna(v.z - h.z);
+        r.w = tf32_rna(v.w - h.w);
+        hi[i] = h;
+        lo[i] = r;
+    }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+template <int BM>
+fx_status configure_once() {
+    static std::once_flag once;
+    static cudaError_t status = cudaSuccess;
+    std::call_once(once, [] {
+        status = cudaFuncSetAttribute(tc_gemm_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(TcLayout<BM>::kSmem));
+    });
+    FX_CUDA_TRY(status, "raising the tensor-core GEMM's shared memory");
+    return FX_OK;
+}
+
+}  // namespace
+
+fx_status tc_encode_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int box_rows,
+                        const char* what) {
+    static std::once_flag once;
+    static EncodeTiledFn encode = nullptr;
+    std::call_once(once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult found{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &found) == cudaSuccess &&
+            found == cudaDriverEntryPointSuccess)
+            encode = reinterpret_cast<EncodeTiledFn>(fn);
+    });
+    if (encode == nullptr) {
+        set_error("flux tensor-core GEMM: cuTensorMapEncodeTiled is unavailable from the driver");
+        return FX_ERR_CUDA;
+    }
+    if (rows <= 0 || cols <= 0 || cols % 4 != 0 || reinterpret_cast<uintptr_t>(base) % 16 != 0 || box_rows <= 0 ||
+        box_rows > 256) {
+        set_error(std::string("flux tensor-core GEMM: ") + what + " is not a 16-byte aligned row-major matrix");
+        return FX_ERR_INVALID;
+    }
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * sizeof(float)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcTileK), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t element_strides[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+                              element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error(std::string("flux tensor-core GEMM: encoding the tensor map of ") + what + " failed (CUresult " +
+                  std::to_string(static_cast<int>(r)) + ")");
+        return FX_ERR_CUDA;
+    }
+    return FX_OK;
+}
+
+fx_status tc_split(const float* w, float* hi, float* lo, size_t n, cudaStream_t stream) {
+    FX_REQUIRE(n % 4 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(hi) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(lo) % 16 == 0,
+               "tf32 split: sizes and pointers must be multiples of 4 floats / 16 bytes");
+    if (n == 0) return FX_OK;
+    const size_t n4 = n / 4;
+    const unsigned blocks = static_cast<unsigned>(std::min<size_t>((n4 + 255) / 256, 148 * 16));
+    tf32_split_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const float4*>(w), reinterpret_cast<float4*>(hi),
+                                                  reinterpret_cast<float4*>(lo), n4);
+    FX_CUDA_TRY(cudaGetLastError(), "launching the tf32 split");
+    return FX_OK;
+}
+
+fx_status launch_tc_gemm(const TcGemmArgs& args, int bm, int splits, cudaStream_t stream, bool dependent) {
+    FX_REQUIRE(args.k % kTcTileK == 0 && args.k_per_split % kTcTileK == 0 && args.k_per_split > 0 && splits >= 1 &&
+                   args.m > 0 && args.n > 0 && args.ldc >= args.n,
+               "tensor-core GEMM: K and its slices must be multiples of 32, M, N > 0");
+    const dim3 grid(static_cast<unsigned>((args.n + kTcTileN - 1) / kTcTileN),
+                    static_cast<unsigned>((args.m + bm - 1) / bm), static_cast<unsigned>(splits));
+    fx_status st;
+    if (bm == 64) {
+        if ((st = configure_once<64>()) != FX_OK) return st;
+        if (dependent)
+            return launch_dependent(tc_gemm_kernel<64>, grid, dim3(kTcThreads), TcLayout<64>::kSmem, stream,
+                                    "launching the tensor-core GEMM", args);
+        tc_gemm_kernel<64><<<grid, kTcThreads, TcLayout<64>::kSmem, stream>>>(args);
+    } else if (bm == 128) {
+        if ((st = configure_once<128>()) != FX_OK) return st;
+        if (dependent)
+            return launch_dependent(tc_gemm_kernel<128>, grid, dim3(kTcThreads), TcLayout<128>::kSmem, stream,
+                                    "launching the tensor-core GEMM", args);
+        tc_gemm_kernel<128><<<grid, kTcThreads, TcLayout<128>::kSmem, stream>>>(args);
+    } else {
+        set_error("tensor-core GEMM: the activation tile must be 64 or 128 rows");
+        return FX_ERR_INVALID;
+    }
+    FX_CUDA_TRY(cudaGetLastError(), "launching the tensor-core GEMM");
+    return FX_OK;
+}
+
+fx_status tc_weights_create(const fx_model_desc& model, bool lm_head, TcModelWeights* out, cudaStream_t stream) {
+    const size_t per_layer = static_cast<size_t>(kQKV + kHidden + kGateUp) * kHidden + static_cast<size_t>(kHidden) * kInter;
+    const size_t lm = lm_head ? static_cast<size_t>(model.vocab) * kHidden : 0;
+    const size_t total = 2 * (per_layer * kLayers + lm);
+    FX_CUDA_TRY(cudaMalloc(&out->buffer, total * sizeof(float)), "allocating the split projection weights");
+    float* cursor = out->buffer;
+    auto make = [&](TcWeight& w, const float* src, int rows, int cols, const char* what) -> fx_status {
+        const size_t n = static_cast<size_t>(rows) * cols;
+        float* hi = cursor;
+        float* lo = cursor + n;
+        cursor += 2 * n;
+        w.rows = rows;
+        w.cols = cols;
+        fx_status st = tc_split(src, hi, lo, n, stream);
+        if (st != FX_OK) return st;
+        if ((st = tc_encode_map(&w.hi, hi, rows, cols, kTcTileN, what)) != FX_OK) return st;
+        return tc_encode_map(&w.lo, lo, rows, cols, kTcTileN, what);
+    };
+    fx_status st;
+    for (int l = 0; l < kLayers; ++l) {
+        if ((st = make(out->qkv[l], model.packed_qkv[l], kQKV, kHidden, "packed_qkv")) != FX_OK) return st;
+        if ((st = make(out->o[l], model.o_proj[l], kHidden, kHidden, "o_proj")) != FX_OK) return st;
+        if ((st = make(out->gate_up[l], model.gate_up[l], kGateUp, kHidden, "gate_up")) != FX_OK) return st;
+        if ((st = make(out->down[l], model.down[l], kHidden, kInter, "down")) != FX_OK) return st;
+    }
+    out->has_lm_head = lm_head;
+    if (lm_head && (st = make(out->lm_head, model.lm_head, static_cast<int>(model.vocab), kHidden, "lm_head")) != FX_OK)
+        return st;
+    return FX_OK;
+}
+
+void tc_weights_release(TcModelWeights* w) {
+    if (w == nullptr) return;
+    cudaFree(w->buffer);
+    w->buffer = nullptr;
+}
+
+TcGemmArgs tc_args(const TcWeight& w, const CUtensorMap& x, float* c, const float* residual, int* error, int m,
+                   int k_per_split) {
+    TcGemmArgs a{};
+    a.w_hi = w.hi;
+    a.w_lo = w.lo;
+    a.x = x;
+    a.c = c;
+    a.residual = residual;
+    a.error = error;
+    a.m = m;
+    a.n = w.rows;
+    a.k = w.cols;
+    a.ldc = w.rows;
+    a.k_per_split = k_per_split;
+    a.split_stride = static_cast<long long>(m) * w.rows;
+    return a;
+}
+
+}  // namespace fx
+
+using namespace fx;
+
+extern "C" fx_status fx_tf32_split_f32(const float* input, float* hi, float* lo, int64_t n, void* stream) {
+    FX_REQUIRE(input && hi && lo, "fx_tf32_split_f32: null pointer");
+    FX_REQUIRE(n >= 0, "fx_tf32_split_f32: negative size");
+    return tc_split(input, hi, lo, static_cast<size_t>(n), as_stream(stream));
+}
+
+extern "C" fx_status fx_linear_3xtf32_f32(const float* input, const float* weight_hi, const float* weight_lo,
+                                          const float* residual, float* output, int64_t m, int64_t k, int64_t n,
+                                          int* error, void* stream) {
+    FX_REQUIRE(input && weight_hi && weight_lo && output && error, "fx_linear_3xtf32_f32: null pointer");
+    FX_REQUIRE(m > 0 && n > 0 && k > 0 && k % kTcTileK == 0 && m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 31),
+               "fx_linear_3xtf32_f32: M, N > 0 and K a positive multiple of 32");
+    const int bm = m <= 64 ? 64 : 128;
+    TcGemmArgs args{};
+    fx_status st;
+    if ((st = tc_encode_map(&args.w_hi, weight_hi, n, k, kTcTileN, "weight_hi")) != FX_OK) return st;
+    if ((st = tc_encode_map(&args.w_lo, weight_lo, n, k, kTcTileN, "weight_lo")) != FX_OK) return st;
+    if ((st = tc_encode_map(&args.x, input, m, k, bm, "input")) != FX_OK) return st;
+    args.c = output;
+    args.residual = residual;
+    args.error = error;
+    args.m = static_cast<int>(m);
+    args.n = static_cast<int>(n);
+    args.k = static_cast<int>(k);
+    args.ldc = static_cast<int>(n);
+    args.k_per_split = static_cast<int>(k);
+    args.split_stride = 0;
+    return launch_tc_gemm(args, bm, 1, as_stream(stream), false);
+}
+

@@ -149,6 +149,22 @@ FX_API fx_status fx_packed_gate_up_swiglu_f32(const float* input, const float* w
 FX_API fx_status fx_linear_f32(const float* input, const float* weight, float* output, int64_t m, int64_t k,
                         int64_t n, void* stream);
 
+/* hi[i] = tf32(input[i]) and lo[i] = tf32(input[i] - hi[i]) (round to nearest,
+ * ties away), n % 4 == 0, 16-byte aligned.  No counterpart in the reference:
+ * the operand split of the 3xTF32 tensor-core projections below. */
+FX_API fx_status fx_tf32_split_f32(const float* input, float* hi, float* lo, int64_t n, void* stream);
+
+/* output[M, N] = input[M, K] . weight[N, K]^T (+ residual[M, N] when non-null)
+ * on tcgen05 tensor cores with the 3xTF32 split (weight given as the hi / lo
+ * halves from fx_tf32_split_f32; the input is split on chip), FP32
+ * accumulation; K % 32 == 0, 16-byte aligned rows.  `error` is a device int
+ * that gets bit 8 if an internal wait gave up (never expected).  Same
+ * contract as fx_linear_f32 (csrc/cublaslt_linear/cublaslt_linear_cuda.h:20-33),
+ * used by the batched and prefill projections. */
+FX_API fx_status fx_linear_3xtf32_f32(const float* input, const float* weight_hi, const float* weight_lo,
+                               const float* residual, float* output, int64_t m, int64_t k, int64_t n,
+                               int* error, void* stream);
+
 /* *token = argmax(logits) with NaN as the maximum and the lowest index on ties.
  * Replaces flux::greedy_argmax_cuda_fp32
  * (csrc/greedy_generation/greedy_generation_cuda.h:9-14). */
