@@ -1,20 +1,22 @@
 // 3xTF32 projection GEMM on tcgen05 tensor cores (sm_100a).
 //
 // One CTA computes a 128 (weight rows) x BM (activation rows) tile of
-// C = X . W^T over its K slice.  192 threads in three roles:
+// C = X . W^T over its K slice.  320 threads in three roles:
 //   warp 0, lane 0  TMA producer: per 32-column stage, W_hi and W_lo boxes
 //                   (128 x 32) and the raw X box (BM x 32), 128-byte
 //                   swizzled, completing on full[stage];
 //   warp 1          allocates 4 BM TMEM columns; lane 0 issues the MMAs
 //                   (M = 128, N = BM, K = 8 per instruction, 3 products per
 //                   K step), commits each stage back to empty[stage] and its
-//                   hi.hi accumulator to acc_full[stage & 1];
-//   warps 2-5       split the staged X tile in shared memory into hi (in
+//                   hi.hi accumulator (fresh every second stage, two
+//                   buffers) to acc_full;
+//   warps 2-9       split the staged X tile in shared memory into hi (in
 //                   place) and lo (a second buffer), publish it to the
 //                   tensor core with fence.proxy.async, arrive on
-//                   conv[stage]; they add each stage's hi.hi accumulator
-//                   into FP32 registers (warp w owns TMEM lanes 32 (w % 4)
-//                   ..), then the cross-term accumulator, and write C,
+//                   conv[stage]; they add the hi.hi accumulator of every
+//                   second stage into FP32 registers (warp w reads TMEM
+//                   lanes 32 (w % 4) .., half the columns), then the
+//                   cross-term accumulator, and write C,
 //                   transposed so each store is 32 consecutive floats of one
 //                   output row.
 // The operands are K-major with the canonical 128-byte swizzle: 8-row groups
@@ -31,7 +33,9 @@ namespace fx {
 namespace {
 
 constexpr unsigned long long kTcWaitNs = 1000000000ull;  // 1 s per wait
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;  // producer warp, MMA warp, 8 split/epilogue warps
+constexpr int kTcEpi = kTcThreads - 64;
+constexpr int kTcPromote = 2;    // stages per hi.hi accumulator before it is added into registers
 constexpr uint32_t kWBox = kTcTileN * kTcTileK * 4;  // 16 KB
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -193,12 +197,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             bar_init(&full[s], 1);
-            bar_init(&conv[s], 128);
+            bar_init(&conv[s], kTcEpi);
             bar_init(&empty[s], 1);
         }
         for (int j = 0; j < 2; ++j) {
             bar_init(&acc_full[j], 1);
-            bar_init(&acc_empty[j], 128);
+            bar_init(&acc_empty[j], kTcEpi);
         }
         bar_init(done, 1);
         *abort = 0;
@@ -243,9 +247,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         if (lane == 0) {
             constexpr uint32_t idesc = tf32_idesc(BM);
             for (int i = 0; i < nk; ++i) {
-                const int s = i % S, j = i & 1;
+                const int s = i % S, g = i / kTcPromote, j = g & 1;
+                const bool first = i % kTcPromote == 0, last = i % kTcPromote == kTcPromote - 1 || i == nk - 1;
                 if (!bar_wait(&conv[s], static_cast<uint32_t>(i / S) & 1u, abort, a.error)) break;
-                if (i >= 2 && !bar_wait(&acc_empty[j], static_cast<uint32_t>(i / 2 - 1) & 1u, abort, a.error)) break;
+                if (first && g >= 2 &&
+                    !bar_wait(&acc_empty[j], static_cast<uint32_t>(g / 2 - 1) & 1u, abort, a.error))
+                    break;
                 fence_after_sync();
                 const uint64_t ah = sw128_desc(smem_addr(w_hi(s))), al = sw128_desc(smem_addr(w_lo(s)));
                 const uint64_t bh = sw128_desc(smem_addr(x_hi(s))), bl = sw128_desc(smem_addr(x_lo(s)));
@@ -255,10 +262,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     const uint64_t step = static_cast<uint64_t>(kk * 32 >> 4);  // 8 TF32 = 32 bytes
                     mma_tf32(tmem, ah + step, bl + step, idesc, (i | kk) != 0 ? 1u : 0u);
                     mma_tf32(tmem, al + step, bh + step, idesc, 1u);
-                    mma_tf32(main_acc, ah + step, bh + step, idesc, kk != 0 ? 1u : 0u);
+                    mma_tf32(main_acc, ah + step, bh + step, idesc, (!first || kk != 0) ? 1u : 0u);
                 }
                 mma_commit(&empty[s]);
-                mma_commit(&acc_full[j]);
+                if (last) mma_commit(&acc_full[j]);
             }
             mma_commit(done);  // arrives once every MMA issued above has completed
         }
@@ -266,25 +273,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     } else {
         // The tensor core's accumulation truncates, so a long chain of MMAs
         // into one accumulator drifts by about one unit in the last place
-        // per step.  Each stage's hi.hi products start a fresh accumulator
-        // and are added here in FP32 with round-to-nearest; the cross terms
-        // (2^-11 of the result) stay in one accumulator.
-        const int t = threadIdx.x - 64;  // 0..127
+        // per step.  Every kTcPromote stages the hi.hi products start a
+        // fresh accumulator and are added here in FP32 with
+        // round-to-nearest; the cross terms (2^-11 of the result) stay in one
+        // accumulator.  Warps w and w + 4 share TMEM lane quarter w % 4 and
+        // take one half of the columns each.
+        constexpr int kHalf = BM / 2;
+        const int t = threadIdx.x - 64;  // 0..255
         const int quarter = warp & 3;
+        const int c0 = (warp - 2) / 4 * kHalf;
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-        float acc[BM];
+        const int groups = (nk + kTcPromote - 1) / kTcPromote;
+        float acc[kHalf];
 #pragma unroll
-        for (int c = 0; c < BM; ++c) acc[c] = 0.0f;
+        for (int c = 0; c < kHalf; ++c) acc[c] = 0.0f;
         bool ok = true;
-        auto promote = [&](int i) {
-            const int j = i & 1;
-            ok = ok && bar_wait(&acc_full[j], static_cast<uint32_t>(i / 2) & 1u, abort, a.error);
+        int promoted = 0;
+        auto promote = [&](int g) {
+            const int j = g & 1;
+            ok = ok && bar_wait(&acc_full[j], static_cast<uint32_t>(g / 2) & 1u, abort, a.error);
             __syncwarp();
             fence_after_sync();
 #pragma unroll
-            for (int col = 0; col < BM; col += 32) {
+            for (int col = 0; col < kHalf; col += 32) {
                 float v[32];
-                tmem_load32(tmem + lane_base + static_cast<uint32_t>((1 + j) * BM + col), v);
+                tmem_load32(tmem + lane_base + static_cast<uint32_t>((1 + j) * BM + c0 + col), v);
 #pragma unroll
                 for (int c = 0; c < 32; ++c) acc[col + c] += v[c];
             }
@@ -299,8 +312,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             }
             float4* xh = reinterpret_cast<float4*>(x_hi(s));
             float4* xl = reinterpret_cast<float4*>(x_lo(s));
-#pragma unroll 4
-            for (int q = t; q < BM * kTcTileK / 4; q += 128) {
+#pragma unroll
+            for (int q = t; q < BM * kTcTileK / 4; q += kTcEpi) {
                 const float4 v = xh[q];
                 float4 h, r;
                 h.x = tf32_rna(v.x);
@@ -316,9 +329,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             bar_arrive(&conv[s]);
-            if (i >= 1) promote(i - 1);
+            if (promoted < i / kTcPromote) promote(promoted++);
         }
-        if (ok && nk > 0) promote(nk - 1);
+        while (ok && promoted < groups) promote(promoted++);
         grid_dependency_wait();  // the residual and C belong to earlier kernels too
         ok = ok && bar_wait(done, 0, abort, a.error) && !*abort;
         __syncwarp();
@@ -326,10 +339,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         const int n = n0 + quarter * 32 + lane;
         float* c = a.c + static_cast<long long>(blockIdx.z) * a.split_stride;
 #pragma unroll
-        for (int col = 0; col < BM; col += 32) {
+        for (int col = 0; col < kHalf; col += 32) {
             float v[32];
             if (nk > 0) {
-                tmem_load32(tmem + lane_base + static_cast<uint32_t>(col), v);
+                tmem_load32(tmem + lane_base + static_cast<uint32_t>(c0 + col), v);
             } else {
 #pragma unroll
                 for (int q = 0; q < 32; ++q) v[q] = 0.0f;
@@ -337,7 +350,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             if (ok && n < a.n) {
 #pragma unroll
                 for (int q = 0; q < 32; ++q) {
-                    const int m = m0 + col + q;
+                    const int m = m0 + c0 + col + q;
                     if (m < a.m) {
                         const long long at = static_cast<long long>(m) * a.ldc + n;
                         const float r = acc[col + q] + v[q];
