@@ -37,30 +37,30 @@ constexpr int64_t kMaxCapacity = 131072;
 
 // ------------------------------------------------------------- kernels
 
-// h[b] = embedding[tokens[b]] (zeros for an out-of-range token).
-__global__ void embed_rows_kernel(const int64_t* __restrict__ tokens, const float* __restrict__ embedding,
-                                  int64_t vocab, float* __restrict__ h) {
-    grid_dependency_wait();
-
-    const int b = blockIdx.x;
-    const int64_t t = tokens[b];
-    const bool valid = t >= 0 && t < vocab;
-    for (int i = threadIdx.x; i < kHidden; i += blockDim.x) h[b * kHidden + i] = valid ? embedding[t * kHidden + i] : 0.0f;
+// Row b of the residual stream (one CTA of 576 threads, one element each)
+// is written to h and its RMSNorm n = h * rsqrt(mean(h^2) + eps) * w to
+// norm_out.
+__device__ __forceinline__ void store_row_and_norm(int b, int i, float v, float* __restrict__ h,
+                                                   const float* __restrict__ w, float eps, float* __restrict__ norm_out) {
+    __shared__ float scratch[32];
+    h[static_cast<size_t>(b) * kHidden + i] = v;
+    const float ss = block_sum(v * v, scratch);
+    const float inv = rsqrtf(ss / static_cast<float>(kHidden) + eps);
+    norm_out[static_cast<size_t>(b) * kHidden + i] = v * inv * w[i];
 }
 
-// out[b] = x[b] * rsqrt(mean(x[b]^2) + eps) * w; one CTA per row.
-__global__ void __launch_bounds__(192) norm_rows_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                        float* __restrict__ out, float eps) {
+// h[b] = embedding[tokens[b]] (zeros for an out-of-range token) and the
+// first layer's input norm of it.
+__global__ void __launch_bounds__(kHidden) embed_rows_kernel(const int64_t* __restrict__ tokens,
+                                                             const float* __restrict__ embedding, int64_t vocab,
+                                                             float* __restrict__ h, const float* __restrict__ w,
+                                                             float eps, float* __restrict__ norm_out) {
     grid_dependency_wait();
 
-    __shared__ float scratch[32];
-    const int b = blockIdx.x;
-    const float* row = x + static_cast<size_t>(b) * kHidden;
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < kHidden; i += blockDim.x) ss = fmaf(row[i], row[i], ss);
-    ss = block_sum(ss, scratch);
-    const float inv = rsqrtf(ss / static_cast<float>(kHidden) + eps);
-    for (int i = threadIdx.x; i < kHidden; i += blockDim.x) out[static_cast<size_t>(b) * kHidden + i] = row[i] * inv * w[i];
+    const int b = blockIdx.x, i = threadIdx.x;
+    const int64_t t = tokens[b];
+    const bool valid = t >= 0 && t < vocab;
+    store_row_and_norm(b, i, valid ? embedding[t * kHidden + i] : 0.0f, h, w, eps, norm_out);
 }
 
 // P[split][m][n] = sum over k in the split's slice of X[m][k] * W[n][k]
@@ -173,6 +173,22 @@ __global__ void reduce_splits_kernel(const float* __restrict__ P, int splits, in
     out[i] = residual != nullptr ? residual[i] + v : v;
 }
 
+// h_out[m] = residual[m] + sum_s P[s][m] (the o_proj / down split-K sum
+// onto the residual stream) and the following RMSNorm of it; one CTA of
+// 576 threads per row.
+__global__ void __launch_bounds__(kHidden) reduce_residual_norm_kernel(const float* __restrict__ P, int splits, int M,
+                                                                       const float* __restrict__ residual,
+                                                                       float* __restrict__ h_out,
+                                                                       const float* __restrict__ w, float eps,
+                                                                       float* __restrict__ norm_out) {
+    grid_dependency_wait();
+
+    const int b = blockIdx.x, i = threadIdx.x;
+    const size_t e = static_cast<size_t>(b) * kHidden + i;
+    const float v = residual[e] + split_sum(P, splits, static_cast<size_t>(M) * kHidden, e);
+    store_row_and_norm(b, i, v, h_out, w, eps, norm_out);
+}
+
 // out[m][i] = swiglu(sum_s P[s][m][i], sum_s P[s][m][I + i]) for the packed gate|up columns.
 __global__ void reduce_swiglu_kernel(const float* __restrict__ P, int splits, int M, float* __restrict__ out) {
     grid_dependency_wait();
@@ -186,10 +202,12 @@ __global__ void reduce_swiglu_kernel(const float* __restrict__ P, int splits, in
     out[e] = swiglu(g, u);
 }
 
-// RoPE on q/k of every sequence at its own position, K/V rows written into
-// the layer's cache [B][3][cap][64], q -> [B][9][64], lengths[b] = pos + 1.
-// One thread per (sequence, pair): q/k pairs (d, d + 32), v single values.
-__global__ void rope_cache_rows_kernel(const float* __restrict__ qkv, const int64_t* __restrict__ positions,
+// The packed QKV projection's split-K sum, then RoPE on q/k of every
+// sequence at its own position, K/V rows written into the layer's cache
+// [B][3][cap][64], q -> [B][9][64], lengths[b] = pos + 1.  `qkv` holds
+// `splits` partials [s][B][960] (one split: the projection itself).  One
+// thread per (sequence, pair): q/k pairs (d, d + 32), v single values.
+__global__ void rope_cache_rows_kernel(const float* __restrict__ qkv, int splits, const int64_t* __restrict__ positions,
                                        const float* __restrict__ cos_table, const float* __restrict__ sin_table,
                                        float* __restrict__ kc, float* __restrict__ vc, float* __restrict__ q,
                                        int64_t* __restrict__ lengths, int64_t cap, int B, unsigned* __restrict__ error) {
@@ -205,10 +223,11 @@ __global__ void rope_cache_rows_kernel(const float* __restrict__ qkv, const int6
         return;
     }
     if (t == 0) lengths[b] = pos + 1;
-    const float* row = qkv + static_cast<size_t>(b) * kQKV;
+    const size_t stride = static_cast<size_t>(B) * kQKV;
+    auto value = [&](int n) { return split_sum(qkv, splits, stride, static_cast<size_t>(b) * kQKV + n); };
     if (t < (kQHeads + kKVHeads) * (kHeadDim / 2)) {
         const int head = t / (kHeadDim / 2), d = t % (kHeadDim / 2);  // heads 0..8 q, 9..11 k
-        const float x1 = row[head * kHeadDim + d], x2 = row[head * kHeadDim + d + kHeadDim / 2];
+        const float x1 = value(head * kHeadDim + d), x2 = value(head * kHeadDim + d + kHeadDim / 2);
         const float* c = cos_table + pos * kHeadDim;
         const float* s = sin_table + pos * kHeadDim;
         const float r1 = rope_value(x1, x2, c[d], s[d], true);
@@ -224,7 +243,7 @@ __global__ void rope_cache_rows_kernel(const float* __restrict__ qkv, const int6
     } else {
         const int u = t - (kQHeads + kKVHeads) * (kHeadDim / 2);
         vc[((static_cast<size_t>(b) * kKVHeads + u / kHeadDim) * cap + pos) * kHeadDim + u % kHeadDim] =
-            row[kHidden + kKVHeads * kHeadDim + u];
+            value(kHidden + kKVHeads * kHeadDim + u);
     }
 }
 
@@ -372,21 +391,25 @@ fx_status run_step(fx_batch* r, cudaStream_t s) {
     const fx_model_desc& m = r->model;
     const int B = static_cast<int>(r->batch);
     fx_status st;
-    if ((st = launch_dependent(embed_rows_kernel, dim3(B), dim3(192), 0, s, "launching the embedding gather",
-                               static_cast<const int64_t*>(r->tokens), m.embedding, r->vocab, r->h)) != FX_OK)
+    if ((st = launch_dependent(embed_rows_kernel, dim3(B), dim3(kHidden), 0, s, "launching the embedding gather",
+                               static_cast<const int64_t*>(r->tokens), m.embedding, r->vocab, r->h, m.input_norm[0],
+                               m.epsilon, r->norm)) != FX_OK)
         return st;
+    auto residual_norm = [&](const GemmPlan& p, const float* residual, float* h_out, const float* w) {
+        return launch_dependent(reduce_residual_norm_kernel, dim3(B), dim3(kHidden), 0, s,
+                                "launching the split-K sum / residual / RMSNorm rows",
+                                static_cast<const float*>(r->partials), p.splits, B, residual, h_out, w, m.epsilon,
+                                r->norm);
+    };
     for (int l = 0; l < kLayers; ++l) {
         float* kc = r->key_cache + l * r->layer_stride();
         float* vc = r->value_cache + l * r->layer_stride();
-        if ((st = launch_dependent(norm_rows_kernel, dim3(B), dim3(192), 0, s, "launching RMSNorm rows",
-                                   static_cast<const float*>(r->h), m.input_norm[l], r->norm, m.epsilon)) != FX_OK)
-            return st;
         if ((st = gemm(r, r->norm, m.packed_qkv[l], kQKV, kHidden, r->qkv_plan, r->qkv, s, &r->tc.qkv[l], &r->x_norm)) != FX_OK) return st;
-        if (r->qkv_plan.splits > 1 && (st = reduce(r, r->qkv_plan, kQKV, nullptr, r->qkv, s)) != FX_OK) return st;
         {
             const int64_t n = static_cast<int64_t>(B) * ((kQHeads + kKVHeads) * (kHeadDim / 2) + kKVHeads * kHeadDim);
+            const float* src = r->qkv_plan.splits > 1 ? r->partials : r->qkv;
             if ((st = launch_dependent(rope_cache_rows_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s,
-                                       "launching the batched RoPE / cache write", static_cast<const float*>(r->qkv),
+                                       "launching the batched QKV sum / RoPE / cache write", src, r->qkv_plan.splits,
                                        static_cast<const int64_t*>(r->positions), m.rope_cos, m.rope_sin, kc, vc, r->q,
                                        r->lengths, r->capacity, B, r->error)) != FX_OK)
                 return st;
@@ -407,10 +430,7 @@ fx_status run_step(fx_batch* r, cudaStream_t s) {
         a.chunk_rows = kCompactChunk;
         if ((st = launch_compact_attention(a, s, true)) != FX_OK) return st;
         if ((st = gemm(r, r->attn, m.o_proj[l], kHidden, kHidden, r->o_plan, nullptr, s, &r->tc.o[l], &r->x_attn)) != FX_OK) return st;
-        if ((st = reduce(r, r->o_plan, kHidden, r->h, r->h2, s)) != FX_OK) return st;
-        if ((st = launch_dependent(norm_rows_kernel, dim3(B), dim3(192), 0, s, "launching RMSNorm rows",
-                                   static_cast<const float*>(r->h2), m.post_norm[l], r->norm, m.epsilon)) != FX_OK)
-            return st;
+        if ((st = residual_norm(r->o_plan, r->h, r->h2, m.post_norm[l])) != FX_OK) return st;
         if ((st = gemm(r, r->norm, m.gate_up[l], kGateUp, kHidden, r->gu_plan, nullptr, s, &r->tc.gate_up[l], &r->x_norm)) != FX_OK) return st;
         {
             const int64_t n = static_cast<int64_t>(B) * kInter;
@@ -420,11 +440,11 @@ fx_status run_step(fx_batch* r, cudaStream_t s) {
                 return st;
         }
         if ((st = gemm(r, r->act, m.down[l], kHidden, kInter, r->down_plan, nullptr, s, &r->tc.down[l], &r->x_act)) != FX_OK) return st;
-        if ((st = reduce(r, r->down_plan, kHidden, r->h2, r->h, s)) != FX_OK) return st;
+        // h = h' + down, then the next layer's input norm (the final norm after the last layer)
+        if ((st = residual_norm(r->down_plan, r->h2, r->h, l + 1 < kLayers ? m.input_norm[l + 1] : m.final_norm)) !=
+            FX_OK)
+            return st;
     }
-    if ((st = launch_dependent(norm_rows_kernel, dim3(B), dim3(192), 0, s, "launching the final RMSNorm",
-                               static_cast<const float*>(r->h), m.final_norm, r->norm, m.epsilon)) != FX_OK)
-        return st;
     if ((st = gemm(r, r->norm, m.lm_head, static_cast<int>(r->vocab), kHidden, r->lm_plan, r->logits, s, &r->tc.lm_head,
                     &r->x_norm)) != FX_OK)
         return st;
@@ -688,7 +708,7 @@ extern "C" fx_status fx_batch_get_buffers(const fx_batch* r, fx_batch_buffers* o
     out->batch = r->batch;
     out->capacity = r->capacity;
     out->generated_capacity = r->gen_cap;
-    out->kernels_per_step = 1 + kLayers * (12 + (r->qkv_plan.splits > 1 ? 1 : 0)) + 4 + (r->lm_plan.splits > 1 ? 1 : 0);
+    out->kernels_per_step = 1 + kLayers * 10 + 3 + (r->lm_plan.splits > 1 ? 1 : 0);
     return FX_OK;
 }
 
