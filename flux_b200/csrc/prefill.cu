@@ -11,9 +11,12 @@
 // split once at create); the attention is a flash-style FP32 SIMT kernel.
 // The SIMT GEMM below serves the generic fx_linear_f32 op.
 #include "common.cuh"
+#include "tc_attention.cuh"
 #include "tc_gemm.cuh"
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <cmath>
 #include <new>
 #include <string>
@@ -137,12 +140,33 @@ __global__ void embedding_gather_kernel(const int64_t* __restrict__ ids, const f
     }
 }
 
+__device__ __forceinline__ float tf32_round(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+// The TF32 hi / lo halves of v at index i of the split planes.
+__device__ __forceinline__ void store_split(float* __restrict__ hi, float* __restrict__ lo, size_t i, float v) {
+    const float h = tf32_round(v);
+    hi[i] = h;
+    lo[i] = tf32_round(v - h);
+}
+
 // Rows [0, S) of packed QKV -> q [9, S, 64] (RoPE), K (RoPE) / V into the
-// cache rows [0, S) (native_prefill_runtime_cuda.cu:124-163).
+// cache rows [0, S) (native_prefill_runtime_cuda.cu:124-163).  With
+// `split` set, also the tensor-core attention's operands: q and K as TF32
+// hi / lo planes ([9][S][64], [3][padded][64]) and V transposed per kv head
+// ([3][64][padded]).
+struct PrefillSplit {
+    float *q_hi, *q_lo, *k_hi, *k_lo, *vt_hi, *vt_lo;
+    int64_t padded;
+};
+
 __global__ void prefill_rope_cache_kernel(const float* __restrict__ packed, const float* __restrict__ cos,
                                           const float* __restrict__ sin, float* __restrict__ q,
                                           float* __restrict__ key_cache, float* __restrict__ value_cache,
-                                          int64_t rows, int64_t capacity) {
+                                          int64_t rows, int64_t capacity, PrefillSplit split) {
     const int64_t total = rows * kQKV;
     for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
          t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -155,14 +179,20 @@ __global__ void prefill_rope_cache_kernel(const float* __restrict__ packed, cons
             const float v = rope_value(prow[base + d], prow[base + partner], cos[r * kHeadDim + d],
                                        sin[r * kHeadDim + d], d < kHeadDim / 2);
             if (col < kHidden) {
-                q[(static_cast<int64_t>(col / kHeadDim) * rows + r) * kHeadDim + d] = v;
+                const size_t at = (static_cast<int64_t>(col / kHeadDim) * rows + r) * kHeadDim + d;
+                q[at] = v;
+                if (split.q_hi != nullptr) store_split(split.q_hi, split.q_lo, at, v);
             } else {
                 const int h = (col - kHidden) / kHeadDim;
                 key_cache[(static_cast<int64_t>(h) * capacity + r) * kHeadDim + d] = v;
+                if (split.k_hi != nullptr)
+                    store_split(split.k_hi, split.k_lo, (static_cast<int64_t>(h) * split.padded + r) * kHeadDim + d, v);
             }
         } else {
             const int u = col - kHidden - kKVHeads * kHeadDim;
             value_cache[(static_cast<int64_t>(u / kHeadDim) * capacity + r) * kHeadDim + u % kHeadDim] = prow[col];
+            if (split.vt_hi != nullptr)
+                store_split(split.vt_hi, split.vt_lo, static_cast<size_t>(u) * split.padded + r, prow[col]);
         }
     }
 }
@@ -346,6 +376,11 @@ struct fx_prefill {
     fx::TcModelWeights tc;                  // split projection weights
     CUtensorMap x_norm, x_attn, x_swiglu;   // activation maps of the projections
     int bm = 128;                           // activation rows per tensor-core tile
+    // Tensor-core attention (unless FLUX_B200_PREFILL_ATTENTION=simt): split
+    // q / K / V^T planes and their maps.
+    bool tc_attention = true;
+    float* split_buffer = nullptr;
+    fx::TcAttentionArgs attn_args{};
 };
 
 namespace fx {
@@ -368,6 +403,7 @@ fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
     const int64_t S = p->rows;
     const int64_t cap = m.capacity;
     int* error = decode_error_word(p->decode);
+    p->attn_args.error = error;
     auto project = [&](const TcWeight& w, const CUtensorMap& x, float* c, const float* residual) {
         return launch_tc_gemm(tc_args(w, x, c, residual, error, static_cast<int>(S), w.cols), p->bm, 1, s, false);
     };
@@ -381,12 +417,26 @@ fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
         float* vc = db.value_cache + l * layer_stride;
         if ((st = fx_rmsnorm_f32(in, m.input_norm[l], p->norm, S, kHidden, m.epsilon, s)) != FX_OK) return st;
         if ((st = project(p->tc.qkv[l], p->x_norm, p->qkv, nullptr)) != FX_OK) return st;
+        PrefillSplit split{};
+        if (p->tc_attention) {
+            const int64_t P = tc_attention_padded(S);
+            float* b = p->split_buffer;
+            split = {b, b + S * kHidden, b + 2 * S * kHidden, b + 2 * S * kHidden + kKVHeads * P * kHeadDim,
+                     b + 2 * S * kHidden + 2 * kKVHeads * P * kHeadDim,
+                     b + 2 * S * kHidden + 3 * kKVHeads * P * kHeadDim, P};
+        }
         prefill_rope_cache_kernel<<<blocks_for(S * kQKV), 256, 0, s>>>(p->qkv, m.rope_cos, m.rope_sin, p->q, kc, vc,
-                                                                       S, cap);
+                                                                       S, cap, split);
         FX_CUDA_TRY(cudaGetLastError(), "launching prefill RoPE/cache fill");
-        prefill_flash_kernel<<<dim3(static_cast<unsigned>((S + kFlash - 1) / kFlash), kQHeads), kFlashThreads,
-                               kFlashSmem, s>>>(p->q, kc, vc, p->attn, S, cap, m.attention_scale[l]);
-        FX_CUDA_TRY(cudaGetLastError(), "launching prefill attention");
+        if (p->tc_attention) {
+            TcAttentionArgs args = p->attn_args;
+            args.scale = m.attention_scale[l];
+            if ((st = launch_tc_prefill_attention(args, s)) != FX_OK) return st;
+        } else {
+            prefill_flash_kernel<<<dim3(static_cast<unsigned>((S + kFlash - 1) / kFlash), kQHeads), kFlashThreads,
+                                   kFlashSmem, s>>>(p->q, kc, vc, p->attn, S, cap, m.attention_scale[l]);
+            FX_CUDA_TRY(cudaGetLastError(), "launching prefill attention");
+        }
         // residual = attn . Wo^T + in; norm = rmsnorm(residual)
         if ((st = project(p->tc.o[l], p->x_attn, p->residual, in)) != FX_OK) return st;
         if ((st = fx_rmsnorm_f32(p->residual, m.post_norm[l], p->norm, S, kHidden, m.epsilon, s)) != FX_OK) return st;
@@ -408,6 +458,7 @@ void prefill_release(fx_prefill* p) {
     cudaSetDevice(p->model.device);
     if (p->decode != nullptr) fx_decode_destroy(p->decode);  // waits for pending work
     tc_weights_release(&p->tc);
+    cudaFree(p->split_buffer);
     cudaFree(p->buffer);
     cudaFree(p->logits);
     cudaFree(p->initial_token);
@@ -442,6 +493,32 @@ fx_status prefill_create_impl(fx_prefill* p, const int64_t* ids, cudaStream_t s)
     FX_CUDA_TRY(cudaMemsetAsync(p->buffer, 0, p->buffer_bytes, s), "clearing the prefill workspace");
     fx_status st0 = tc_weights_create(p->model, false, &p->tc, s);
     if (st0 != FX_OK) return st0;
+    const char* attention_mode = std::getenv("FLUX_B200_PREFILL_ATTENTION");
+    p->tc_attention = !(attention_mode != nullptr && std::strcmp(attention_mode, "simt") == 0);
+    if (p->tc_attention) {
+        const int64_t P = tc_attention_padded(S);
+        const size_t floats = 2 * static_cast<size_t>(S) * kHidden + 4 * static_cast<size_t>(kKVHeads) * P * kHeadDim;
+        FX_CUDA_TRY(cudaMalloc(&p->split_buffer, floats * sizeof(float)), "allocating the split attention operands");
+        FX_CUDA_TRY(cudaMemsetAsync(p->split_buffer, 0, floats * sizeof(float), s), "clearing the split operands");
+        float* b = p->split_buffer;
+        TcAttentionArgs& a = p->attn_args;
+        float* k_hi = b + 2 * S * kHidden;
+        float* k_lo = k_hi + kKVHeads * P * kHeadDim;
+        float* vt_hi = k_lo + kKVHeads * P * kHeadDim;
+        float* vt_lo = vt_hi + kKVHeads * P * kHeadDim;
+        if ((st0 = tc_encode_map(&a.q_hi, b, kQHeads * S, kHeadDim, kTcAttnQ, "the split queries")) != FX_OK ||
+            (st0 = tc_encode_map(&a.q_lo, b + S * kHidden, kQHeads * S, kHeadDim, kTcAttnQ, "the split queries")) !=
+                FX_OK ||
+            (st0 = tc_encode_map(&a.k_hi, k_hi, kKVHeads * P, kHeadDim, kTcAttnKeys, "the split keys")) != FX_OK ||
+            (st0 = tc_encode_map(&a.k_lo, k_lo, kKVHeads * P, kHeadDim, kTcAttnKeys, "the split keys")) != FX_OK ||
+            (st0 = tc_encode_map(&a.vt_hi, vt_hi, kKVHeads * kHeadDim, P, kTcAttnKeys, "the split values")) != FX_OK ||
+            (st0 = tc_encode_map(&a.vt_lo, vt_lo, kKVHeads * kHeadDim, P, kTcAttnKeys, "the split values")) != FX_OK)
+            return st0;
+        a.out = p->attn;
+        a.error = nullptr;  // set at run time (the decode runtime's error word)
+        a.rows = static_cast<int>(S);
+        a.padded = static_cast<int>(P);
+    }
     if ((st0 = tc_encode_map(&p->x_norm, p->norm, R, kHidden, p->bm, "the prefill norm rows")) != FX_OK) return st0;
     if ((st0 = tc_encode_map(&p->x_attn, p->attn, R, kHidden, p->bm, "the prefill attention rows")) != FX_OK) return st0;
     if ((st0 = tc_encode_map(&p->x_swiglu, p->swiglu_out, R, kInter, p->bm, "the prefill SwiGLU rows")) != FX_OK)
