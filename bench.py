@@ -64,9 +64,10 @@ def parse_args(argv=None):
     p.add_argument("--no-batched", action="store_true", help="skip the batched configuration")
     p.add_argument("--no-attention", action="store_true", help="skip the isolated-attention sweep")
     p.add_argument("--no-sweep", action="store_true", help="skip the context sweep of the batch-1 decode")
-    p.add_argument("--probe", choices=("batched", "tc-gemm"), default=None,
+    p.add_argument("--probe", choices=("batched", "tc-gemm", "prefill"), default=None,
                    help="run a small fixed workload for a profiler (no JSON line): two batched steps of 64 "
-                        "sequences, or three 8192 x 576 -> 3072 tensor-core projections")
+                        "sequences, three 8192 x 576 -> 3072 tensor-core projections, or one --context-token "
+                        "prefill")
     return p.parse_args(argv)
 
 
@@ -535,6 +536,18 @@ def run_probe(args) -> None:
                                                    m, k, n, err.data_ptr(), stream))
         torch.cuda.synchronize()
         assert int(err.item()) == 0
+    elif args.probe == "prefill":
+        from oracle.host import limit_threads
+        limit_threads()
+        from flux_b200.integration import FINAL_FLUX_OPERATOR_CATEGORIES, enable_flux_ops
+        from flux_b200.runtime import NativeSmolLM2Prefill
+        from tests.golden.inputs import uniform_prompt
+        _, cpu_model = build_models(args.context, 2, args.seed)
+        model = enable_flux_ops(copy.deepcopy(cpu_model).to(device), operators=FINAL_FLUX_OPERATOR_CATEGORIES)
+        with torch.inference_mode():
+            NativeSmolLM2Prefill.capture(model, uniform_prompt(args.context, seed=args.seed).to(device),
+                                         max_decode_steps=1)
+        torch.cuda.synchronize()
     else:
         from oracle.host import limit_threads
         limit_threads()

@@ -13,8 +13,9 @@
 //   warps 2-5 / 6-9  two softmax sets taking alternate key tiles (so one
 //                    set's softmax overlaps the other's MMAs).  Warp w reads
 //                    TMEM lanes 32 (w % 4) .., i.e. one query row per thread:
-//                    s = (S_a + S_b) * scale * log2(e), causal mask, running
-//                    max, p = 2^(s - m), row sum; p split into hi / lo written
+//                    t = S_a + S_b, causal mask on diagonal tiles, running
+//                    max m of t c (c = scale log2(e) > 0), p = 2^(t c - m),
+//                    row sum; p split into hi / lo written
 //                    back over S_a / S_b with tcgen05.st; after the P V MMAs
 //                    O_acc = O_acc * alpha + O_tile in FP32 through registers
 //                    (each tile's P V product starts a fresh accumulator: the
@@ -34,26 +35,38 @@ namespace {
 
 using namespace tc;
 
-constexpr int kAttnThreads = 320;
-constexpr int kKvStages = 2;
+constexpr int kAttnThreads = 352;  // K producer, MMA, 8 softmax warps, V producer
+constexpr int kKStages = 3;         // K is free once the scores are done ...
+constexpr int kVStages = 2;         // ... V^T only after P V
 constexpr uint32_t kQBox = kTcAttnQ * 128;              // 128 rows x 32 floats (16 KB)
 constexpr uint32_t kKBox = kTcAttnKeys * 128;           // 64 rows x 32 floats (8 KB)
 constexpr uint32_t kQBytes = 4 * kQBox;                 // hi b0, hi b1, lo b0, lo b1
-constexpr uint32_t kStageBytes = 8 * kKBox;             // K hi b0 b1, K lo b0 b1, V^T hi b0 b1, V^T lo b0 b1
-constexpr size_t kAttnSmem = kQBytes + kKvStages * kStageBytes + 1024 + 256;
+constexpr uint32_t kHalfStage = 4 * kKBox;              // K: hi b0 b1, lo b0 b1 / V^T: hi b0 b1, lo b0 b1
+constexpr uint32_t kRingBytes = (kKStages + kVStages) * kHalfStage;
+constexpr size_t kAttnSmem = kQBytes + kRingBytes + 1024 + 256;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x on the SFU (ex2.approx.ftz: relative error ~2^-22; 2^-inf = 0).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(const __grid_constant__ TcAttentionArgs a) {
     extern __shared__ unsigned char attn_raw[];
     unsigned char* smem = attn_raw + ((1024u - (smem_addr(attn_raw) & 1023u)) & 1023u);
     unsigned char* qs = smem;
-    auto stage = [&](int s) { return smem + kQBytes + s * kStageBytes; };
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kQBytes + kKvStages * kStageBytes);
+    auto kstage = [&](int s) { return smem + kQBytes + s * kHalfStage; };
+    auto vstage = [&](int s) { return smem + kQBytes + (kKStages + s) * kHalfStage; };
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kQBytes + kRingBytes);
     uint64_t* q_full = bars;
-    uint64_t* kv_full = bars + 1;
-    uint64_t* kv_empty = kv_full + kKvStages;
-    uint64_t* s_full = kv_empty + kKvStages;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = k_full + kKStages;
+    uint64_t* v_full = k_empty + kKStages;
+    uint64_t* v_empty = v_full + kVStages;
+    uint64_t* s_full = v_empty + kVStages;
     uint64_t* p_full = s_full + 2;
     uint64_t* o_full = p_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
@@ -69,9 +82,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
 
     if (threadIdx.x == 0) {
         bar_init(q_full, 1);
-        for (int s = 0; s < kKvStages; ++s) {
-            bar_init(&kv_full[s], 1);
-            bar_init(&kv_empty[s], 1);
+        for (int s = 0; s < kKStages; ++s) {
+            bar_init(&k_full[s], 1);
+            bar_init(&k_empty[s], 1);
+        }
+        for (int s = 0; s < kVStages; ++s) {
+            bar_init(&v_full[s], 1);
+            bar_init(&v_empty[s], 1);
         }
         for (int x = 0; x < 2; ++x) {
             bar_init(&s_full[x], 1);
@@ -87,6 +104,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
     fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
+    // One producer lane per ring: warp 0 loads Q and the K tiles, warp 9 the
+    // V^T tiles.
+    auto produce = [&](int stages, uint64_t* full, uint64_t* empty, auto&& load) {
+        int issued = 0;
+        for (int t = 0; t < nt; ++t) {
+            const int s = t % stages;
+            if (t >= stages && !bar_wait(&empty[s], static_cast<uint32_t>(t / stages - 1) & 1u, abort, a.error))
+                break;
+            bar_expect(&full[s], kHalfStage);
+            load(t, s, &full[s]);
+            issued = t + 1;
+        }
+        // Copies in flight land before the CTA leaves (a no-op unless a
+        // consumer gave up early).
+        for (int t = max(0, issued - stages); t < issued; ++t) {
+            const unsigned long long t0 = now_ns();
+            while (!bar_test(&full[t % stages], static_cast<uint32_t>(t / stages) & 1u))
+                if (now_ns() - t0 > kTcWaitNs) break;
+        }
+    };
     if (warp == 0) {
         if (lane == 0) {
             bar_expect(q_full, kQBytes);
@@ -95,36 +132,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
             tma_box(qs + 1 * kQBox, &a.q_hi, 32, qy, q_full);
             tma_box(qs + 2 * kQBox, &a.q_lo, 0, qy, q_full);
             tma_box(qs + 3 * kQBox, &a.q_lo, 32, qy, q_full);
-            int issued = 0;
-            for (int t = 0; t < nt; ++t) {
-                const int s = t % kKvStages;
-                if (t >= kKvStages &&
-                    !bar_wait(&kv_empty[s], static_cast<uint32_t>(t / kKvStages - 1) & 1u, abort, a.error))
-                    break;
-                unsigned char* st = stage(s);
+            produce(kKStages, k_full, k_empty, [&](int t, int s, uint64_t* bar) {
+                unsigned char* st = kstage(s);
                 const int ky = g * a.padded + t * kTcAttnKeys;
-                const int vx = t * kTcAttnKeys;
-                bar_expect(&kv_full[s], kStageBytes);
-                tma_box(st + 0 * kKBox, &a.k_hi, 0, ky, &kv_full[s]);
-                tma_box(st + 1 * kKBox, &a.k_hi, 32, ky, &kv_full[s]);
-                tma_box(st + 2 * kKBox, &a.k_lo, 0, ky, &kv_full[s]);
-                tma_box(st + 3 * kKBox, &a.k_lo, 32, ky, &kv_full[s]);
-                tma_box(st + 4 * kKBox, &a.vt_hi, vx, g * kHeadDim, &kv_full[s]);
-                tma_box(st + 5 * kKBox, &a.vt_hi, vx + 32, g * kHeadDim, &kv_full[s]);
-                tma_box(st + 6 * kKBox, &a.vt_lo, vx, g * kHeadDim, &kv_full[s]);
-                tma_box(st + 7 * kKBox, &a.vt_lo, vx + 32, g * kHeadDim, &kv_full[s]);
-                issued = t + 1;
-            }
-            // Copies in flight land before the CTA leaves (a no-op unless a
-            // consumer gave up early).
-            for (int t = max(0, issued - kKvStages); t < issued; ++t) {
-                const unsigned long long t0 = now_ns();
-                while (!bar_test(&kv_full[t % kKvStages], static_cast<uint32_t>(t / kKvStages) & 1u))
-                    if (now_ns() - t0 > kTcWaitNs) break;
-            }
+                tma_box(st + 0 * kKBox, &a.k_hi, 0, ky, bar);
+                tma_box(st + 1 * kKBox, &a.k_hi, 32, ky, bar);
+                tma_box(st + 2 * kKBox, &a.k_lo, 0, ky, bar);
+                tma_box(st + 3 * kKBox, &a.k_lo, 32, ky, bar);
+            });
             const unsigned long long t0 = now_ns();
             while (!bar_test(q_full, 0))
                 if (now_ns() - t0 > kTcWaitNs) break;
+        }
+    } else if (warp == kAttnThreads / 32 - 1) {
+        if (lane == 0) {
+            produce(kVStages, v_full, v_empty, [&](int t, int s, uint64_t* bar) {
+                unsigned char* st = vstage(s);
+                const int vx = t * kTcAttnKeys;
+                tma_box(st + 0 * kKBox, &a.vt_hi, vx, g * kHeadDim, bar);
+                tma_box(st + 1 * kKBox, &a.vt_hi, vx + 32, g * kHeadDim, bar);
+                tma_box(st + 2 * kKBox, &a.vt_lo, vx, g * kHeadDim, bar);
+                tma_box(st + 3 * kKBox, &a.vt_lo, vx + 32, g * kHeadDim, bar);
+            });
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -133,12 +162,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
             const uint64_t qh0 = sw128_desc(smem_addr(qs)), qh1 = sw128_desc(smem_addr(qs + kQBox));
             const uint64_t ql0 = sw128_desc(smem_addr(qs + 2 * kQBox)), ql1 = sw128_desc(smem_addr(qs + 3 * kQBox));
             auto issue_scores = [&](int t) -> bool {
-                const int s = t % kKvStages, x = t & 1, u = t >> 1;
-                if (!bar_wait(&kv_full[s], static_cast<uint32_t>(t / kKvStages) & 1u, abort, a.error)) return false;
+                const int s = t % kKStages, x = t & 1, u = t >> 1;
+                if (!bar_wait(&k_full[s], static_cast<uint32_t>(t / kKStages) & 1u, abort, a.error)) return false;
                 // S_x / P_x of tile t - 2 are free once its P V products are done.
                 if (u >= 1 && !bar_wait(&o_full[x], static_cast<uint32_t>(u - 1) & 1u, abort, a.error)) return false;
                 fence_after_sync();
-                unsigned char* st = stage(s);
+                unsigned char* st = kstage(s);
 #pragma unroll
                 for (int b = 0; b < 2; ++b) {
                     const uint32_t d = tmem + static_cast<uint32_t>(x * 256 + b * 64);
@@ -154,30 +183,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
                     }
                 }
                 mma_commit(&s_full[x]);
+                mma_commit(&k_empty[s]);
                 return true;
             };
             ok = ok && nt > 0 && issue_scores(0);
             for (int t = 0; ok && t < nt; ++t) {
                 if (t + 1 < nt && !issue_scores(t + 1)) break;
-                const int s = t % kKvStages, x = t & 1, u = t >> 1;
+                const int s = t % kVStages, x = t & 1, u = t >> 1;
+                if (!bar_wait(&v_full[s], static_cast<uint32_t>(t / kVStages) & 1u, abort, a.error)) break;
                 if (!bar_wait(&p_full[x], static_cast<uint32_t>(u) & 1u, abort, a.error)) break;
                 fence_after_sync();
-                unsigned char* st = stage(s);
+                unsigned char* st = vstage(s);
                 const uint32_t o = tmem + static_cast<uint32_t>(x * 256 + 128);
                 const uint32_t ph = tmem + static_cast<uint32_t>(x * 256), pl = ph + 64;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const int vb = kk / 4;
                     const uint64_t step = static_cast<uint64_t>((kk % 4) * 2);
-                    const uint64_t vh = sw128_desc(smem_addr(st + (4 + vb) * kKBox)) + step;
-                    const uint64_t vl = sw128_desc(smem_addr(st + (6 + vb) * kKBox)) + step;
+                    const uint64_t vh = sw128_desc(smem_addr(st + vb * kKBox)) + step;
+                    const uint64_t vl = sw128_desc(smem_addr(st + (2 + vb) * kKBox)) + step;
                     const uint32_t col = static_cast<uint32_t>(kk * 8);
                     mma_tf32_ts(o, ph + col, vl, idesc, kk != 0 ? 1u : 0u);
                     mma_tf32_ts(o, pl + col, vh, idesc, 1u);
                     mma_tf32_ts(o, ph + col, vh, idesc, 1u);
                 }
                 mma_commit(&o_full[x]);
-                mma_commit(&kv_empty[s]);
+                mma_commit(&v_empty[s]);
             }
         }
         __syncwarp();
@@ -196,43 +227,44 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
             ok = bar_wait(&s_full[set], static_cast<uint32_t>(u) & 1u, abort, a.error);
             __syncwarp();
             fence_after_sync();
-            // Two passes over the scores in TMEM (max, then p), 16 columns at a
-            // time, so few values are live in registers.
+            // Raw scores t = S_a + S_b (the scale c > 0 is applied inside the
+            // exponent: max(t) c is the max of the scaled scores).
             const int k0 = t * kTcAttnKeys;
-            auto scores = [&](int part, float (&sv)[16]) {
-                float va[16], vb[16];
-                tmem_load16(sa + static_cast<uint32_t>(part * 16), va);
-                tmem_load16(sa + static_cast<uint32_t>(64 + part * 16), vb);
+            float tv[kTcAttnKeys];
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    sv[j] = k0 + part * 16 + j > qpos ? -INFINITY : (va[j] + vb[j]) * c;
-            };
-            float mt = -INFINITY;
-#pragma unroll 1
-            for (int part = 0; part < 4; ++part) {
-                float sv[16];
-                scores(part, sv);
+            for (int half = 0; half < 2; ++half) {
+                float va[32], vb[32];
+                tmem_load32(sa + static_cast<uint32_t>(half * 32), va);
+                tmem_load32(sa + static_cast<uint32_t>(64 + half * 32), vb);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) mt = fmaxf(mt, sv[j]);
+                for (int j = 0; j < 32; ++j) tv[half * 32 + j] = va[j] + vb[j];
             }
-            const float m_new = fmaxf(m_run, mt);
+            if (k0 + kTcAttnKeys - 1 > q0) {  // a tile on the causal diagonal (block-uniform)
+#pragma unroll
+                for (int j = 0; j < kTcAttnKeys; ++j)
+                    if (k0 + j > qpos) tv[j] = -INFINITY;
+            }
+            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int j = 0; j < kTcAttnKeys; ++j) mx[j & 3] = fmaxf(mx[j & 3], tv[j]);
+            const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * c);
             const float mref = m_new == -INFINITY ? 0.0f : m_new;  // a row with no key yet
-            const float alpha = exp2f(m_run - mref);
-            float rs = 0.0f;
-#pragma unroll 1
-            for (int part = 0; part < 4; ++part) {
-                float sv[16], ph[16], pl[16];
-                scores(part, sv);
+            const float alpha = fast_exp2(m_run - mref);
+            float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const float p = exp2f(sv[j] - mref);
-                    rs += p;
-                    ph[j] = tf32_rna(p);
-                    pl[j] = tf32_rna(p - ph[j]);
+            for (int half = 0; half < 2; ++half) {
+                float ph[32], pl[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float p = fast_exp2(fmaf(tv[half * 32 + j], c, -mref));
+                    sum[j & 3] += p;
+                    ph[j] = tf32_round_int(p);
+                    pl[j] = tf32_round_int(p - ph[j]);
                 }
-                tmem_store16(sa + static_cast<uint32_t>(part * 16), ph);
-                tmem_store16(sa + static_cast<uint32_t>(64 + part * 16), pl);
+                tmem_store32(sa + static_cast<uint32_t>(half * 32), ph);
+                tmem_store32(sa + static_cast<uint32_t>(64 + half * 32), pl);
             }
+            const float rs = (sum[0] + sum[1]) + (sum[2] + sum[3]);
             tmem_store_wait();
             fence_before_sync();
             bar_arrive(&p_full[set]);
@@ -259,7 +291,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
         // Merge the two sets' rows: set 1 hands (m, l, O) to set 0 through the
         // (now idle) K / V stages.
         asm volatile("bar.sync 1, 256;" ::: "memory");  // every MMA has completed
-        float* scratch = reinterpret_cast<float*>(stage(0)) + row * (kHeadDim + 4);
+        float* scratch = reinterpret_cast<float*>(kstage(0)) + row * (kHeadDim + 4);
         if (set == 1) {
             scratch[0] = m_run;
             scratch[1] = l_run;
@@ -280,7 +312,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
         if (set == 0) {
             const float mb = scratch[0], lb = scratch[1];
             const float m = fmaxf(m_run, mb);
-            const float fa = exp2f(m_run - m), fb = mb == -INFINITY ? 0.0f : exp2f(mb - m);
+            const float fa = fast_exp2(m_run - m), fb = mb == -INFINITY ? 0.0f : fast_exp2(mb - m);
             const float inv = 1.0f / (l_run * fa + lb * fb);
             float4* dst = reinterpret_cast<float4*>(a.out + static_cast<size_t>(qpos) * kHidden + head * kHeadDim);
 #pragma unroll
@@ -320,6 +352,7 @@ fx_status launch_tc_prefill_attention(const TcAttentionArgs& args, cudaStream_t 
     FX_CUDA_TRY(status, "raising the tensor-core attention's shared memory");
     FX_REQUIRE(args.rows > 0 && args.padded >= args.rows && args.padded % kTcAttnKeys == 0,
                "tensor-core attention: bad row counts");
+    FX_REQUIRE(args.scale > 0.0f, "tensor-core attention: the attention scale must be positive");
     const dim3 grid(static_cast<unsigned>((args.rows + kTcAttnQ - 1) / kTcAttnQ), kQHeads);
     tc_prefill_attention_kernel<<<grid, kAttnThreads, kAttnSmem, stream>>>(args);
     FX_CUDA_TRY(cudaGetLastError(), "launching the tensor-core prefill attention");

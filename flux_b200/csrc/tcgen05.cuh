@@ -71,6 +71,14 @@ __device__ __forceinline__ void tma_box(void* dst, const CUtensorMap* map, int x
         : "memory");
 }
 
+// Round to TF32 (10-bit mantissa), nearest with ties away from zero, on
+// the integer ALUs: add half a TF32 unit to the magnitude bits and clear the
+// 13 low bits.  Equal to cvt.rna.tf32.f32 for finite x whose rounding does
+// not overflow; for values that are not NaN (probabilities, activations).
+__device__ __forceinline__ float tf32_round_int(float x) {
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+
 __device__ __forceinline__ float tf32_rna(float x) {
     uint32_t r;
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));

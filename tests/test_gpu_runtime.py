@@ -225,11 +225,12 @@ def test_replay_on_non_default_stream_and_memory(tiny_flux):
     assert memory.owned_tensor_bytes > memory.cache_bytes
 
 
-@pytest.mark.parametrize("prompt_length", [64, 65, 200, 777])
+@pytest.mark.parametrize("prompt_length", [1, 64, 65, 200, 777])
 def test_prefill_long_prompt_vs_oracle(smollm2_model, smollm2_flux, prompt_length):
-    """The native prefill (flash-style causal attention over 64-row key tiles,
-    partial last tile, causal diagonal) against the oracle: prefill logits,
-    every cache row, and the first decode step after it."""
+    """The native prefill (tensor-core causal attention over 128-query blocks
+    and 64-row key tiles: one row, partial last tile, causal diagonal)
+    against the oracle: prefill logits, every cache row, and the first decode
+    step after it."""
     from flux_b200.runtime import NativeSmolLM2Prefill
     ids = gi.uniform_prompt(prompt_length, seed=prompt_length).cuda()
     with torch.inference_mode():
@@ -246,3 +247,23 @@ def test_prefill_long_prompt_vs_oracle(smollm2_model, smollm2_flux, prompt_lengt
     token = int(np.argmax(expected))
     logits = native.replay(torch.tensor([[token]], device="cuda"))
     np.testing.assert_allclose(np32(logits), oracle.step(token), rtol=LOGIT_TOL, atol=LOGIT_TOL)
+
+
+def test_prefill_tensor_core_attention_matches_simt(smollm2_flux, monkeypatch):
+    """A 2500-token prompt (neither a multiple of the 128-query blocks nor of
+    the 64-key tiles) through the tcgen05 3xTF32 attention and through the
+    FP32 SIMT flash kernel (FLUX_B200_PREFILL_ATTENTION=simt): prefill logits
+    and every layer's cache rows agree to FP32 rounding."""
+    from flux_b200.runtime import NativeSmolLM2Prefill
+    ids = gi.uniform_prompt(2500, seed=25).cuda()
+    with torch.inference_mode():
+        tc = NativeSmolLM2Prefill.capture(smollm2_flux, ids, max_decode_steps=1)
+        tc_logits, tc_keys = tc.logits.clone(), tc.key_cache[:, 0, :, :2500].clone()
+        tc_values = tc.value_cache[:, 0, :, :2500].clone()
+        del tc
+        monkeypatch.setenv("FLUX_B200_PREFILL_ATTENTION", "simt")
+        simt = NativeSmolLM2Prefill.capture(smollm2_flux, ids, max_decode_steps=1)
+    torch.testing.assert_close(tc_logits, simt.logits, rtol=LOGIT_TOL, atol=LOGIT_TOL)
+    torch.testing.assert_close(tc_keys, simt.key_cache[:, 0, :, :2500], rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(tc_values, simt.value_cache[:, 0, :, :2500], rtol=1e-4, atol=1e-5)
+
