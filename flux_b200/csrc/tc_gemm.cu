@@ -196,16 +196,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             float4* xl = reinterpret_cast<float4*>(x_lo(s));
 #pragma unroll
             for (int q = t; q < BM * kTcTileK / 4; q += kTcEpi) {
+                // integer-ALU rounding (the conversion pipe is quarter rate)
                 const float4 v = xh[q];
                 float4 h, r;
-                h.x = tf32_rna(v.x);
-                h.y = tf32_rna(v.y);
-                h.z = tf32_rna(v.z);
-                h.w = tf32_rna(v.w);
-                r.x = tf32_rna(v.x - h.x);
-                r.y = tf32_rna(v.y - h.y);
-                r.z = tf32_rna(v.z - h.z);
-                r.w = tf32_rna(v.w - h.w);
+                h.x = tf32_round_int(v.x);
+                h.y = tf32_round_int(v.y);
+                h.z = tf32_round_int(v.z);
+                h.w = tf32_round_int(v.w);
+                r.x = tf32_round_int(v.x - h.x);
+                r.y = tf32_round_int(v.y - h.y);
+                r.z = tf32_round_int(v.z - h.z);
+                r.w = tf32_round_int(v.w - h.w);
                 xh[q] = h;
                 xl[q] = r;
             }
