@@ -764,9 +764,18 @@ fx_status create_impl(fx_decode* r, const int64_t* token, const float* const* ks
     if (r->persistent) {
         const fx_status prep = prepare_step_kernel(r->model.device, &r->step_grid);
         if (prep != FX_OK) return prep;
+        if (const char* g = std::getenv("FLUX_B200_STEP_GRID")) {  // tuning: another persistent grid
+            int sms = 0;
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, r->model.device);
+            const int want = std::atoi(g);
+            if (want >= kStepMinGrid && want <= sms) r->step_grid = want;
+        }
+        r->nch = std::max(1, std::min(r->step_grid / kKVHeads, 64));
+        chunk = (r->capacity + r->nch - 1) / r->nch;
+        r->chunk_max = static_cast<int>(((chunk + 31) / 32) * 32);
         FX_REQUIRE(r->step_grid >= kStepMinGrid && r->step_grid <= kStepMaxGrid && r->step_grid <= r->lm_blocks &&
                        kKVHeads * r->nch <= r->step_grid,
-                   "flux native decode: the persistent step needs a GPU with 140 to 384 SMs");
+                   "flux native decode: the persistent step needs a GPU with 128 to 384 SMs");
         for (int l = 0; l < kLayers; ++l) {
             StepLayer& L = r->step_layers[l];
             const fx_status enc = encode_step_maps(r->model.o_proj[l], r->model.down[l], &L);

@@ -1150,10 +1150,16 @@ fx_status prepare_step_kernel(int device, int* grid) {
         return FX_ERR_CUDA;
     }
     if (sms < kStepMinGrid || sms > kStepMaxGrid) {
-        set_error("flux native decode: the persistent step needs a GPU with 140 to 384 SMs");
+        set_error("flux native decode: the persistent step needs a GPU with 128 to 384 SMs");
         return FX_ERR_INVALID;
     }
-    *grid = sms;
+    // The largest grid that splits the 384 SwiGLU feature blocks evenly (128
+    // on a 148-SM B200): phase D is balanced and the split-K tally words have
+    // fewer contributors.  Measured on B200: 13.9 vs 14.3 us per layer at
+    // context 128, equal at 8192.
+    int g = sms;
+    while (g > kStepMinGrid && (kInter / kStepBlock) % g != 0) --g;
+    *grid = g;
     return FX_OK;
 }
 

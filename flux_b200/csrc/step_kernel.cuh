@@ -18,7 +18,7 @@ constexpr int kStepBlock = 4;              // columns per split-K strip (one 16-
 constexpr int kStepStripRows = 192;        // rows per 2-D TMA box of a strip
 constexpr int kStepReplicas = 4;           // copies of the published q | k | v words
 constexpr int kStepAccReplicas = 2;        // copies of each split-K accumulator (spreads the atomics)
-constexpr int kStepMinGrid = 140;          // the per-CTA slices must fit one slot
+constexpr int kStepMinGrid = 128;          // the per-CTA slices must fit one slot (12 SwiGLU features)
 constexpr int kStepMaxGrid = 384;          // every CTA owns at least one block of 4 MLP features
 
 struct StepLayer {
