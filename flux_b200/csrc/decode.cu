@@ -527,6 +527,7 @@ struct fx_decode {
     StepExchange exchange{};      // persistent step: cross-CTA exchange region
     StepLayer step_layers[kLayers]{};  // persistent step: per-layer pointers and strip tensor maps
     int* error;
+    int* inject;  // test hook of the persistent step (fx_decode_inject_failure)
 
     int64_t* token() const { return state; }
     int64_t* position() const { return state + 1; }
@@ -600,6 +601,7 @@ fx_status allocate(fx_decode* r) {
         r->cand_index = carve<long long>(cursor, r->lm_blocks);
         r->counters = carve<unsigned>(cursor, 8);
         r->error = carve<int>(cursor, 4);
+        r->inject = carve<int>(cursor, 4);
         if (pass == 1) r->exchange = step_exchange_views(words, r->nch);
         if (pass == 0) {
             r->workspace_bytes = static_cast<size_t>(reinterpret_cast<uintptr_t>(cursor)) + 256;
@@ -666,6 +668,7 @@ fx_status run_body(fx_decode* r, cudaStream_t stream) {
         a.cand_index = r->cand_index;
         a.sync = r->step_sync;
         a.error = r->error;
+        a.inject = r->inject;
         a.nch = r->nch;
         a.timeline = r->timeline;
         return launch_step_kernel(a, r->step_grid, stream);
@@ -809,7 +812,12 @@ fx_status create_impl(fx_decode* r, const int64_t* token, const float* const* ks
     FX_CUDA_TRY(cudaStreamBeginCapture(r->capture_stream, cudaStreamCaptureModeThreadLocal),
                 "beginning CUDA graph capture");
     r->capture_active = true;
-    st = run_body(r, r->capture_stream);
+    if (std::getenv("FLUX_B200_INJECT_CAPTURE_FAILURE") != nullptr) {  // test hook: a failing launch in capture
+        set_error("flux native decode: injected failure during CUDA graph capture");
+        st = FX_ERR_CUDA;
+    } else {
+        st = run_body(r, r->capture_stream);
+    }
     cudaGraph_t graph = nullptr;
     const cudaError_t end = cudaStreamEndCapture(r->capture_stream, &graph);
     r->capture_active = false;
@@ -1002,10 +1010,26 @@ extern "C" fx_status fx_decode_read_state(fx_decode* r, int32_t which, int64_t* 
         set_error("flux native prefill: a bounded wait in a tensor-core projection gave up");
         return FX_ERR_DEVICE;
     }
+    if (error & 2) {
+        set_error("flux native full decode: a step gave up a bounded wait (or a CTA reported a failure); "
+                  "reset the runtime before the next replay");
+        return FX_ERR_DEVICE;
+    }
     if (error != 0) {
         set_error("flux native full decode: a step ran with its position outside the cache capacity");
         return FX_ERR_DEVICE;
     }
+    return FX_OK;
+}
+
+extern "C" fx_status fx_decode_inject_failure(fx_decode* r, int32_t layer) {
+    FX_REQUIRE(r != nullptr, "fx_decode_inject_failure: null runtime");
+    FX_REQUIRE(r->persistent, "fx_decode_inject_failure: only the persistent step has the hook");
+    FX_REQUIRE(layer >= -1 && layer < kLayers, "fx_decode_inject_failure: layer must be in [-1, 30)");
+    DeviceGuard guard(r->model.device);
+    if (r->pending) FX_CUDA_TRY(cudaEventSynchronize(r->done), "waiting before setting the failure hook");
+    const int value = layer + 1;
+    FX_CUDA_TRY(cudaMemcpy(r->inject, &value, sizeof(int), cudaMemcpyHostToDevice), "setting the failure hook");
     return FX_OK;
 }
 

@@ -635,8 +635,20 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 st_zero(next + i);
         }
         int k = 0;
+        const int inject = *a.inject;
         for (int l = 0; l < kLayers; ++l) {
             const uint32_t tag = s.epoch * 64u + static_cast<uint32_t>(l) + 1u;
+            if (inject == l + 1 && cta == 0) {
+                // Test hook: CTA 0 reports a failure here (as if one of its
+                // bounded waits had expired) and leaves; the other CTAs find
+                // the error word within ~1 ms in their polls and drain.
+                if (tid == 0) {
+                    sh.abort = 1;
+                    atomicOr(a.error, 2);
+                }
+                consumer_sync();
+                goto done;
+            }
             // ------------------------------------------------------ phase A
             if (l == 0) {
                 const bool valid = s.tok >= 0 && s.tok < a.vocab;

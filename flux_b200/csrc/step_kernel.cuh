@@ -74,6 +74,7 @@ struct StepArgs {
     long long* cand_index;    // [grid]
     unsigned* sync;           // [0] LM-head arrivals, [1] step epoch
     int* error;               // bit 1: position outside capacity, bit 2: a bounded wait gave up
+    const int* inject;        // test hook: layer + 1 at which CTA 0 reports a failure (0: none)
     int nch;                  // attention chunks per kv head
     unsigned long long* timeline;  // optional [grid][kStepTimelineEvents] %globaltimer stamps
 };

@@ -374,6 +374,13 @@ FX_API fx_status fx_batch_get_buffers(const fx_batch* runtime, fx_batch_buffers*
 FX_API void fx_batch_destroy(fx_batch* runtime);
 
 #ifdef __cplusplus
+/* Test hook (no counterpart in the reference): the next persistent decode
+ * steps have CTA 0 report a failure at `layer` (0-29; -1 clears) as if one
+ * of its bounded waits had expired.  The other CTAs find the error word in
+ * their polls, drain their copies and return; fx_decode_read_state then
+ * reports FX_ERR_DEVICE until fx_decode_reset.  No GPU fault is involved. */
+FX_API fx_status fx_decode_inject_failure(fx_decode* runtime, int32_t layer);
+
 }  /* extern "C" */
 #endif
 

@@ -267,3 +267,55 @@ def test_prefill_tensor_core_attention_matches_simt(smollm2_flux, monkeypatch):
     torch.testing.assert_close(tc_keys, simt.key_cache[:, 0, :, :2500], rtol=1e-4, atol=1e-5)
     torch.testing.assert_close(tc_values, simt.value_cache[:, 0, :, :2500], rtol=1e-4, atol=1e-5)
 
+
+
+def _decode_from_cache(model, length=300, capacity=320, token=77):
+    from flux_b200.runtime import NativeSmolLM2Decode
+    keys, values = hf.synthetic_cache(hf.smollm2_config(), length, seed=9, std=0.5)
+    keys, values = [k.cuda() for k in keys], [v.cuda() for v in values]
+    tok = torch.tensor([[token]], device="cuda")
+    rt = NativeSmolLM2Decode.capture_from_state(model, tok, keys, values, cache_position=length,
+                                                cache_capacity=capacity)
+    return rt, tok, keys, values
+
+
+def test_step_failure_is_reported_and_recoverable(smollm2_flux):
+    """Failure detection without a GPU fault: CTA 0 of the persistent step
+    reports a failure at layer 7 (fx_decode_inject_failure, as if one of its
+    bounded waits had expired).  The other CTAs find the error word in their
+    polls within ~1 ms and drain, so the step ends promptly (well inside the
+    2 s wait bound), the host reads FX_ERR_DEVICE, the context stays usable,
+    and after a reset the runtime reproduces a fresh runtime's logits."""
+    import time
+    from flux_b200 import _native
+    fresh, tok, keys, values = _decode_from_cache(smollm2_flux)
+    expected = fresh.replay().clone()
+    rt, _, _, _ = _decode_from_cache(smollm2_flux)
+    handle = rt.native_object()._handle
+    _native.check(_native.load().fx_decode_inject_failure(handle, 7))
+    start = time.perf_counter()
+    rt.replay()
+    torch.cuda.synchronize()
+    assert time.perf_counter() - start < 1.0
+    with pytest.raises(RuntimeError, match="bounded wait"):
+        rt.cache_position  # noqa: B018  (reads the state and the error word)
+    _native.check(_native.load().fx_decode_inject_failure(handle, -1))
+    rt.reset(tok, keys, values, cache_position=300)
+    logits = rt.replay()
+    torch.cuda.synchronize()
+    assert rt.cache_position == 301
+    torch.testing.assert_close(logits, expected, rtol=1e-6, atol=1e-6)
+
+
+def test_capture_failure_is_reported_and_cleaned_up(smollm2_flux, monkeypatch):
+    """Host-side injection: a launch that fails while the step graph is being
+    captured ends the capture, frees the half-built runtime and reports the
+    error; the next runtime builds and runs normally."""
+    monkeypatch.setenv("FLUX_B200_INJECT_CAPTURE_FAILURE", "1")
+    with pytest.raises(RuntimeError, match="injected failure during CUDA graph capture"):
+        _decode_from_cache(smollm2_flux)
+    monkeypatch.delenv("FLUX_B200_INJECT_CAPTURE_FAILURE")
+    rt, _, _, _ = _decode_from_cache(smollm2_flux)
+    rt.replay()
+    torch.cuda.synchronize()
+    assert rt.cache_position == 301
