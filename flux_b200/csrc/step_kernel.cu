@@ -366,14 +366,38 @@ __device__ __forceinline__ void fail(const StepArgs& a, Shared& sh) {
     atomicOr(a.error, 2);
 }
 
-// Bounded mbarrier wait; false when the wait gave up or the CTA aborted.
+// Consumer-side bounded mbarrier wait; false when the wait gave up, another
+// CTA reported a failure, or this CTA aborted.  Only consumer threads write
+// sh.abort, and always before a consumer barrier after which every consumer
+// reads it, so they leave together.
 __device__ bool wait_bar(const StepArgs& a, Shared& sh, uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = global_timer();
     while (!mbar_try_wait(bar, parity)) {
         if (sh.abort) return false;
-        if (global_timer() - t0 > kWaitNs) {
+        const unsigned long long dt = global_timer() - t0;
+        if (dt > kPeerCheckNs && ld_error(a.error) != 0) {
+            sh.abort = 1;
+            return false;
+        }
+        if (dt > kWaitNs) {
             fail(a, sh);
+            return false;
+        }
+    }
+    return true;
+}
+
+// Producer-side bounded wait for a free slot.  On expiry it only reports
+// through the error word (the consumers see it in their own waits), since
+// the producer is outside the consumers' barrier.
+__device__ bool producer_wait(const StepArgs& a, Shared& sh, uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_timer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (sh.abort) return false;
+        if (global_timer() - t0 > kWaitNs) {
+            atomicOr(a.error, 2);
             return false;
         }
     }
@@ -609,7 +633,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         if (lane == 0) {
             for (int k = 0; k < s.total; ++k) {
                 const int slot = k % kStepSlots;
-                if (!wait_bar(a, sh, &sh.empty[slot], (static_cast<uint32_t>(k / kStepSlots) & 1u) ^ 1u)) break;
+                if (!producer_wait(a, sh, &sh.empty[slot], (static_cast<uint32_t>(k / kStepSlots) & 1u) ^ 1u)) break;
                 unsigned char* dst = ring + static_cast<size_t>(slot) * kStepSlotBytes;
                 const uint32_t bytes = issue_tile(a, s, k, dst, &sh.full[slot], TileOp::kCount);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
