@@ -443,8 +443,9 @@ def run_attention_sweep(device, peak: float) -> dict:
             v = torch.randn(batch, 3, length, 64, device=device, generator=g)
             ln = torch.tensor(length, device=device)
             out = torch.empty(batch, 9, 1, 64, device=device)
-            floats = lib.fx_gqa_decode_attention_workspace_floats(batch, 9, length, 64)
-            ws = torch.empty(floats, device=device)
+            # partials + zeroed merge counters: the merge runs in the chunk kernel (one launch)
+            floats = lib.fx_gqa_decode_attention_workspace_floats(batch, 9, length, 64) + batch * 3
+            ws = torch.zeros(floats, device=device)
             args = (q.data_ptr(), _native.int64_array(q.stride()), k.data_ptr(), _native.int64_array(k.stride()),
                     v.data_ptr(), _native.int64_array(v.stride()), None, None, None, ln.data_ptr(), out.data_ptr(),
                     ws.data_ptr(), floats, 0.125, batch, 9, 3, length, 64)

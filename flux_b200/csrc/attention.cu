@@ -36,7 +36,10 @@ struct ChunkShared {
     float wsum[kWarps][kGroup];
     alignas(16) float o[kSplits][kGroup][kHeadDim];
     float l[kSplits][kGroup];
+    float mscr[kGroup][2];  // in-kernel merge: per-head max / total of the two warps of a head
+    float tscr[kGroup][2];
     int failed;
+    int last;
 };
 template <int kRows>
 constexpr size_t tile_bytes() { return static_cast<size_t>(kRows) * kHeadDim * sizeof(float); }
@@ -242,6 +245,53 @@ __global__ void __launch_bounds__(kThreads) compact_chunk_kernel(const __grid_co
         }
     }
     if (tid == 0 && sh.failed && a.error != nullptr) atomicOr(a.error, 1u);
+    if (a.counters == nullptr) return;
+    // The last chunk CTA of (b, g) to arrive merges the 3 heads over every
+    // chunk, in chunk order (the merge kernel's arithmetic: bitwise the same
+    // result whichever CTA is last), then rearms the counter.
+    const int active = static_cast<int>((len + kRows - 1) / kRows);
+    __syncthreads();  // this CTA's partials are written
+    if (tid == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(&a.counters[b * kKVHeads + g], 1u);
+        sh.last = prev + 1 == static_cast<unsigned>(active) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!sh.last) return;
+    __threadfence();
+    float* weight = ktile;  // [3][active], the K / V tiles are no longer needed
+    const int mh = tid / kHeadDim, d = tid % kHeadDim, mw = (tid % kHeadDim) >> 5;
+    const bool merger = tid < kGroup * kHeadDim;
+    const float* w = a.ws + (static_cast<size_t>(b) * kQHeads + g * kGroup + (merger ? mh : 0)) * a.chunks * kPart;
+    float mx = -INFINITY;
+    if (merger)
+        for (int cc = d; cc < active; cc += kHeadDim) mx = fmaxf(mx, __ldcg(w + static_cast<size_t>(cc) * kPart));
+    mx = warp_max(mx);
+    if (merger && lane == 0) sh.mscr[mh][mw] = mx;
+    __syncthreads();
+    mx = merger ? fmaxf(sh.mscr[mh][0], sh.mscr[mh][1]) : 0.0f;
+    float total = 0.0f;
+    if (merger)
+        for (int cc = d; cc < active; cc += kHeadDim) {
+            const float f = expf(__ldcg(w + static_cast<size_t>(cc) * kPart) - mx);
+            weight[mh * active + cc] = f;
+            total = fmaf(__ldcg(w + static_cast<size_t>(cc) * kPart + 1), f, total);
+        }
+    total = warp_sum(total);
+    if (merger && lane == 0) sh.tscr[mh][mw] = total;
+    __syncthreads();
+    if (!merger) return;
+    total = sh.tscr[mh][0] + sh.tscr[mh][1];
+    const float* wf = weight + mh * active;
+    float acc = 0.0f, acc2 = 0.0f;
+    int cc = 0;
+    for (; cc + 1 < active; cc += 2) {
+        acc = fmaf(__ldcg(w + static_cast<size_t>(cc) * kPart + 2 + d), wf[cc], acc);
+        acc2 = fmaf(__ldcg(w + static_cast<size_t>(cc + 1) * kPart + 2 + d), wf[cc + 1], acc2);
+    }
+    if (cc < active) acc = fmaf(__ldcg(w + static_cast<size_t>(cc) * kPart + 2 + d), wf[cc], acc);
+    a.out[(static_cast<size_t>(b) * kQHeads + g * kGroup + mh) * kHeadDim + d] = (acc + acc2) / total;
+    if (tid == 0) a.counters[b * kKVHeads + g] = 0u;
 }
 
 // grid (B * 9), 64 threads: combine the active chunks of one (sequence, q
@@ -309,7 +359,7 @@ fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t strea
                                               "launching compact attention chunks", a)
                            : launch_dependent(compact_chunk_kernel<64>, grid, dim3(kThreads), chunk_smem<64>(), stream,
                                               "launching compact attention chunks", a);
-        if (st != FX_OK) return st;
+        if (st != FX_OK || a.counters != nullptr) return st;
         return launch_dependent(compact_merge_kernel, merge_grid, dim3(kHeadDim), 0, stream,
                                 "launching compact attention merge", a);
     }
@@ -318,6 +368,7 @@ fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t strea
     else
         compact_chunk_kernel<64><<<grid, kThreads, chunk_smem<64>(), stream>>>(a);
     FX_CUDA_TRY(cudaGetLastError(), "launching compact attention chunks");
+    if (a.counters != nullptr) return FX_OK;
     compact_merge_kernel<<<merge_grid, kHeadDim, 0, stream>>>(a);
     FX_CUDA_TRY(cudaGetLastError(), "launching compact attention merge");
     return FX_OK;

@@ -18,6 +18,9 @@ struct CompactAttention {
     float* out;                  // [B][9][64]
     float* ws;                   // [B][9][chunks][66]
     unsigned* error;             // optional: bit 1 set if a bounded wait gave up
+    unsigned* counters;          // optional [B][3] arrival counters, zero before the first launch (every launch
+                                 // leaves them zero): the last chunk CTA of a (sequence, kv head) merges, no
+                                 // separate merge launch; null: merge kernel
     float scale;
     int64_t batch, cap, chunks;  // chunks = ceil(cap / chunk_rows)
     int chunk_rows;              // 128 (the op's workspace format) or 64
@@ -28,8 +31,9 @@ inline int64_t compact_attention_workspace(int64_t batch, int64_t cap, int rows 
     return batch * kQHeads * ((cap + rows - 1) / rows) * (kHeadDim + 2);
 }
 
-// Enqueue the chunk and merge kernels on `stream` (`dependent`: as
-// programmatic dependent launches of the preceding kernel).
+// Enqueue the chunk kernel (and the merge kernel unless `counters` is set)
+// on `stream` (`dependent`: as programmatic dependent launches of the
+// preceding kernel).
 fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream, bool dependent = false);
 
 }  // namespace fx

@@ -14,6 +14,8 @@
 namespace fx {
 namespace {
 
+constexpr int64_t kFusedMergeMaxCtas = 512;  // chunk CTAs up to which the op merges in-kernel
+
 // ------------------------------------------------------------------ norms
 
 // One CTA per row.  With `residual` set, v = hidden + residual is written to
@@ -539,6 +541,13 @@ extern "C" fx_status fx_gqa_decode_attention_f32(const float* query, const int64
         c.lengths = cache_length; c.length_stride = 0;
         c.out = output; c.ws = workspace; c.error = nullptr; c.scale = scale;
         c.batch = batch; c.cap = capacity; c.chunks = chunks; c.chunk_rows = kCompactChunk;
+        // Room for merge counters after the partials and a small grid: merge
+        // inside the chunk kernel (one launch).  On large grids the per-CTA
+        // fence and arrival cost more than the merge launch saves (B200,
+        // B = 64, L = 8192: 182 vs 160 us), so they keep the merge kernel.
+        const int64_t partials = fx_gqa_decode_attention_workspace_floats(batch, query_heads, capacity, head_dim);
+        if (workspace_floats >= partials + batch * kv_heads && batch * kv_heads * chunks <= kFusedMergeMaxCtas)
+            c.counters = reinterpret_cast<unsigned*>(workspace + partials);
         return launch_compact_attention(c, as_stream(stream));
     }
     a.mask = mask; a.length = cache_length; a.out = output; a.ws = workspace; a.scale = scale;
@@ -669,8 +678,8 @@ extern "C" fx_status fx_gqa_decode_attention_static_scratch_f32(
     float* scratch = nullptr;
     const fx_status status = fx::static_scratch_address(&scratch);
     if (status != FX_OK) return status;
+    // exactly the partials (no merge counters: the array is shared by calls of any size)
     return fx_gqa_decode_attention_f32(query, query_strides4, key_cache, key_strides4, value_cache, value_strides4,
-                                       mask, mask_sizes4, mask_strides4, cache_length, output, scratch,
-                                       fx::kStaticScratchFloats, scale, batch, query_heads, kv_heads, capacity,
-                                       head_dim, stream);
+                                       mask, mask_sizes4, mask_strides4, cache_length, output, scratch, needed, scale,
+                                       batch, query_heads, kv_heads, capacity, head_dim, stream);
 }

@@ -107,7 +107,13 @@ FX_API int64_t fx_gqa_decode_attention_workspace_floats(int64_t batch, int64_t q
  * query [B, Hq, 1, D], caches [B, Hkv, capacity, D] (strides in elements),
  * optional additive mask broadcastable to [B, Hq, 1, capacity], optional
  * device scalar cache_length (valid rows, clamped to [1, capacity]); output
- * contiguous [B, Hq, 1, D].  head_dim <= 256.
+ * contiguous [B, Hq, 1, D].  head_dim <= 256.  For SmolLM2's geometry over
+ * contiguous caches, a workspace of at least
+ * fx_gqa_decode_attention_workspace_floats(...) + batch * kv_heads floats
+ * holds merge counters after the partials (zero them before the first call
+ * with that workspace; every call leaves them zero): when the problem has at
+ * most 512 chunk CTAs (batch * kv_heads * ceil(capacity / 128)) the merge
+ * then runs in the chunk kernel, one launch instead of two.
  * Replaces flux::gqa_decode_attention_cuda_fp32
  * (csrc/gqa_decode_attention/gqa_decode_attention_cuda.h:10-30). */
 FX_API fx_status fx_gqa_decode_attention_f32(const float* query, const int64_t* query_strides4,

@@ -18,15 +18,17 @@ pytestmark = pytest.mark.gpu
 TOL = dict(rtol=2e-5, atol=2e-6)
 
 
-def attention(q, k, v, length):
+def attention(q, k, v, length, fused=False):
     """``fx_gqa_decode_attention_f32`` through the C ABI (any batch; the torch
-    op keeps the reference's batch-1 contract)."""
+    op keeps the reference's batch-1 contract).  `fused`: a workspace with
+    zeroed merge counters after the partials (the merge runs in the chunk
+    kernel)."""
     from flux_b200 import _native
     lib = _native.load()
     batch, capacity = q.shape[0], k.shape[2]
     out = torch.empty(batch, 9, 1, 64, device="cuda")
-    floats = lib.fx_gqa_decode_attention_workspace_floats(batch, 9, capacity, 64)
-    ws = torch.empty(floats, device="cuda")
+    floats = lib.fx_gqa_decode_attention_workspace_floats(batch, 9, capacity, 64) + (batch * 3 if fused else 0)
+    ws = torch.zeros(floats, device="cuda") if fused else torch.empty(floats, device="cuda")
     ln = torch.tensor(length, device="cuda")
     _native.check(lib.fx_gqa_decode_attention_f32(
         q.data_ptr(), _native.int64_array(q.stride()), k.data_ptr(), _native.int64_array(k.stride()),
@@ -93,3 +95,45 @@ def test_compact_attention_large_batch_long_context_properties():
         out = attention(q[7:8].contiguous(), k[7:8].contiguous(), vs.cuda(), length)
         expected = o.gqa_decode_attention(qs, ks, vs.numpy(), None, 0.125, length)
         np.testing.assert_allclose(out.cpu().numpy(), expected, **TOL)
+
+
+@pytest.mark.parametrize("batch,length,capacity", [(1, 1, 130), (1, 128, 128), (3, 777, 1000), (16, 1024, 1024),
+                                                   (64, 4097, 4097), (2, 8192, 8192)])
+def test_in_kernel_merge_matches_merge_kernel(batch, length, capacity):
+    """The last-CTA merge (workspace with counters) is bitwise the merge
+    kernel's result; repeated calls on one workspace (the counters rearm)
+    and a CUDA-graph replay give the same bits."""
+    from flux_b200 import _native
+    lib = _native.load()
+    q, k, v = (t.cuda() for t in _inputs(batch, length, capacity, seed=batch * 31 + length))
+    two_launch = attention(q, k, v, length)
+    one_launch = attention(q, k, v, length, fused=True)
+    assert torch.equal(one_launch, two_launch)
+    out = torch.empty(batch, 9, 1, 64, device="cuda")
+    floats = lib.fx_gqa_decode_attention_workspace_floats(batch, 9, capacity, 64) + batch * 3
+    ws = torch.zeros(floats, device="cuda")
+    ln = torch.tensor(length, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def call():
+        _native.check(lib.fx_gqa_decode_attention_f32(
+            q.data_ptr(), _native.int64_array(q.stride()), k.data_ptr(), _native.int64_array(k.stride()),
+            v.data_ptr(), _native.int64_array(v.stride()), None, None, None, ln.data_ptr(), out.data_ptr(),
+            ws.data_ptr(), floats, 0.125, batch, 9, 3, capacity, 64, stream.cuda_stream))
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            call()
+        stream.synchronize()
+        assert torch.equal(out, two_launch)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            call()
+        for _ in range(3):
+            out.zero_()
+            graph.replay()
+        stream.synchronize()
+    assert torch.equal(out, two_launch)
+    counters = ws[-batch * 3:].view(torch.int32)
+    assert int(counters.abs().sum()) == 0
+
