@@ -428,8 +428,10 @@ def run_context_sweep(model, device, seed: int, peak: float, steps: int = 32, wa
 
 def run_attention_sweep(device, peak: float) -> dict:
     """the compact decode attention alone through the C ABI,
-    Q/K/V ~ N(0, 1) seeded, B x L grid, L2 flushed before every launch; each
-    launch is replayed from a CUDA graph so host submission is not timed."""
+    Q/K/V ~ N(0, 1) seeded, B x L grid, L2 flushed before every launch (a
+    256 MB write in the same graph); 20 graph replays per timing, minus the
+    same replays of the flush alone, so host submission is not timed and the
+    event clock's ~2 us tick does not quantise small launches."""
     from flux_b200 import _native
     lib = _native.load()
     flush = torch.empty(64 * 1024 * 1024, device=device)  # 256 MB > L2
@@ -452,26 +454,39 @@ def run_attention_sweep(device, peak: float) -> dict:
             with torch.cuda.stream(stream):
                 _native.check(lib.fx_gqa_decode_attention_f32(*args, stream.cuda_stream))  # loads the kernels
                 stream.synchronize()
-                graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(graph, stream=stream):
+                # graph A: L2 flush + attention; graph B: the flush alone.  Each is
+                # replayed `reps` times between two events (the event clock ticks
+                # ~2 us on this GPU); attention time = (A - B) / reps.
+                with_attention, flush_only = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+                with torch.cuda.graph(with_attention, stream=stream):
+                    flush.fill_(1.0)
                     _native.check(lib.fx_gqa_decode_attention_f32(*args, stream.cuda_stream))
-                times = []
-                for it in range(13):
-                    flush.fill_(float(it))
+                with torch.cuda.graph(flush_only, stream=stream):
+                    flush.fill_(2.0)
+                reps = 20
+
+                def timed(graph):
                     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     s.record(stream)
-                    graph.replay()
+                    for _ in range(reps):
+                        graph.replay()
                     e.record(stream)
                     stream.synchronize()
-                    if it >= 3:
-                        times.append(s.elapsed_time(e))
+                    return s.elapsed_time(e) / reps
+
+                times = []
+                for it in range(5):
+                    ta, tb = timed(with_attention), timed(flush_only)
+                    if it >= 1:
+                        times.append(ta - tb)
             t = statistics.median(times) * 1e-3
             nbytes = batch * (1536 * length + 4608)
             rows.append({"B": batch, "L": length, "us": round(t * 1e6, 2), "GBps": round(nbytes / t / 1e9, 1),
                          "frac": round(nbytes / t / 1e9 / peak, 3)})
-            del graph, q, k, v, out, ws
+            del with_attention, flush_only, q, k, v, out, ws
     return {"metric": "isolated decode attention GB/s (configs[4])", "unit": "GB/s", "peak": peak,
             "algorithmic_bytes": "B*(1536*L + 4608)", "l2": "flushed (256 MB write) before every launch",
+            "timing": "20 graph replays of (flush + attention) minus 20 of the flush alone, median of 4",
             "rows": rows}
 
 
