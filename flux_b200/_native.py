@@ -154,6 +154,7 @@ SIGNATURES: dict[str, tuple] = {
     "fx_decode_generate": (_st, [_p, _i64, _p]),
     "fx_decode_reset": (_st, [_p, _p, _p, _p, _i64, _i64, _p]),
     "fx_decode_inject_failure": (_st, [_p, ctypes.c_int32]),
+    "fx_decode_set_eos": (_st, [_p, _i64]),
     "fx_decode_install_prefill": (_st, [_p, _p, _i64, _p]),
     "fx_decode_wait": (_st, [_p, _p]),
     "fx_decode_get_buffers": (_st, [_p, ctypes.POINTER(DecodeBuffers)]),

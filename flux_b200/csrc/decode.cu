@@ -370,6 +370,7 @@ __global__ void __launch_bounds__(128) down_kernel(const float* __restrict__ s, 
 }
 
 struct LmArgs {
+    int* stop;               // [0] generation ended on EOS (state frozen), [1] EOS token + 1 (0: none)
     const float* h;
     const float* norm_w;
     float eps;
@@ -456,12 +457,15 @@ __global__ void __launch_bounds__(256) lm_head_kernel(LmArgs a) {
         argmax_combine(bv, bi, v, i);
     }
     if (lane == 0) {
-        const int64_t selected = bi < 0 ? 0 : bi;
-        *a.token = selected;
-        const int64_t st = *a.step;
-        if (st >= 0 && st < a.generated_capacity) a.generated[st] = selected;
-        *a.step = st + 1;
-        *a.position = *a.length;
+        if (a.stop[0] == 0) {  // after an EOS the state stays frozen
+            const int64_t selected = bi < 0 ? 0 : bi;
+            *a.token = selected;
+            const int64_t st = *a.step;
+            if (st >= 0 && st < a.generated_capacity) a.generated[st] = selected;
+            *a.step = st + 1;
+            *a.position = *a.length;
+            if (a.stop[1] != 0 && selected == static_cast<int64_t>(a.stop[1]) - 1) a.stop[0] = 1;
+        }
         *a.counter = 0u;
     }
 }
@@ -469,7 +473,7 @@ __global__ void __launch_bounds__(256) lm_head_kernel(LmArgs a) {
 // Device-side state installation (graph-safe, no host staging).
 __global__ void set_state_kernel(int64_t* token, const int64_t* token_src, int64_t* position, int64_t* length,
                                  int64_t* step, int64_t* generated, int64_t value, int64_t step_value,
-                                 bool seed_generated) {
+                                 bool seed_generated, int* stop) {
     if (threadIdx.x != 0) return;
     const int64_t t = *token_src;
     *token = t;
@@ -477,6 +481,7 @@ __global__ void set_state_kernel(int64_t* token, const int64_t* token_src, int64
     *length = value;
     *step = step_value;
     if (seed_generated) generated[0] = t;
+    stop[0] = 0;  // a new generation (the EOS token, stop[1], is kept)
 }
 
 // ------------------------------------------------------------------ host
@@ -528,6 +533,7 @@ struct fx_decode {
     StepLayer step_layers[kLayers]{};  // persistent step: per-layer pointers and strip tensor maps
     int* error;
     int* inject;  // test hook of the persistent step (fx_decode_inject_failure)
+    int* stop;    // [0] generation ended on EOS, [1] EOS token + 1 (0: none; fx_decode_set_eos)
 
     int64_t* token() const { return state; }
     int64_t* position() const { return state + 1; }
@@ -602,6 +608,7 @@ fx_status allocate(fx_decode* r) {
         r->counters = carve<unsigned>(cursor, 8);
         r->error = carve<int>(cursor, 4);
         r->inject = carve<int>(cursor, 4);
+        r->stop = carve<int>(cursor, 4);
         if (pass == 1) r->exchange = step_exchange_views(words, r->nch);
         if (pass == 0) {
             r->workspace_bytes = static_cast<size_t>(reinterpret_cast<uintptr_t>(cursor)) + 256;
@@ -635,7 +642,7 @@ fx_status initialize_state(fx_decode* r, const int64_t* token, const float* cons
     FX_CUDA_TRY(cudaMemsetAsync(r->workspace, 0, r->workspace_bytes, stream), "clearing workspace");
     FX_CUDA_TRY(cudaMemsetAsync(r->generated(), 0, r->capacity * sizeof(int64_t), stream), "clearing generated");
     set_state_kernel<<<1, 32, 0, stream>>>(r->token(), token, r->position(), r->length(), r->step(), r->generated(),
-                                           position, 0, false);
+                                           position, 0, false, r->stop);
     FX_CUDA_TRY(cudaGetLastError(), "initializing decode state");
     return FX_OK;
 }
@@ -669,6 +676,7 @@ fx_status run_body(fx_decode* r, cudaStream_t stream) {
         a.sync = r->step_sync;
         a.error = r->error;
         a.inject = r->inject;
+        a.stop = r->stop;
         a.nch = r->nch;
         a.timeline = r->timeline;
         return launch_step_kernel(a, r->step_grid, stream);
@@ -707,6 +715,7 @@ fx_status run_body(fx_decode* r, cudaStream_t stream) {
         down_kernel<<<kHidden / 4, 128, 0, stream>>>(r->swiglu_out, m.down[l], r->h_mid, h_out);
     }
     LmArgs la{};
+    la.stop = r->stop;
     la.h = r->h_a;  // 30 layers: the last output lands in h_a
     la.norm_w = m.final_norm;
     la.eps = m.epsilon;
@@ -958,7 +967,7 @@ extern "C" fx_status fx_decode_install_prefill(fx_decode* r, const int64_t* toke
     DeviceGuard guard(r->model.device);
     cudaStream_t s = as_stream(stream);
     set_state_kernel<<<1, 32, 0, s>>>(r->token(), token, r->position(), r->length(), r->step(), r->generated(),
-                                      position, 1, true);
+                                      position, 1, true, r->stop);
     FX_CUDA_TRY(cudaGetLastError(), "installing prefill state");
     FX_CUDA_TRY(cudaEventRecord(r->done, s), "recording prefill completion");
     r->start_position = position;
@@ -1026,6 +1035,16 @@ extern "C" fx_status fx_decode_read_state(fx_decode* r, int32_t which, int64_t* 
         set_error("flux native full decode: a step ran with its position outside the cache capacity");
         return FX_ERR_DEVICE;
     }
+    return FX_OK;
+}
+
+extern "C" fx_status fx_decode_set_eos(fx_decode* r, int64_t eos_token) {
+    FX_REQUIRE(r != nullptr, "fx_decode_set_eos: null runtime");
+    FX_REQUIRE(eos_token >= -1 && eos_token < r->vocab, "fx_decode_set_eos: EOS token must be -1 or a vocabulary id");
+    DeviceGuard guard(r->model.device);
+    if (r->pending) FX_CUDA_TRY(cudaEventSynchronize(r->done), "waiting before setting the EOS token");
+    const int value = static_cast<int>(eos_token + 1);
+    FX_CUDA_TRY(cudaMemcpy(r->stop + 1, &value, sizeof(int), cudaMemcpyHostToDevice), "setting the EOS token");
     return FX_OK;
 }
 

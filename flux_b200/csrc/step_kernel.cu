@@ -607,6 +607,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = gridDim.x, cta = blockIdx.x;
 
+    if (*reinterpret_cast<volatile int*>(a.stop) != 0) return;  // generation already ended on EOS (uniform)
     Sched s;
     make_sched(a, G, cta, s);
     if (s.pos < 0 || s.pos >= a.capacity) {
@@ -1074,6 +1075,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     *a.token = selected;
                     const int64_t st = *a.step;
                     if (st >= 0 && st < cap) a.generated[st] = selected;
+                    if (a.stop[1] != 0 && selected == static_cast<int64_t>(a.stop[1]) - 1) a.stop[0] = 1;
                     *a.step = st + 1;
                     *a.position = s.pos + 1;
                     a.sync[0] = 0u;

@@ -76,6 +76,8 @@ struct StepArgs {
     unsigned* sync;           // [0] LM-head arrivals, [1] step epoch
     int* error;               // bit 1: position outside capacity, bit 2: a bounded wait gave up
     const int* inject;        // test hook: layer + 1 at which CTA 0 reports a failure (0: none)
+    int* stop;                // [0] set once a step produced the EOS token: later steps return at once
+                              // [1] EOS token + 1 (0: no EOS)
     int nch;                  // attention chunks per kv head
     unsigned long long* timeline;  // optional [grid][kStepTimelineEvents] %globaltimer stamps
 };

@@ -256,8 +256,12 @@ class NativeDecodeObject:
                                                       _stream(self._device)))
         return self._logits
 
-    def generate_greedy(self, decode_steps: int) -> torch.Tensor:
-        _native.check(_native.load().fx_decode_generate(self._handle, int(decode_steps), _stream(self._device)))
+    def generate_greedy(self, decode_steps: int, eos_token_id: int | None = None) -> torch.Tensor:
+        """`decode_steps` chained greedy steps on device; with `eos_token_id`
+        the steps after the one that samples it leave the state unchanged."""
+        lib = _native.load()
+        _native.check(lib.fx_decode_set_eos(self._handle, -1 if eos_token_id is None else int(eos_token_id)))
+        _native.check(lib.fx_decode_generate(self._handle, int(decode_steps), _stream(self._device)))
         return self._generated
 
     def reset(self, token: torch.Tensor, key_caches: Sequence[torch.Tensor], value_caches: Sequence[torch.Tensor],
@@ -348,13 +352,26 @@ class NativePrefillObject:
     def replay(self, token: torch.Tensor | None = None) -> torch.Tensor:
         return self._decode.replay(token)
 
-    def generate_greedy(self, max_new_tokens: int) -> torch.Tensor:
+    def generate_greedy(self, max_new_tokens: int, eos_token_id: int | None = None) -> torch.Tensor:
         if max_new_tokens < 1:
             raise RuntimeError(f"{self._PREFIX}: max_new_tokens must be positive")
         if max_new_tokens > self._decode.capacity() - self._rows + 1:
             raise RuntimeError(f"{self._PREFIX}: generation exceeds fixed cache capacity")
-        storage = self._decode.generate_greedy(max_new_tokens - 1)
-        return storage.narrow(0, 0, max_new_tokens).view(1, max_new_tokens)
+        if eos_token_id is None:
+            storage = self._decode.generate_greedy(max_new_tokens - 1)
+            return storage.narrow(0, 0, max_new_tokens).view(1, max_new_tokens)
+        if not 0 <= int(eos_token_id) < self._decode.vocabulary_size():
+            raise RuntimeError(f"{self._PREFIX}: eos_token_id must be a vocabulary id")
+        # The prefill's own token may already be EOS; otherwise the device
+        # loop stops itself and the step counter gives the length.
+        if int(self._decode.generated_tokens()[0].item()) == int(eos_token_id):
+            steps = 0
+            self._decode.generate_greedy(0, eos_token_id)
+        else:
+            self._decode.generate_greedy(max_new_tokens - 1, eos_token_id)
+            steps = self._decode.generation_step() - 1
+        n = steps + 1
+        return self._decode.generated_tokens().narrow(0, 0, n).view(1, n)
 
     def logits(self) -> torch.Tensor: return self._logits
     def final_hidden(self) -> torch.Tensor: return self._final_hidden
@@ -434,10 +451,13 @@ class NativeSmolLM2Prefill:
     def replay(self, token: torch.Tensor | None = None) -> torch.Tensor:
         return self._native.replay(token)
 
-    def generate_greedy(self, max_new_tokens: int) -> torch.Tensor:
+    def generate_greedy(self, max_new_tokens: int, *, eos_token_id: int | None = None) -> torch.Tensor:
+        """Greedy tokens [1, n] starting with the prefill's token: n =
+        max_new_tokens, or fewer when `eos_token_id` is given and sampled (the
+        EOS token is included; the device loop stops on it)."""
         if max_new_tokens < 1:
             raise ValueError("max_new_tokens must be positive")
-        return self._native.generate_greedy(max_new_tokens)
+        return self._native.generate_greedy(max_new_tokens, eos_token_id)
 
     logits = property(lambda self: self._native.logits())
     final_hidden = property(lambda self: self._native.final_hidden())
@@ -650,12 +670,14 @@ class NativeSmolLM2Decode:
         return self._native
 
 
-def native_smollm2_greedy_generate(model: nn.Module, input_ids: torch.Tensor, *, max_new_tokens: int) -> torch.Tensor:
-    """Generate greedily with native prefill and native decode replay."""
+def native_smollm2_greedy_generate(model: nn.Module, input_ids: torch.Tensor, *, max_new_tokens: int,
+                                   eos_token_id: int | None = None) -> torch.Tensor:
+    """Generate greedily with native prefill and native decode replay (stopping
+    on device after `eos_token_id` when given)."""
     if max_new_tokens < 1:
         raise ValueError("max_new_tokens must be positive")
     runtime = NativeSmolLM2Prefill.capture(model, input_ids, max_decode_steps=max_new_tokens - 1)
-    generated = runtime.generate_greedy(max_new_tokens)
+    generated = runtime.generate_greedy(max_new_tokens, eos_token_id=eos_token_id)
     return torch.cat((input_ids, generated), dim=-1)
 
 

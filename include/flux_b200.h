@@ -380,6 +380,14 @@ FX_API fx_status fx_batch_get_buffers(const fx_batch* runtime, fx_batch_buffers*
 FX_API void fx_batch_destroy(fx_batch* runtime);
 
 #ifdef __cplusplus
+/* EOS-aware greedy generation (the reference's generation is fixed-length,
+ * README.md:220; its listed next step, README.md:391): once a step samples
+ * `eos_token`, later replays leave every state buffer unchanged (the
+ * persistent step returns at once), so fx_decode_generate(n) stops on device
+ * and the generation step counter tells how many tokens were produced.  -1
+ * disables it; create and reset disable it, prefill installs keep it. */
+FX_API fx_status fx_decode_set_eos(fx_decode* runtime, int64_t eos_token);
+
 /* Test hook (no counterpart in the reference): the next persistent decode
  * steps have CTA 0 report a failure at `layer` (0-29; -1 clears) as if one
  * of its bounded waits had expired.  The other CTAs find the error word in

@@ -94,6 +94,42 @@ def test_greedy_generation_matches_reference_exactly(tiny_flux, tiny30_golden):
     assert torch.equal(full, expected)
 
 
+@pytest.mark.parametrize("mode", ["persistent", "kernels"])
+def test_greedy_generation_stops_on_eos(tiny_flux, tiny30_golden, monkeypatch, mode):
+    """EOS-aware generation (the reference generates a fixed length; its README
+    lists on-device EOS termination as the next step): the device loop stops
+    after the step that samples the EOS token -- returned tokens, generation
+    step and cache position all end there -- for an EOS inside the sequence,
+    one equal to the prefill's own token, and one never sampled."""
+    from flux_b200.runtime import NativeSmolLM2Prefill, native_smollm2_greedy_generate
+    if mode == "kernels":
+        monkeypatch.setenv("FLUX_B200_DECODE_STEP", "kernels")
+    tokens = tiny30_golden["generate7_8"].reshape(-1)[7:].tolist()  # the reference's 8 greedy tokens
+    k = next((i for i in range(1, len(tokens)) if tokens[i] not in tokens[:i]), None)
+    ids = gi.tiny30_ids(7).cuda()
+    with torch.inference_mode():
+        native = NativeSmolLM2Prefill.capture(tiny_flux, ids, max_decode_steps=7)
+        if k is not None:
+            out = native.generate_greedy(8, eos_token_id=tokens[k]).cpu()
+            assert out.view(-1).tolist() == tokens[:k + 1]
+            assert native.generation_step == k + 1
+            assert native.cache_position == 7 + k
+            native.prefill(ids)
+        out = native.generate_greedy(8, eos_token_id=tokens[0]).cpu()
+        assert out.view(-1).tolist() == tokens[:1]
+        assert native.cache_position == 7
+        native.prefill(ids)
+        never = next(t for t in range(128) if t not in tokens)
+        out = native.generate_greedy(8, eos_token_id=never).cpu()
+        assert out.view(-1).tolist() == tokens
+        assert native.cache_position == 7 + 7
+        native.prefill(ids)
+        assert native.generate_greedy(8).cpu().view(-1).tolist() == tokens  # no EOS: fixed length
+        if k is not None:
+            full = native_smollm2_greedy_generate(tiny_flux, ids, max_new_tokens=8, eos_token_id=tokens[k]).cpu()
+            assert full.view(-1).tolist() == ids.view(-1).cpu().tolist() + tokens[:k + 1]
+
+
 def test_eager_flux_path_and_decode_capture(tiny30_model, tiny_flux, tiny30_golden):
     """Eager Flux ops (HF forward with torch.ops.flux.*) then the native decode
     captured from that eager prefill (``NativeSmolLM2Decode.capture``)."""
