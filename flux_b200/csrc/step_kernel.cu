@@ -490,9 +490,12 @@ __device__ __forceinline__ unsigned long long tally_expected(int G, int r) {
 // dst[i] = base[i] + the split-K sum i, once every contributor's add has
 // landed in every replica word (bounded polls; no fence needed: count and
 // sum share the word).  NaN where a contributor's partial was out of range.
-// The per-warp sums of squares of dst are left in sh.scratch for normalise().
+// The per-warp sums of squares of dst are left in sh.scratch for normalise()
+// / norm_inverse(); with `norm_w`, also xg[i] = dst[i] * norm_w[i] (the
+// RMSNorm weight applied, the 1 / rms factor left to the caller's dot
+// products).
 __device__ bool tally_read(const StepArgs& a, Shared& sh, const unsigned long long* acc, const float* base,
-                           float* dst, int G) {
+                           float* dst, int G, const float* norm_w = nullptr, float* xg = nullptr) {
     float ss = 0.0f;  // sum of squares of dst (per-warp partials left in scratch for the RMSNorm)
     for (int i = threadIdx.x; i < kHidden; i += kStepConsumers) {
         unsigned long long w[kStepAccReplicas];
@@ -532,6 +535,7 @@ __device__ bool tally_read(const StepArgs& a, Shared& sh, const unsigned long lo
         }
         dst[i] = bad ? __int_as_float(0x7fc00000) : base[i] + static_cast<float>(static_cast<double>(total) * kTallyUnit);
         ss = fmaf(dst[i], dst[i], ss);
+        if (xg != nullptr) xg[i] = dst[i] * norm_w[i];
     }
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) sh.scratch[threadIdx.x >> 5] = ss;
@@ -549,6 +553,15 @@ __device__ void normalise(Shared& sh, const float* src, const float* w, float ep
     const float inv = rsqrtf(ss / static_cast<float>(kHidden) + eps);
     for (int i = threadIdx.x; i < kHidden; i += kStepConsumers) sh.xs[i] = src[i] * inv * w[i];
     consumer_sync();
+}
+
+// 1 / rms of the vector whose per-warp sums of squares are in sh.scratch
+// (after the barrier that published them).
+__device__ __forceinline__ float norm_inverse(const Shared& sh, float eps) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kConsumerWarps; ++q) ss += sh.scratch[q];
+    return rsqrtf(ss / static_cast<float>(kHidden) + eps);
 }
 
 // Half-warp dot product of a 576-float row with xs (both in shared memory).
@@ -674,12 +687,18 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 goto done;
             }
             // ------------------------------------------------------ phase A
+            // The tile with this layer's input-norm weights and QKV rows; the
+            // barrier of the h read below also publishes this wait.  xs gets
+            // h * norm weight, and the dot products take the 1 / rms factor.
+            wait_tiles(a, sh, k, 1);
+            const float* t = slot_ptr(ring, k);
             if (l == 0) {
                 const bool valid = s.tok >= 0 && s.tok < a.vocab;
                 float ss = 0.0f;
                 for (int i = tid; i < kHidden; i += kStepConsumers) {
                     sh.hraw[i] = valid ? __ldg(a.embedding + s.tok * kHidden + i) : 0.0f;
                     ss = fmaf(sh.hraw[i], sh.hraw[i], ss);
+                    sh.xs[i] = sh.hraw[i] * t[i];
                 }
                 ss = warp_sum(ss);
                 if (lane == 0) sh.scratch[warp] = ss;
@@ -688,19 +707,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     sh.rope_s[tid] = __ldg(a.sin_table + s.pos * kHeadDim + tid);
                 }
                 consumer_sync();
-            } else if (!tally_read(a, sh, down_tally(l - 1), sh.mid, sh.hraw, G)) {
+                if (sh.abort) goto done;
+            } else if (!tally_read(a, sh, down_tally(l - 1), sh.mid, sh.hraw, G, t, sh.xs)) {
                 goto done;
             }
             LAYER_MARK(0);
             {
-                wait_tiles(a, sh, k, 1);
-                const float* t = slot_ptr(ring, k);
-                normalise(sh, sh.hraw, t, a.eps);  // its barrier also publishes the tile wait
-                if (sh.abort) goto done;
+                const float inv = norm_inverse(sh, a.eps);
                 if (warp < s.t1 - s.t0) {
                     int ra, rb, kind;
                     task_rows(s.t0 + warp, ra, rb, kind);
-                    const float y = row_dot(t + kHidden * (1 + 2 * warp + half), sh.xs, l16);
+                    const float y = row_dot(t + kHidden * (1 + 2 * warp + half), sh.xs, l16) * inv;
                     const float ya = __shfl_sync(0xffffffffu, y, 0);
                     const float yb = __shfl_sync(0xffffffffu, y, 16);
                     float out = y;
@@ -988,17 +1005,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             LAYER_MARK(6);
 
             // ------------------------------------------------------ phase D
-            if (!tally_read(a, sh, mid_tally(l), sh.hraw, sh.mid, G)) goto done;
+            // gate, up and down tiles together; the barrier of the h' read also
+            // publishes these waits (xs = h' * post-norm weight).
+            wait_tiles(a, sh, k, 3);
+            if (!tally_read(a, sh, mid_tally(l), sh.hraw, sh.mid, G, sh.wpost, sh.xs)) goto done;
             LAYER_MARK(7);
             {
                 const int nf = (s.f1 - s.f0) * kStepBlock;
-                // gate, up and down tiles together; the norm's barrier also publishes the waits.
-                wait_tiles(a, sh, k, 3);
-                normalise(sh, sh.mid, sh.wpost, a.eps);
-                if (sh.abort) goto done;
+                const float inv = norm_inverse(sh, a.eps);
                 // warp f: gate row f on lanes 0-15, up row f on lanes 16-31, SwiGLU on lane 0.
                 if (warp < nf) {
-                    const float y = row_dot(slot_ptr(ring, k + half) + warp * kHidden, sh.xs, l16);
+                    const float y = row_dot(slot_ptr(ring, k + half) + warp * kHidden, sh.xs, l16) * inv;
                     const float up = __shfl_sync(0xffffffffu, y, 16);
                     if (lane == 0) sh.act[warp] = swiglu(y, up);
                 }
