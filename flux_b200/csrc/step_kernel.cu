@@ -470,13 +470,28 @@ __device__ unsigned long long poll_word(const StepArgs& a, Shared& sh, const uns
     return v;
 }
 
-// The consumers poll n tagged words into dst; false (uniformly) on abort.
-__device__ bool poll_into(const StepArgs& a, Shared& sh, const unsigned long long* src, int n, uint32_t tag,
-                          float* dst) {
+// Phase B's inputs in one poll round and one barrier: q of kv group g (192
+// words) and, for the CTA that owns the new row, that row's k and v (64 each).
+__device__ bool poll_attention_inputs(const StepArgs& a, Shared& sh, const unsigned long long* qkv, int g,
+                                      bool with_new, uint32_t tag) {
+    constexpr int kQ = kGroup * kHeadDim;
+    const int n = kQ + (with_new ? 2 * kHeadDim : 0);
     for (int i = threadIdx.x; i < n; i += kStepConsumers) {
-        unsigned long long v = ld_word(src + i);
-        if (word_tag(v) != tag) v = poll_word(a, sh, src + i, v, tag);
-        dst[i] = word_value(v);
+        const unsigned long long* src;
+        float* dst;
+        if (i < kQ) {
+            src = qkv + g * kQ + i;
+            dst = sh.qs + i;
+        } else if (i < kQ + kHeadDim) {
+            src = qkv + kHidden + g * kHeadDim + (i - kQ);
+            dst = sh.knew + (i - kQ);
+        } else {
+            src = qkv + kHidden + kKVHeads * kHeadDim + g * kHeadDim + (i - kQ - kHeadDim);
+            dst = sh.vnew + (i - kQ - kHeadDim);
+        }
+        unsigned long long v = ld_word(src);
+        if (word_tag(v) != tag) v = poll_word(a, sh, src, v, tag);
+        *dst = word_value(v);
     }
     consumer_sync();
     return !sh.abort;
@@ -750,13 +765,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             // ------------------------------------------------------ phase B
             if (s.has_rows) {
                 const unsigned long long* qkv = a.x.qkv + (parity(l) * kStepReplicas + cta % kStepReplicas) * kQKV;
-                if (!poll_into(a, sh, qkv + s.g * kGroup * kHeadDim, kGroup * kHeadDim, tag, sh.qs)) goto done;
-                if (s.owns_new) {
-                    if (!poll_into(a, sh, qkv + kHidden + s.g * kHeadDim, kHeadDim, tag, sh.knew)) goto done;
-                    if (!poll_into(a, sh, qkv + kHidden + kKVHeads * kHeadDim + s.g * kHeadDim, kHeadDim, tag,
-                                   sh.vnew))
-                        goto done;
-                }
+                if (!poll_attention_inputs(a, sh, qkv, s.g, s.owns_new, tag)) goto done;
                 LAYER_MARK(2);
                 // Scores in base-2 units: s2 = (q . k) * scale * log2(e), so p = exp2(s2 - max).
                 const float scale2 = a.layer[l].scale * kLog2e;
@@ -788,7 +797,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                         max(static_cast<int64_t>(0), min64(static_cast<int64_t>(nb) * kStepAttnRows, s.cached_end - r0)));
                     const bool with_new = j + nb == s.n_att && s.owns_new;
                     const int rows = cached + (with_new ? 1 : 0);
-                    if (!acquire_batch(a, sh, k, nb)) goto done;
+                    // The first batch needs no barrier of its own (the poll's barrier
+                    // precedes it; an abort is read after the score barrier below).
+                    if (j == 0)
+                        wait_tiles(a, sh, k, nb);
+                    else if (!acquire_batch(a, sh, k, nb))
+                        goto done;
                     auto tile_base = [&](int gi) {
                         return reinterpret_cast<const float*>(
                             ring + static_cast<size_t>((k + gi / kStepAttnRows) % kStepSlots) * kStepSlotBytes);
@@ -839,6 +853,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                         if (lane == 0) sh.att.wm[warp][h] = mb[h];
                     }
                     consumer_sync();
+                    if (sh.abort) goto done;
                     // New running max (uniform over the CTA); rescale earlier batches.
                     float mnew[kGroup];
 #pragma unroll
