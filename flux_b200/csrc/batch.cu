@@ -4,20 +4,23 @@
 // configuration, where each GPU owns its own sequences and replicas of the
 // weights and nothing crosses GPUs.
 //
-// Per layer (12-13 launches): RMSNorm rows -> QKV split-K GEMM (+ its
-// reduction) -> RoPE + cache write at each sequence's own position ->
-// compact split-K attention over each sequence's valid length (attention.cu,
-// chunks + merge) -> o_proj GEMM -> reduction + residual -> RMSNorm ->
-// gate/up GEMM -> reduction + SwiGLU -> down GEMM -> reduction + residual;
-// then the final norm, the tied LM head GEMM and a per-row greedy argmax that
-// advances each sequence's token and position.
+// Per layer (10 launches, programmatic dependent launches in the graph):
+// QKV split-K GEMM -> split-K sum + RoPE + cache write at each sequence's own
+// position -> compact split-K attention over each sequence's valid length
+// (attention.cu, chunks + merge) -> o_proj GEMM -> split-K sum + residual +
+// RMSNorm -> gate/up GEMM -> split-K sum + SwiGLU -> down GEMM -> split-K sum
+// + residual + the next layer's RMSNorm; then the tied LM head GEMM over all
+// rows and a per-row greedy argmax that advances each sequence's token and
+// position.  The batch runs as two lanes (halves) on two streams forked and
+// joined inside the graph, so one half's latency-bound projections and
+// reductions overlap the other half's HBM-bound attention.
 //
-// The projections are skinny GEMMs (M = B <= 64 rows of activations against
-// the weight rows): 64 x 64 output tiles over a slice of K, so that small N
-// still spreads over every SM, then a reduction of the K slices in a fixed
-// order (one thread per output, four loads in flight) that also applies the
-// residual add or the SwiGLU -- deterministic, FP32, and a row's result does
-// not depend on the other rows of the batch.
+// The projections are skinny GEMMs (M <= 64 rows of activations against the
+// weight rows) on tcgen05 tensor cores (tc_gemm.cu) or, optionally, SIMT
+// 64 x 64 tiles, over a slice of K so that small N still spreads over the
+// SMs; the K slices are summed in a fixed order by the following fused
+// kernel -- deterministic, FP32, and a row's result does not depend on the
+// other rows of the batch.
 #include "attention.cuh"
 #include "common.cuh"
 #include "tc_gemm.cuh"
@@ -339,37 +342,55 @@ GemmPlan plan_gemm(int N, int K, int sms, bool tensor_cores) {
 
 using namespace fx;
 
+// One lane: a contiguous range of the batch's sequences with its own
+// activations, split-K partials and attention workspace.  With two lanes the
+// halves of the batch run their layer chains on two streams inside the
+// graph, so one half's latency-bound projections and reductions overlap the
+// other half's HBM-bound attention; they join before the LM head.
+struct BatchLane {
+    int row0 = 0, rows = 0;
+    float *h = nullptr, *h2 = nullptr, *qkv = nullptr, *q = nullptr;
+    float *norm = nullptr, *attn = nullptr, *act = nullptr;  // 64 rows each (rows >= `rows` stay zero)
+    float *partials = nullptr, *attn_ws = nullptr;
+    CUtensorMap x_norm, x_attn, x_act;
+};
+
 struct fx_batch {
     fx_model_desc model{};
     int64_t batch = 0, capacity = 0, gen_cap = 0, vocab = 0;
     int sms = 0;
     int64_t host_max_position = 0;  // host mirror of max(positions): refuses steps past capacity
     bool pending = false;
-    cudaStream_t capture_stream = nullptr;
-    cudaEvent_t done = nullptr;
+    cudaStream_t capture_stream = nullptr, lane_stream = nullptr;
+    cudaEvent_t done = nullptr, fork = nullptr, join = nullptr;
     cudaGraphExec_t exec = nullptr;
     cudaGraph_t graph = nullptr;
     // owned device memory
     int64_t *tokens = nullptr, *positions = nullptr, *lengths = nullptr, *generated = nullptr, *step = nullptr;
     float *logits = nullptr, *key_cache = nullptr, *value_cache = nullptr;
-    float *h = nullptr, *h2 = nullptr, *norm = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
-    float *partials = nullptr, *attn_ws = nullptr;
+    float *activations = nullptr, *partials = nullptr, *attn_ws = nullptr;
+    float* norm_all = nullptr;  // the final norm of every row (LM head input), max(batch, 64) rows
     unsigned* error = nullptr;
+    int lanes = 1;
+    int priority_low = 0, priority_high = 0;  // the device's stream priority range
+    BatchLane lane[2];
     GemmPlan qkv_plan, o_plan, gu_plan, down_plan, lm_plan;
     // Projections on tcgen05 tensor cores (3xTF32) unless FLUX_B200_BATCH_GEMM=simt.
     bool tensor_cores = true;
     fx::TcModelWeights tc;
-    CUtensorMap x_norm, x_attn, x_act;  // activation maps, 64 rows (rows >= batch stay zero)
+    CUtensorMap x_norm_all;
     size_t layer_stride() const { return static_cast<size_t>(batch) * kKVHeads * capacity * kHeadDim; }
+    size_t sequence_stride() const { return static_cast<size_t>(kKVHeads) * capacity * kHeadDim; }
 };
 
 namespace fx {
 namespace {
 
-fx_status gemm(fx_batch* r, const float* x, const float* w, int N, int K, const GemmPlan& p, float* direct_out,
-               cudaStream_t s, const TcWeight* tw = nullptr, const CUtensorMap* xmap = nullptr) {
-    const int M = static_cast<int>(r->batch);
-    float* out = p.splits == 1 && direct_out != nullptr ? direct_out : r->partials;
+// A projection of M activation rows: split-K partials into `partials`, or
+// straight into `direct_out` when there is one split.
+fx_status gemm(fx_batch* r, int M, const float* x, const float* w, int N, int K, const GemmPlan& p, float* direct_out,
+               float* partials, cudaStream_t s, const TcWeight* tw = nullptr, const CUtensorMap* xmap = nullptr) {
+    float* out = p.splits == 1 && direct_out != nullptr ? direct_out : partials;
     if (r->tensor_cores) {
         TcGemmArgs a = tc_args(*tw, *xmap, out, nullptr, reinterpret_cast<int*>(r->error), M, p.k_per_split);
         return launch_tc_gemm(a, 64, p.splits, s, true);
@@ -379,76 +400,114 @@ fx_status gemm(fx_batch* r, const float* x, const float* w, int N, int K, const 
                             out, M, N, K, p.k_per_split);
 }
 
-fx_status reduce(fx_batch* r, const GemmPlan& p, int N, const float* residual, float* out, cudaStream_t s) {
-    const int M = static_cast<int>(r->batch);
+fx_status reduce(int M, const GemmPlan& p, int N, const float* partials, const float* residual, float* out,
+                 cudaStream_t s) {
     const int64_t n = static_cast<int64_t>(M) * N;
     return launch_dependent(reduce_splits_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s,
-                            "launching a split-K reduction", static_cast<const float*>(r->partials), p.splits, M, N,
-                            residual, out);
+                            "launching a split-K reduction", partials, p.splits, M, N, residual, out);
 }
 
-fx_status run_step(fx_batch* r, cudaStream_t s) {
+// Embedding and the 30 layers for the lane's sequences; the last layer's
+// final norm goes to the lane's rows of norm_all.
+fx_status run_lane(fx_batch* r, BatchLane& ln, cudaStream_t s) {
     const fx_model_desc& m = r->model;
-    const int B = static_cast<int>(r->batch);
+    const int B = ln.rows;
+    int64_t* tokens = r->tokens + ln.row0;
+    int64_t* positions = r->positions + ln.row0;
+    int64_t* lengths = r->lengths + ln.row0;
     fx_status st;
     if ((st = launch_dependent(embed_rows_kernel, dim3(B), dim3(kHidden), 0, s, "launching the embedding gather",
-                               static_cast<const int64_t*>(r->tokens), m.embedding, r->vocab, r->h, m.input_norm[0],
-                               m.epsilon, r->norm)) != FX_OK)
+                               static_cast<const int64_t*>(tokens), m.embedding, r->vocab, ln.h, m.input_norm[0],
+                               m.epsilon, ln.norm)) != FX_OK)
         return st;
-    auto residual_norm = [&](const GemmPlan& p, const float* residual, float* h_out, const float* w) {
+    auto residual_norm = [&](const GemmPlan& p, const float* residual, float* h_out, const float* w, float* norm_out) {
         return launch_dependent(reduce_residual_norm_kernel, dim3(B), dim3(kHidden), 0, s,
                                 "launching the split-K sum / residual / RMSNorm rows",
-                                static_cast<const float*>(r->partials), p.splits, B, residual, h_out, w, m.epsilon,
-                                r->norm);
+                                static_cast<const float*>(ln.partials), p.splits, B, residual, h_out, w, m.epsilon,
+                                norm_out);
     };
     for (int l = 0; l < kLayers; ++l) {
-        float* kc = r->key_cache + l * r->layer_stride();
-        float* vc = r->value_cache + l * r->layer_stride();
-        if ((st = gemm(r, r->norm, m.packed_qkv[l], kQKV, kHidden, r->qkv_plan, r->qkv, s, &r->tc.qkv[l], &r->x_norm)) != FX_OK) return st;
+        float* kc = r->key_cache + l * r->layer_stride() + ln.row0 * r->sequence_stride();
+        float* vc = r->value_cache + l * r->layer_stride() + ln.row0 * r->sequence_stride();
+        if ((st = gemm(r, B, ln.norm, m.packed_qkv[l], kQKV, kHidden, r->qkv_plan, ln.qkv, ln.partials, s, &r->tc.qkv[l],
+                       &ln.x_norm)) != FX_OK)
+            return st;
         {
             const int64_t n = static_cast<int64_t>(B) * ((kQHeads + kKVHeads) * (kHeadDim / 2) + kKVHeads * kHeadDim);
-            const float* src = r->qkv_plan.splits > 1 ? r->partials : r->qkv;
+            const float* src = r->qkv_plan.splits > 1 ? ln.partials : ln.qkv;
             if ((st = launch_dependent(rope_cache_rows_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s,
                                        "launching the batched QKV sum / RoPE / cache write", src, r->qkv_plan.splits,
-                                       static_cast<const int64_t*>(r->positions), m.rope_cos, m.rope_sin, kc, vc, r->q,
-                                       r->lengths, r->capacity, B, r->error)) != FX_OK)
+                                       static_cast<const int64_t*>(positions), m.rope_cos, m.rope_sin, kc, vc, ln.q,
+                                       lengths, r->capacity, B, r->error)) != FX_OK)
                 return st;
         }
         CompactAttention a{};
-        a.q = r->q;
+        a.q = ln.q;
         a.k = kc;
         a.v = vc;
-        a.lengths = r->lengths;
+        a.lengths = lengths;
         a.length_stride = 1;
-        a.out = r->attn;
-        a.ws = r->attn_ws;
+        a.out = ln.attn;
+        a.ws = ln.attn_ws;
         a.error = r->error;
         a.scale = m.attention_scale[l];
         a.batch = B;
         a.cap = r->capacity;
         a.chunks = (r->capacity + kCompactChunk - 1) / kCompactChunk;
         a.chunk_rows = kCompactChunk;
-        if ((st = launch_compact_attention(a, s, true)) != FX_OK) return st;
-        if ((st = gemm(r, r->attn, m.o_proj[l], kHidden, kHidden, r->o_plan, nullptr, s, &r->tc.o[l], &r->x_attn)) != FX_OK) return st;
-        if ((st = residual_norm(r->o_plan, r->h, r->h2, m.post_norm[l])) != FX_OK) return st;
-        if ((st = gemm(r, r->norm, m.gate_up[l], kGateUp, kHidden, r->gu_plan, nullptr, s, &r->tc.gate_up[l], &r->x_norm)) != FX_OK) return st;
+        {
+            // HBM-bound attention yields the SMs to the other lane's chain
+            LaunchPriorityScope low(r->priority_low);
+            if ((st = launch_compact_attention(a, s, true)) != FX_OK) return st;
+        }
+        if ((st = gemm(r, B, ln.attn, m.o_proj[l], kHidden, kHidden, r->o_plan, nullptr, ln.partials, s, &r->tc.o[l],
+                       &ln.x_attn)) != FX_OK)
+            return st;
+        if ((st = residual_norm(r->o_plan, ln.h, ln.h2, m.post_norm[l], ln.norm)) != FX_OK) return st;
+        if ((st = gemm(r, B, ln.norm, m.gate_up[l], kGateUp, kHidden, r->gu_plan, nullptr, ln.partials, s,
+                       &r->tc.gate_up[l], &ln.x_norm)) != FX_OK)
+            return st;
         {
             const int64_t n = static_cast<int64_t>(B) * kInter;
             if ((st = launch_dependent(reduce_swiglu_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s,
-                                       "launching the batched SwiGLU", static_cast<const float*>(r->partials),
-                                       r->gu_plan.splits, B, r->act)) != FX_OK)
+                                       "launching the batched SwiGLU", static_cast<const float*>(ln.partials),
+                                       r->gu_plan.splits, B, ln.act)) != FX_OK)
                 return st;
         }
-        if ((st = gemm(r, r->act, m.down[l], kHidden, kInter, r->down_plan, nullptr, s, &r->tc.down[l], &r->x_act)) != FX_OK) return st;
+        if ((st = gemm(r, B, ln.act, m.down[l], kHidden, kInter, r->down_plan, nullptr, ln.partials, s, &r->tc.down[l],
+                       &ln.x_act)) != FX_OK)
+            return st;
         // h = h' + down, then the next layer's input norm (the final norm after the last layer)
-        if ((st = residual_norm(r->down_plan, r->h2, r->h, l + 1 < kLayers ? m.input_norm[l + 1] : m.final_norm)) !=
-            FX_OK)
+        const bool last = l + 1 == kLayers;
+        if ((st = residual_norm(r->down_plan, ln.h2, ln.h, last ? m.final_norm : m.input_norm[l + 1],
+                                last ? r->norm_all + static_cast<size_t>(ln.row0) * kHidden : ln.norm)) != FX_OK)
             return st;
     }
-    if ((st = gemm(r, r->norm, m.lm_head, static_cast<int>(r->vocab), kHidden, r->lm_plan, r->logits, s, &r->tc.lm_head,
-                    &r->x_norm)) != FX_OK)
+    return FX_OK;
+}
+
+fx_status run_step(fx_batch* r, cudaStream_t s) {
+    const fx_model_desc& m = r->model;
+    const int B = static_cast<int>(r->batch);
+    fx_status st;
+    if (r->lanes > 1) {
+        // the latency-bound projections and reductions run at high priority,
+        // the attention chunks at low (node priorities of the graph)
+        LaunchPriorityScope high(r->priority_high);
+        FX_CUDA_TRY(cudaEventRecord(r->fork, s), "forking the batched lanes");
+        FX_CUDA_TRY(cudaStreamWaitEvent(r->lane_stream, r->fork, 0), "forking the batched lanes");
+        if ((st = run_lane(r, r->lane[1], r->lane_stream)) != FX_OK) return st;
+        if ((st = run_lane(r, r->lane[0], s)) != FX_OK) return st;
+        FX_CUDA_TRY(cudaEventRecord(r->join, r->lane_stream), "joining the batched lanes");
+        FX_CUDA_TRY(cudaStreamWaitEvent(s, r->join, 0), "joining the batched lanes");
+    } else if ((st = run_lane(r, r->lane[0], s)) != FX_OK) {
         return st;
-    if (r->lm_plan.splits > 1 && (st = reduce(r, r->lm_plan, static_cast<int>(r->vocab), nullptr, r->logits, s)) != FX_OK)
+    }
+    if ((st = gemm(r, B, r->norm_all, m.lm_head, static_cast<int>(r->vocab), kHidden, r->lm_plan, r->logits,
+                   r->partials, s, &r->tc.lm_head, &r->x_norm_all)) != FX_OK)
+        return st;
+    if (r->lm_plan.splits > 1 &&
+        (st = reduce(B, r->lm_plan, static_cast<int>(r->vocab), r->partials, nullptr, r->logits, s)) != FX_OK)
         return st;
     if ((st = launch_dependent(greedy_rows_kernel, dim3(B), dim3(1024), 0, s, "launching the batched greedy update",
                                static_cast<const float*>(r->logits), r->vocab, r->tokens, r->positions, r->generated,
@@ -474,11 +533,13 @@ void destroy_batch(fx_batch* r) {
     if (r == nullptr) return;
     if (r->exec) cudaGraphExecDestroy(r->exec);
     if (r->graph) cudaGraphDestroy(r->graph);
-    if (r->done) cudaEventDestroy(r->done);
+    for (cudaEvent_t e : {r->done, r->fork, r->join})
+        if (e) cudaEventDestroy(e);
     if (r->capture_stream) cudaStreamDestroy(r->capture_stream);
+    if (r->lane_stream) cudaStreamDestroy(r->lane_stream);
     for (void* p : {static_cast<void*>(r->tokens), static_cast<void*>(r->logits), static_cast<void*>(r->key_cache),
-                    static_cast<void*>(r->value_cache), static_cast<void*>(r->h), static_cast<void*>(r->partials),
-                    static_cast<void*>(r->attn_ws)})
+                    static_cast<void*>(r->value_cache), static_cast<void*>(r->activations),
+                    static_cast<void*>(r->partials), static_cast<void*>(r->attn_ws)})
         cudaFree(p);
     tc_weights_release(&r->tc);
     delete r;
@@ -486,6 +547,7 @@ void destroy_batch(fx_batch* r) {
 
 fx_status create_batch(fx_batch* r, cudaStream_t stream) {
     FX_CUDA_TRY(cudaDeviceGetAttribute(&r->sms, cudaDevAttrMultiProcessorCount, r->model.device), "querying SM count");
+    FX_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&r->priority_low, &r->priority_high), "querying stream priorities");
     const int64_t B = r->batch;
     // state: tokens, positions, lengths, step, generated (one allocation)
     const size_t state_words = 3 * B + 1 + B * r->gen_cap;
@@ -499,58 +561,104 @@ fx_status create_batch(fx_batch* r, cudaStream_t stream) {
     const size_t cache = static_cast<size_t>(kLayers) * r->layer_stride() * sizeof(float);
     FX_CUDA_TRY(cudaMalloc(&r->key_cache, cache), "allocating the batched K cache");
     FX_CUDA_TRY(cudaMalloc(&r->value_cache, cache), "allocating the batched V cache");
-    // activations; the projection inputs (norm, attn, act) hold 64 rows so
-    // the tensor-core tiles never read past them (rows >= batch stay zero)
     const char* mode = std::getenv("FLUX_B200_BATCH_GEMM");
     r->tensor_cores = !(mode != nullptr && std::strcmp(mode, "simt") == 0);
+    // Lanes (FLUX_B200_BATCH_LANES=1 runs the whole batch as one chain).  The
+    // split-K plans depend only on the configured lane count, never on the
+    // batch size, so a sequence's result is the same in any batch.
+    const char* lanes_env = std::getenv("FLUX_B200_BATCH_LANES");
+    const int lanes_cfg = lanes_env != nullptr && std::strcmp(lanes_env, "1") == 0 ? 1 : 2;
+    r->lanes = static_cast<int>(std::min<int64_t>(lanes_cfg, B));
+    r->lane[0].row0 = 0;
+    r->lane[0].rows = static_cast<int>((B + r->lanes - 1) / r->lanes);
+    r->lane[1].row0 = r->lane[0].rows;
+    r->lane[1].rows = static_cast<int>(B - r->lane[0].rows);
+    const bool tc = r->tensor_cores;
+    const int plan_sms = std::max(1, r->sms / lanes_cfg);
+    r->qkv_plan = plan_gemm(kQKV, kHidden, plan_sms, tc);
+    r->o_plan = plan_gemm(kHidden, kHidden, plan_sms, tc);
+    r->gu_plan = plan_gemm(kGateUp, kHidden, plan_sms, tc);
+    r->down_plan = plan_gemm(kHidden, kInter, plan_sms, tc);
+    r->lm_plan = plan_gemm(static_cast<int>(r->vocab), kHidden, r->sms, tc);
+    // Activations per lane; the projection inputs (norm, attn, act) hold 64
+    // rows so the tensor-core tiles never read past them (rows past the
+    // lane's stay zero).  Then norm_all, max(batch, 64) rows.
     const int64_t R = std::max<int64_t>(B, 64);
-    const size_t act_floats = static_cast<size_t>(B) * (2 * kHidden + kQKV + kHidden) +
-                              static_cast<size_t>(R) * (2 * kHidden + kInter);
-    FX_CUDA_TRY(cudaMalloc(&r->h, act_floats * sizeof(float)), "allocating batched activations");
-    FX_CUDA_TRY(cudaMemsetAsync(r->h, 0, act_floats * sizeof(float), stream), "clearing batched activations");
-    r->h2 = r->h + B * kHidden;
-    r->qkv = r->h2 + B * kHidden;
-    r->q = r->qkv + B * kQKV;
-    r->norm = r->q + B * kHidden;
-    r->attn = r->norm + R * kHidden;
-    r->act = r->attn + R * kHidden;
-    if (r->tensor_cores) {
+    auto lane_act = [](int64_t rows) {
+        return static_cast<size_t>(rows) * (3 * kHidden + kQKV) + static_cast<size_t>(64) * (2 * kHidden + kInter);
+    };
+    size_t act_floats = static_cast<size_t>(R) * kHidden;
+    for (int i = 0; i < r->lanes; ++i) act_floats += lane_act(r->lane[i].rows);
+    FX_CUDA_TRY(cudaMalloc(&r->activations, act_floats * sizeof(float)), "allocating batched activations");
+    FX_CUDA_TRY(cudaMemsetAsync(r->activations, 0, act_floats * sizeof(float), stream), "clearing batched activations");
+    // split-K partials per lane (gate/up always reduces through them: SwiGLU
+    // epilogue); the LM head's, if split, reuse the whole buffer after the join
+    auto lane_partials = [&](int64_t rows) {
+        size_t n = 0;
+        for (const auto& p : {std::pair<const GemmPlan*, int>{&r->qkv_plan, kQKV}, {&r->o_plan, kHidden},
+                              {&r->gu_plan, kGateUp}, {&r->down_plan, kHidden}})
+            if (p.first->splits > 1 || p.second == kGateUp)
+                n = std::max(n, static_cast<size_t>(p.first->splits) * rows * p.second);
+        return (n + 63) / 64 * 64;
+    };
+    size_t partial_floats = 0;
+    for (int i = 0; i < r->lanes; ++i) partial_floats += lane_partials(r->lane[i].rows);
+    if (r->lm_plan.splits > 1)
+        partial_floats = std::max(partial_floats, static_cast<size_t>(r->lm_plan.splits) * B * r->vocab);
+    FX_CUDA_TRY(cudaMalloc(&r->partials, partial_floats * sizeof(float)), "allocating split-K partials");
+    // attention partials per lane (the merge runs as its own kernel: with
+    // thousands of chunk CTAs per layer the in-kernel last-CTA merge measured
+    // slower, 3.34 vs 3.12 ms per step)
+    auto lane_ws = [&](int64_t rows) {
+        return static_cast<size_t>((compact_attention_workspace(rows, r->capacity) + 63) / 64 * 64);
+    };
+    size_t attn_floats = 0;
+    for (int i = 0; i < r->lanes; ++i) attn_floats += lane_ws(r->lane[i].rows);
+    FX_CUDA_TRY(cudaMalloc(&r->attn_ws, attn_floats * sizeof(float)), "allocating the attention workspace");
+    FX_CUDA_TRY(cudaMemsetAsync(r->attn_ws, 0, attn_floats * sizeof(float), stream), "clearing the attention workspace");
+    r->norm_all = r->activations;
+    float* act = r->activations + static_cast<size_t>(R) * kHidden;
+    float* part = r->partials;
+    float* ws = r->attn_ws;
+    for (int i = 0; i < r->lanes; ++i) {
+        BatchLane& ln = r->lane[i];
+        const int64_t n = ln.rows;
+        ln.h = act;
+        ln.h2 = ln.h + n * kHidden;
+        ln.qkv = ln.h2 + n * kHidden;
+        ln.q = ln.qkv + n * kQKV;
+        ln.norm = ln.q + n * kHidden;
+        ln.attn = ln.norm + 64 * kHidden;
+        ln.act = ln.attn + 64 * kHidden;
+        act += lane_act(n);
+        ln.partials = part;
+        part += lane_partials(n);
+        ln.attn_ws = ws;
+        ws += lane_ws(n);
+    }
+    if (tc) {
         fx_status st0 = tc_weights_create(r->model, true, &r->tc, stream);
         if (st0 != FX_OK) return st0;
-        if ((st0 = tc_encode_map(&r->x_norm, r->norm, R, kHidden, 64, "the batched norm rows")) != FX_OK) return st0;
-        if ((st0 = tc_encode_map(&r->x_attn, r->attn, R, kHidden, 64, "the batched attention rows")) != FX_OK) return st0;
-        if ((st0 = tc_encode_map(&r->x_act, r->act, R, kInter, 64, "the batched SwiGLU rows")) != FX_OK) return st0;
+        if ((st0 = tc_encode_map(&r->x_norm_all, r->norm_all, R, kHidden, 64, "the batched final-norm rows")) != FX_OK)
+            return st0;
+        for (int i = 0; i < r->lanes; ++i) {
+            BatchLane& ln = r->lane[i];
+            if ((st0 = tc_encode_map(&ln.x_norm, ln.norm, 64, kHidden, 64, "the batched norm rows")) != FX_OK) return st0;
+            if ((st0 = tc_encode_map(&ln.x_attn, ln.attn, 64, kHidden, 64, "the batched attention rows")) != FX_OK)
+                return st0;
+            if ((st0 = tc_encode_map(&ln.x_act, ln.act, 64, kInter, 64, "the batched SwiGLU rows")) != FX_OK) return st0;
+        }
     }
-    const bool tc = r->tensor_cores;
-    r->qkv_plan = plan_gemm(kQKV, kHidden, r->sms, tc);
-    r->o_plan = plan_gemm(kHidden, kHidden, r->sms, tc);
-    r->gu_plan = plan_gemm(kGateUp, kHidden, r->sms, tc);
-    r->down_plan = plan_gemm(kHidden, kInter, r->sms, tc);
-    r->lm_plan = plan_gemm(static_cast<int>(r->vocab), kHidden, r->sms, tc);
-    size_t partial_floats = 0;
-    const std::pair<const GemmPlan*, int> plans[] = {{&r->qkv_plan, kQKV}, {&r->o_plan, kHidden},
-                                                     {&r->gu_plan, kGateUp}, {&r->down_plan, kHidden},
-                                                     {&r->lm_plan, static_cast<int>(r->vocab)}};
-    for (const auto& p : plans)
-        if (p.first->splits > 1)
-            partial_floats = std::max(partial_floats, static_cast<size_t>(p.first->splits) * B * p.second);
-    // gate/up always reduces through the partial buffer (SwiGLU epilogue)
-    partial_floats = std::max(partial_floats, static_cast<size_t>(r->gu_plan.splits) * B * kGateUp);
-    FX_CUDA_TRY(cudaMalloc(&r->partials, partial_floats * sizeof(float)), "allocating split-K partials");
-    // attention partials (the merge runs as its own kernel: with thousands of
-    // chunk CTAs per layer the in-kernel last-CTA merge measured slower,
-    // 3.34 vs 3.12 ms per step)
-    const size_t attn_floats = compact_attention_workspace(B, r->capacity);
-    FX_CUDA_TRY(cudaMalloc(&r->attn_ws, attn_floats * sizeof(float)),
-                "allocating the attention workspace");
-    FX_CUDA_TRY(cudaMemsetAsync(r->attn_ws, 0, attn_floats * sizeof(float), stream), "clearing the attention workspace");
     FX_CUDA_TRY(cudaMemsetAsync(r->tokens, 0, state_words * sizeof(int64_t) + 256, stream), "clearing batched state");
     FX_CUDA_TRY(cudaMemsetAsync(r->key_cache, 0, cache, stream), "clearing the batched K cache");
     FX_CUDA_TRY(cudaMemsetAsync(r->value_cache, 0, cache, stream), "clearing the batched V cache");
     FX_CUDA_TRY(cudaMemsetAsync(r->logits, 0, static_cast<size_t>(B) * r->vocab * sizeof(float), stream),
                 "clearing batched logits");
     FX_CUDA_TRY(cudaStreamCreateWithFlags(&r->capture_stream, cudaStreamNonBlocking), "creating the capture stream");
+    FX_CUDA_TRY(cudaStreamCreateWithFlags(&r->lane_stream, cudaStreamNonBlocking), "creating the lane stream");
     FX_CUDA_TRY(cudaEventCreateWithFlags(&r->done, cudaEventDisableTiming), "creating the completion event");
+    FX_CUDA_TRY(cudaEventCreateWithFlags(&r->fork, cudaEventDisableTiming), "creating the lane fork event");
+    FX_CUDA_TRY(cudaEventCreateWithFlags(&r->join, cudaEventDisableTiming), "creating the lane join event");
     FX_CUDA_TRY(cudaStreamSynchronize(stream), "initialising the batched runtime");
     // Load every kernel once outside capture (function attributes, modules),
     // then restore the cleared state and capture one step.
@@ -571,7 +679,8 @@ fx_status create_batch(fx_batch* r, cudaStream_t stream) {
     }
     FX_CUDA_TRY(end, "ending capture");
     r->graph = graph;
-    FX_CUDA_TRY(cudaGraphInstantiate(&r->exec, r->graph, 0), "instantiating the batched graph");
+    FX_CUDA_TRY(cudaGraphInstantiate(&r->exec, r->graph, cudaGraphInstantiateFlagUseNodePriority),
+                "instantiating the batched graph");
     FX_CUDA_TRY(cudaStreamSynchronize(r->capture_stream), "finalising the batched runtime");
     return FX_OK;
 }
@@ -713,7 +822,7 @@ extern "C" fx_status fx_batch_get_buffers(const fx_batch* r, fx_batch_buffers* o
     out->batch = r->batch;
     out->capacity = r->capacity;
     out->generated_capacity = r->gen_cap;
-    out->kernels_per_step = 1 + kLayers * 10 + 3 + (r->lm_plan.splits > 1 ? 1 : 0);
+    out->kernels_per_step = r->lanes * (1 + kLayers * 10) + 3 + (r->lm_plan.splits > 1 ? 1 : 0);
     return FX_OK;
 }
 

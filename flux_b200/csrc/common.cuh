@@ -62,6 +62,20 @@ int* decode_error_word(fx_decode* runtime);
 // early: measured, an early trigger slowed the batched step.
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Scheduling priority given to this thread's launch_dependent() launches
+// (cudaLaunchAttributePriority, lower is more urgent; a captured launch keeps
+// it as its graph node's priority), none by default.
+constexpr int kNoLaunchPriority = 1 << 30;
+inline int& launch_priority() {
+    static thread_local int priority = kNoLaunchPriority;
+    return priority;
+}
+struct LaunchPriorityScope {
+    int saved;
+    explicit LaunchPriorityScope(int priority) : saved(launch_priority()) { launch_priority() = priority; }
+    ~LaunchPriorityScope() { launch_priority() = saved; }
+};
+
 template <typename... KArgs, typename... Args>
 fx_status launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                            const char* what, Args&&... args) {
@@ -70,11 +84,16 @@ fx_status launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size
     config.blockDim = block;
     config.dynamicSmemBytes = smem;
     config.stream = stream;
-    cudaLaunchAttribute attribute{};
-    attribute.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attribute.val.programmaticStreamSerializationAllowed = 1;
-    config.attrs = &attribute;
+    cudaLaunchAttribute attributes[2]{};
+    attributes[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attributes[0].val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = attributes;
     config.numAttrs = 1;
+    if (launch_priority() != kNoLaunchPriority) {
+        attributes[1].id = cudaLaunchAttributePriority;
+        attributes[1].val.priority = launch_priority();
+        config.numAttrs = 2;
+    }
     FX_CUDA_TRY(cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...), what);
     return FX_OK;
 }

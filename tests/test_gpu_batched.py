@@ -116,3 +116,33 @@ def test_batched_capacity_exhausted(model_gpu):
     runtime.check()
     with pytest.raises(RuntimeError, match="exhausted"):
         runtime.step(1)
+
+
+def test_two_lanes_match_one_lane(model_gpu, monkeypatch):
+    """The batch split into two lanes on two streams (the default) against
+    the whole batch as one chain (FLUX_B200_BATCH_LANES=1): the split-K plans
+    differ, so the logits agree to rounding; each run's tokens are the argmax
+    of its own logits."""
+    from flux_b200.runtime import NativeSmolLM2BatchedDecode
+    rng = np.random.default_rng(5)
+    lengths = [int(x) for x in rng.integers(1, 500, size=7)]
+    capacity = 512
+    config = hf.smollm2_config()
+    caches = [hf.synthetic_cache(config, n, seed=2000 + i, std=0.5) for i, n in enumerate(lengths)]
+    runs = []
+    for lanes in ("1", "2"):
+        monkeypatch.setenv("FLUX_B200_BATCH_LANES", lanes)
+        runtime = NativeSmolLM2BatchedDecode(model_gpu, len(lengths), capacity)
+        for i, n in enumerate(lengths):
+            keys, values = caches[i]
+            runtime.load(i, (101 * i + 3) % 49152, [k.cuda() for k in keys], [v.cuda() for v in values], n)
+        logits = [runtime.step(1).clone() for _ in range(3)]
+        runtime.check()
+        runs.append((logits, runtime.generated_tokens()[:, :3].clone(), runtime.kernels_per_step))
+    (one, gen_one, k_one), (two, gen_two, k_two) = runs
+    for a, b in zip(one, two):
+        torch.testing.assert_close(b, a, rtol=2e-5, atol=2e-5)
+    for logits, gen in ((one, gen_one), (two, gen_two)):
+        for step, row in enumerate(logits):
+            assert torch.equal(gen[:, step], row.argmax(dim=-1).to(gen.dtype))
+    assert k_two == k_one + 1 + 30 * 10
