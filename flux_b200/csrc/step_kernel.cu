@@ -54,7 +54,7 @@ constexpr int kBatchTiles = 4;                           // attention tiles held
 constexpr int kBatchRows = kBatchTiles * kStepAttnRows + 4;  // + the new row, padded (220)
 constexpr int kRowGroups = kConsumerWarps * 8;           // 4-lane score groups (120)
 constexpr int kRowSlots = (kBatchTiles * kStepAttnRows + 1 + kRowGroups - 1) / kRowGroups;  // rows per group per batch (2)
-constexpr int kPvSplits = kStepConsumers / (kGroup * kHeadDim / 4);  // P.V row splits (10)
+constexpr int kPvSplits = kStepConsumers / (kHeadDim / 4);  // P.V row splits (30), two per warp
 constexpr float kLog2e = 1.4426950408889634f;            // log2(e): scores kept in base-2 units
 constexpr float kLn2 = 0.6931471805599453f;              // ln(2)
 constexpr int kMaxOBlocks = 2;                           // needs >= 24 chunks per kv head
@@ -183,8 +183,8 @@ __device__ __forceinline__ int64_t min64(int64_t x, int64_t y) { return x < y ? 
 struct AttnScratch {
     alignas(16) float p[kGroup][kBatchRows];
     float wm[kConsumerWarps][kGroup];
-    alignas(16) float o[kPvSplits][kGroup][kHeadDim];
-    float l[kPvSplits][kGroup];
+    alignas(16) float o[kConsumerWarps][kGroup][kHeadDim];  // per warp (its two row splits summed)
+    float l[kConsumerWarps][kGroup];
 };
 
 struct Shared {
@@ -779,10 +779,16 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
                         qr[h][j] = reinterpret_cast<const float4*>(sh.qs + h * kHeadDim)[l4 + 4 * ((j + gl) & 3)];
-                // P.V threads: (4-dim quad, head, row split).
-                const int pq = tid & 15, ph = (tid >> 4) % kGroup, psplit = tid / (kGroup * 16);
-                float4 pacc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                float plsum = 0.0f;
+                // P.V threads: (4-dim quad, row split), all 3 heads, so every V
+                // row is read from shared memory once.
+                const int pq = tid & 15, psplit = tid >> 4;
+                float4 pacc[kGroup];
+                float plsum[kGroup];
+#pragma unroll
+                for (int h = 0; h < kGroup; ++h) {
+                    pacc[h] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    plsum[h] = 0.0f;
+                }
                 float mrun[kGroup];
 #pragma unroll
                 for (int h = 0; h < kGroup; ++h) mrun[h] = -INFINITY;
@@ -863,15 +869,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                         for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
                         mnew[h] = fmaxf(mrun[h], mx);
                     }
-                    {
-                        const float mo = ph == 0 ? mrun[0] : (ph == 1 ? mrun[1] : mrun[2]);
-                        const float mn = ph == 0 ? mnew[0] : (ph == 1 ? mnew[1] : mnew[2]);
-                        const float f = exp2f(mo - mn);  // first batch: mrun = -inf -> 0
-                        pacc.x *= f;
-                        pacc.y *= f;
-                        pacc.z *= f;
-                        pacc.w *= f;
-                        plsum *= f;
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) {
+                        const float f = exp2f(mrun[h] - mnew[h]);  // first batch: mrun = -inf -> 0
+                        pacc[h].x *= f;
+                        pacc[h].y *= f;
+                        pacc[h].z *= f;
+                        pacc[h].w *= f;
+                        plsum[h] *= f;
                     }
 #pragma unroll
                     for (int h = 0; h < kGroup; ++h) mrun[h] = mnew[h];
@@ -880,10 +885,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     for (int h = 0; h < kGroup; ++h)
                         for (int r = tid; r < rows; r += kStepConsumers) sh.att.p[h][r] = exp2f(sh.att.p[h][r] - mrun[h]);
                     consumer_sync();
-                    // P.V: rows psplit, psplit + 10, ... of the batch, tile by tile.
+                    // P.V: rows psplit, psplit + 30, ... of the batch, tile by tile.
                     {
-                        const float* prow = sh.att.p[ph];
-                        float4 acc2 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                        float4 acc2[kGroup];
+#pragma unroll
+                        for (int h = 0; h < kGroup; ++h) acc2[h] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                        auto pv_row = [&](float4 (&acc)[kGroup], int row, const float4 v) {
+#pragma unroll
+                            for (int h = 0; h < kGroup; ++h) {
+                                const float p = sh.att.p[h][row];
+                                acc[h].x = fmaf(p, v.x, acc[h].x);
+                                acc[h].y = fmaf(p, v.y, acc[h].y);
+                                acc[h].z = fmaf(p, v.z, acc[h].z);
+                                acc[h].w = fmaf(p, v.w, acc[h].w);
+                                plsum[h] += p;
+                            }
+                        };
                         for (int b = 0; b < nb; ++b) {
                             const int base = b * kStepAttnRows;
                             const int n = min(kStepAttnRows, cached - base);
@@ -893,42 +910,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                             int rr = psplit - base % kPvSplits;
                             if (rr < 0) rr += kPvSplits;
                             for (; rr + kPvSplits < n; rr += 2 * kPvSplits) {  // two rows per trip
-                                const float p0 = prow[base + rr], p1 = prow[base + rr + kPvSplits];
                                 const float4 v0 = *reinterpret_cast<const float4*>(vb + rr * kHeadDim);
                                 const float4 v1 = *reinterpret_cast<const float4*>(vb + (rr + kPvSplits) * kHeadDim);
-                                pacc.x = fmaf(p0, v0.x, pacc.x);
-                                pacc.y = fmaf(p0, v0.y, pacc.y);
-                                pacc.z = fmaf(p0, v0.z, pacc.z);
-                                pacc.w = fmaf(p0, v0.w, pacc.w);
-                                acc2.x = fmaf(p1, v1.x, acc2.x);
-                                acc2.y = fmaf(p1, v1.y, acc2.y);
-                                acc2.z = fmaf(p1, v1.z, acc2.z);
-                                acc2.w = fmaf(p1, v1.w, acc2.w);
-                                plsum += p0 + p1;
+                                pv_row(pacc, base + rr, v0);
+                                pv_row(acc2, base + rr + kPvSplits, v1);
                             }
-                            if (rr < n) {
-                                const float p0 = prow[base + rr];
-                                const float4 v0 = *reinterpret_cast<const float4*>(vb + rr * kHeadDim);
-                                pacc.x = fmaf(p0, v0.x, pacc.x);
-                                pacc.y = fmaf(p0, v0.y, pacc.y);
-                                pacc.z = fmaf(p0, v0.z, pacc.z);
-                                pacc.w = fmaf(p0, v0.w, pacc.w);
-                                plsum += p0;
-                            }
+                            if (rr < n) pv_row(pacc, base + rr, *reinterpret_cast<const float4*>(vb + rr * kHeadDim));
                         }
-                        if (with_new && cached % kPvSplits == psplit) {
-                            const float p0 = prow[cached];
-                            const float4 v0 = reinterpret_cast<const float4*>(sh.vnew)[pq];
-                            pacc.x = fmaf(p0, v0.x, pacc.x);
-                            pacc.y = fmaf(p0, v0.y, pacc.y);
-                            pacc.z = fmaf(p0, v0.z, pacc.z);
-                            pacc.w = fmaf(p0, v0.w, pacc.w);
-                            plsum += p0;
+                        if (with_new && cached % kPvSplits == psplit)
+                            pv_row(pacc, cached, reinterpret_cast<const float4*>(sh.vnew)[pq]);
+#pragma unroll
+                        for (int h = 0; h < kGroup; ++h) {
+                            pacc[h].x += acc2[h].x;
+                            pacc[h].y += acc2[h].y;
+                            pacc[h].z += acc2[h].z;
+                            pacc[h].w += acc2[h].w;
                         }
-                        pacc.x += acc2.x;
-                        pacc.y += acc2.y;
-                        pacc.z += acc2.z;
-                        pacc.w += acc2.w;
                     }
                     if (j + nb < s.n_att) {
                         release_batch(sh, k, nb);  // the next batch needs the producer to move on
@@ -939,9 +936,18 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     j += nb;
                 } while (j < s.n_att);
                 LAYER_MARK(3);
-                // Sum the row splits.
-                reinterpret_cast<float4*>(sh.att.o[psplit][ph])[pq] = pacc;
-                if (pq == 0) sh.att.l[psplit][ph] = plsum;
+                // Sum the row splits: the warp's two halves by a shuffle, then the
+                // 15 warps' sums.
+#pragma unroll
+                for (int h = 0; h < kGroup; ++h) {
+                    pacc[h].x += __shfl_xor_sync(0xffffffffu, pacc[h].x, 16);
+                    pacc[h].y += __shfl_xor_sync(0xffffffffu, pacc[h].y, 16);
+                    pacc[h].z += __shfl_xor_sync(0xffffffffu, pacc[h].z, 16);
+                    pacc[h].w += __shfl_xor_sync(0xffffffffu, pacc[h].w, 16);
+                    plsum[h] += __shfl_xor_sync(0xffffffffu, plsum[h], 16);
+                    if (lane < 16) reinterpret_cast<float4*>(sh.att.o[warp][h])[pq] = pacc[h];
+                    if (lane == 0) sh.att.l[warp][h] = plsum[h];
+                }
                 consumer_sync();  // every thread is done with the last batch's tiles
                 if (tid == 0) {
                     for (int b = 0; b < last_batch; ++b) mbar_arrive(&sh.empty[(k + b) % kStepSlots]);
@@ -953,7 +959,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     const float mx = (h == 0 ? mrun[0] : (h == 1 ? mrun[1] : mrun[2])) * kLn2;  // natural-log units
                     float total = 0.0f, acc = 0.0f;
 #pragma unroll
-                    for (int w = 0; w < kPvSplits; ++w) {
+                    for (int w = 0; w < kConsumerWarps; ++w) {
                         total += sh.att.l[w][h];
                         acc += sh.att.o[w][h][d];
                     }
