@@ -193,11 +193,12 @@ def run_native(args) -> dict | None:
     device = torch.device("cuda", local)
     K, W, ctx = args.steps, args.warmup, args.context
     e2e_steps = K
-    config, cpu_model = build_models(ctx, W + K + W + e2e_steps, args.seed)
+    decode_steps = W + K + 2 * (W + e2e_steps)  # device-timed, then the two end-to-end legs
+    config, cpu_model = build_models(ctx, decode_steps, args.seed)
     model = enable_flux_ops(copy.deepcopy(cpu_model).to(device), operators=FINAL_FLUX_OPERATOR_CATEGORIES)
     prompt = uniform_prompt(ctx, seed=args.seed + rank).to(device)
     with torch.inference_mode():
-        runtime = NativeSmolLM2Prefill.capture(model, prompt, max_decode_steps=W + K + W + e2e_steps)
+        runtime = NativeSmolLM2Prefill.capture(model, prompt, max_decode_steps=decode_steps)
         torch.cuda.synchronize()
         # prefill time of the same prompt (the native prefill re-run; not part of ms/token)
         p_start, p_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -227,14 +228,39 @@ def run_native(args) -> dict | None:
             dist.barrier()
         elapsed_ms = start.elapsed_time(end)
 
-        # ---- end-to-end: host token in (pinned H2D), one replay, host token out (D2H read)
+        # ---- end-to-end, host buffers: the token goes in from host memory and the
+        # sampled token comes back to host memory every step.  (1) the C-ABI
+        # host-buffer step (fx_decode_replay_host through replay_host); (2) the
+        # tensor API: pinned host tensor -> device tensor -> replay(token) ->
+        # pinned host tensor.
+        def timed_loop(step) -> float:
+            for _ in range(W):
+                step()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e_start.record(stream)
+            for _ in range(e2e_steps):
+                step()
+            e_end.record(stream)
+            torch.cuda.synchronize()
+            return e_start.elapsed_time(e_end)
+
+        host_token = [int(runtime.current_token.item())]
+
+        def host_step():
+            host_token[0] = runtime.replay_host(host_token[0])
+
+        e2e_ms = timed_loop(host_step)
+
         host_in = torch.empty((1, 1), dtype=torch.int64, pin_memory=True)
         host_out = torch.empty((1, 1), dtype=torch.int64, pin_memory=True)
         dev_in = torch.empty((1, 1), dtype=torch.int64, device=device)
         host_in.copy_(runtime.current_token.cpu())
         ready = torch.cuda.Event()
 
-        def e2e_step():
+        def tensor_step():
             dev_in.copy_(host_in, non_blocking=True)
             runtime.replay(dev_in)
             host_out.copy_(runtime.current_token, non_blocking=True)
@@ -242,24 +268,13 @@ def run_native(args) -> dict | None:
             ready.synchronize()
             host_in.copy_(host_out)
 
-        for _ in range(W):
-            e2e_step()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e_start.record(stream)
-        for _ in range(e2e_steps):
-            e2e_step()
-        e_end.record(stream)
-        torch.cuda.synchronize()
-        e2e_ms = e_start.elapsed_time(e_end)
+        e2e_tensor_ms = timed_loop(tensor_step)
         kernels_per_step = native._decode.kernels_per_step()
 
-    times = torch.tensor([elapsed_ms, e2e_ms], dtype=torch.float64, device=device)
+    times = torch.tensor([elapsed_ms, e2e_ms, e2e_tensor_ms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    elapsed_ms, e2e_ms = times.tolist()
+    elapsed_ms, e2e_ms, e2e_tensor_ms = times.tolist()
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs")
     peak_src = "measured" if peak else "fallback"
@@ -312,7 +327,11 @@ def run_native(args) -> dict | None:
         },
         "e2e": {"value": round(e2e_ms / e2e_steps, 5), "unit": "ms/token", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 8,
-                "api": "NativeSmolLM2Prefill.replay(token) with pinned host token in / next token read back"},
+                "api": "NativeSmolLM2Prefill.replay_host(token) -> next token (C-ABI fx_decode_replay_host: host "
+                       "token in, one replay, sampled token back in host memory, every step)",
+                "tensor_api_value": round(e2e_tensor_ms / e2e_steps, 5),
+                "tensor_api": "NativeSmolLM2Prefill.replay(token) with a pinned host token copied in and the next "
+                              "token read back through torch copies"},
         "gpu_launches": int(kernels_per_step * K),
         "clocks": clocks.summary(),
     }

@@ -151,6 +151,7 @@ SIGNATURES: dict[str, tuple] = {
     "fx_greedy_argmax_update_f32": (_st, [_p, _i64, _p, _p, _i64, _p, _p, _p, _p]),
     "fx_decode_create": (_st, [ctypes.POINTER(ModelDesc), _p, _p, _p, _i64, _i64, _p, ctypes.POINTER(_p)]),
     "fx_decode_replay": (_st, [_p, _p, _p]),
+    "fx_decode_replay_host": (_st, [_p, _p, _p, _p]),
     "fx_decode_generate": (_st, [_p, _i64, _p]),
     "fx_decode_reset": (_st, [_p, _p, _p, _p, _i64, _i64, _p]),
     "fx_decode_inject_failure": (_st, [_p, ctypes.c_int32]),

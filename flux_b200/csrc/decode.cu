@@ -516,6 +516,7 @@ struct fx_decode {
     cudaEvent_t done = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
+    int64_t* host_io = nullptr;   // page-locked [0] token in, [1] token out (fx_decode_replay_host)
     // owned device memory
     int64_t* state = nullptr;     // token, position, length, step, generated[capacity]
     float* logits = nullptr;
@@ -754,6 +755,7 @@ void release(fx_decode* r) {
         cudaStreamSynchronize(r->capture_stream);
         cudaStreamDestroy(r->capture_stream);
     }
+    if (r->host_io) cudaFreeHost(r->host_io);
     cudaFree(r->state);
     cudaFree(r->logits);
     cudaFree(r->key_cache);
@@ -815,6 +817,8 @@ fx_status create_impl(fx_decode* r, const int64_t* token, const float* const* ks
     if (st != FX_OK) return st;
     FX_CUDA_TRY(cudaStreamCreateWithFlags(&r->capture_stream, cudaStreamNonBlocking), "creating capture stream");
     FX_CUDA_TRY(cudaEventCreateWithFlags(&r->done, cudaEventDisableTiming), "creating completion event");
+    FX_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&r->host_io), 2 * sizeof(int64_t), cudaHostAllocDefault),
+                "allocating page-locked token words");
     st = initialize_state(r, token, ks, vs, rows, position, stream);
     if (st != FX_OK) return st;
     FX_CUDA_TRY(cudaEventRecord(r->done, stream), "recording setup");
@@ -903,6 +907,33 @@ extern "C" fx_status fx_decode_replay(fx_decode* r, const int64_t* token, void* 
     FX_CUDA_TRY(cudaEventRecord(r->done, s), "recording replay completion");
     r->pending = true;
     ++r->replay_count;
+    return FX_OK;
+}
+
+extern "C" fx_status fx_decode_replay_host(fx_decode* r, const int64_t* host_token, int64_t* host_next,
+                                          void* stream) {
+    FX_REQUIRE(r != nullptr && host_next != nullptr, "fx_decode_replay_host: null pointer");
+    if (r->replay_count >= r->capacity - r->start_position) {
+        set_error("flux native full decode: fixed-capacity state is exhausted");
+        return FX_ERR_EXHAUSTED;
+    }
+    DeviceGuard guard(r->model.device);
+    cudaStream_t s = as_stream(stream);
+    if (r->pending) FX_CUDA_TRY(cudaStreamWaitEvent(s, r->done, 0), "ordering consecutive replays");
+    // The staging words are free: the previous call returned after its copies.
+    if (host_token != nullptr) {
+        r->host_io[0] = *host_token;
+        FX_CUDA_TRY(cudaMemcpyAsync(r->token(), r->host_io, sizeof(int64_t), cudaMemcpyHostToDevice, s),
+                    "copying the host replay token");
+    }
+    FX_CUDA_TRY(cudaGraphLaunch(r->exec, s), "launching the decode graph");
+    FX_CUDA_TRY(cudaMemcpyAsync(r->host_io + 1, r->token(), sizeof(int64_t), cudaMemcpyDeviceToHost, s),
+                "copying the sampled token to the host");
+    FX_CUDA_TRY(cudaEventRecord(r->done, s), "recording replay completion");
+    r->pending = true;
+    ++r->replay_count;
+    FX_CUDA_TRY(cudaEventSynchronize(r->done), "waiting for the replay");
+    *host_next = r->host_io[1];
     return FX_OK;
 }
 

@@ -242,6 +242,8 @@ class NativeDecodeObject:
         self._position = _view(buffers.position, (), i64, o, device)
         self._length = _view(buffers.cache_length, (), i64, o, device)
         self._workspace = _view(buffers.workspace, (buffers.workspace_bytes,), torch.uint8, o, device)
+        self._host_in, self._host_out = ctypes.c_int64(0), ctypes.c_int64(0)
+        self._host_in_addr, self._host_out_addr = ctypes.addressof(self._host_in), ctypes.addressof(self._host_out)
 
     def _info(self) -> _native.DecodeInfo:
         info = _native.DecodeInfo()
@@ -255,6 +257,16 @@ class NativeDecodeObject:
         _native.check(_native.load().fx_decode_replay(self._handle, None if token is None else token.data_ptr(),
                                                       _stream(self._device)))
         return self._logits
+
+    def replay_host(self, token: int | None = None) -> int:
+        """One step with host buffers (``fx_decode_replay_host``): the host
+        token in (None keeps the device's current token), the sampled token
+        back as a Python int once it is on the host."""
+        if token is not None:
+            self._host_in.value = token
+        _native.check(_native.load().fx_decode_replay_host(
+            self._handle, None if token is None else self._host_in_addr, self._host_out_addr, _stream(self._device)))
+        return self._host_out.value
 
     def generate_greedy(self, decode_steps: int, eos_token_id: int | None = None) -> torch.Tensor:
         """`decode_steps` chained greedy steps on device; with `eos_token_id`
@@ -351,6 +363,9 @@ class NativePrefillObject:
 
     def replay(self, token: torch.Tensor | None = None) -> torch.Tensor:
         return self._decode.replay(token)
+
+    def replay_host(self, token: int | None = None) -> int:
+        return self._decode.replay_host(token)
 
     def generate_greedy(self, max_new_tokens: int, eos_token_id: int | None = None) -> torch.Tensor:
         if max_new_tokens < 1:
@@ -450,6 +465,11 @@ class NativeSmolLM2Prefill:
 
     def replay(self, token: torch.Tensor | None = None) -> torch.Tensor:
         return self._native.replay(token)
+
+    def replay_host(self, token: int | None = None) -> int:
+        """One synchronous step with host buffers: `token` in, the greedy
+        token sampled by the step out (``fx_decode_replay_host``)."""
+        return self._native.replay_host(token)
 
     def generate_greedy(self, max_new_tokens: int, *, eos_token_id: int | None = None) -> torch.Tensor:
         """Greedy tokens [1, n] starting with the prefill's token: n =
@@ -640,6 +660,11 @@ class NativeSmolLM2Decode:
     def replay(self, token: torch.Tensor | None = None) -> torch.Tensor:
         """Asynchronously enqueue an optional token copy and one graph launch."""
         return self._native.replay(token)
+
+    def replay_host(self, token: int | None = None) -> int:
+        """One synchronous step with host buffers: `token` in, the greedy
+        token sampled by the step out (``fx_decode_replay_host``)."""
+        return self._native.replay_host(token)
 
     def reset(self, token: torch.Tensor, key_caches, value_caches, *, cache_position: int) -> None:
         """Synchronously restore prefilled state outside steady replay."""

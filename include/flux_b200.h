@@ -254,6 +254,17 @@ FX_API fx_status fx_decode_create(const fx_model_desc* model, const int64_t* ini
  * Replaces NativeSmolLM2Decode::replay (native_decode_runtime_cuda.cu:907-931). */
 FX_API fx_status fx_decode_replay(fx_decode* runtime, const int64_t* token, void* stream);
 
+/* One step with HOST buffers, synchronous: copies *host_token in (skipped
+ * when NULL), one graph launch, copies the sampled token out and returns once
+ * *host_next holds it.  Both copies go through page-locked words owned by the
+ * runtime, so any host pointer works and the copies stay asynchronous to the
+ * launch.  Same capacity rule as fx_decode_replay.  The host-buffer form of
+ * NativeSmolLM2Decode::replay followed by a read of the current token
+ * (native_decode_runtime_cuda.cu:907-931), for hosts that keep tokens in host
+ * memory (an FFI caller feeding tokens one at a time). */
+FX_API fx_status fx_decode_replay_host(fx_decode* runtime, const int64_t* host_token, int64_t* host_next,
+                                       void* stream);
+
 /* `steps` chained greedy steps (graph launches), async.  FX_ERR_STATE when
  * called twice without a prefill or reset in between.
  * Replaces NativeSmolLM2Decode::generate_greedy (native_decode_runtime_cuda.cu:933-960). */

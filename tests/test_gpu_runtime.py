@@ -262,6 +262,29 @@ def test_replay_on_non_default_stream_and_memory(tiny_flux):
     assert memory.owned_tensor_bytes > memory.cache_bytes
 
 
+def test_replay_host_matches_tensor_replay(tiny_flux):
+    """The host-buffer step (``fx_decode_replay_host``): teacher-forced host
+    tokens in, the sampled token back as an int; bitwise the same logits and
+    tokens as the tensor replay path, and None keeps the device token."""
+    from flux_b200.runtime import NativeSmolLM2Prefill
+    ids = gi.tiny30_ids(5).cuda()
+    host = NativeSmolLM2Prefill.capture(tiny_flux, ids, max_decode_steps=6)
+    dev = NativeSmolLM2Prefill.capture(tiny_flux, ids, max_decode_steps=6)
+    host_logits = host.native_object()._decode.logits()  # the decode step's (not the prefill's) logits
+    for i, token in enumerate([7, 123, 49151, None, 5]):
+        nxt = host.replay_host(token)
+        if token is None:
+            expected = dev.replay().clone()
+        else:
+            expected = dev.replay(torch.tensor([[token]], dtype=torch.int64, device="cuda")).clone()
+        torch.cuda.synchronize()
+        assert torch.equal(host_logits, expected), i
+        assert nxt == int(dev.current_token.item()) == int(host.current_token.item())
+    with pytest.raises(RuntimeError, match="exhausted"):
+        for _ in range(8):
+            host.replay_host(1)
+
+
 @pytest.mark.parametrize("prompt_length", [1, 64, 65, 200, 777])
 def test_prefill_long_prompt_vs_oracle(smollm2_model, smollm2_flux, prompt_length):
     """The native prefill (tensor-core causal attention over 128-query blocks
