@@ -393,7 +393,9 @@ fx_status gemm(fx_batch* r, int M, const float* x, const float* w, int N, int K,
     float* out = p.splits == 1 && direct_out != nullptr ? direct_out : partials;
     if (r->tensor_cores) {
         TcGemmArgs a = tc_args(*tw, *xmap, out, nullptr, reinterpret_cast<int*>(r->error), M, p.k_per_split);
-        return launch_tc_gemm(a, 64, p.splits, s, true);
+        // With two lanes, 3 pipeline stages (145 KB) let a projection CTA of
+        // one lane share an SM with an attention chunk CTA of the other.
+        return launch_tc_gemm(a, 64, p.splits, s, true, r->lanes > 1 ? 3 : 0);
     }
     const dim3 grid((N + kTileN - 1) / kTileN, p.splits);
     return launch_dependent(skinny_gemm_kernel, grid, dim3(kGemmThreads), 0, s, "launching a batched projection", x, w,

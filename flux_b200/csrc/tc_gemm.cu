@@ -40,20 +40,23 @@ constexpr int kTcEpi = kTcThreads - 64;
 constexpr int kTcPromote = 2;    // stages per hi.hi accumulator before it is added into registers
 constexpr uint32_t kWBox = kTcTileN * kTcTileK * 4;  // 16 KB
 
-template <int BM>
+// Default stage counts: 4 for 64-row tiles, 3 for 128-row tiles.
+constexpr int tc_default_stages(int bm) { return bm == 64 ? 4 : 3; }
+
+template <int BM, int STAGES>
 struct TcLayout {
     static constexpr uint32_t kX = BM * kTcTileK * 4;
     static constexpr uint32_t kStage = 2 * kWBox + 2 * kX;  // W_hi, W_lo, X (-> X_hi), X_lo
-    static constexpr int kStages = BM == 64 ? 4 : 3;
+    static constexpr int kStages = STAGES;
     static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStage + 1024 + 256;
     // TMEM columns: [0, BM) the cross terms, [BM, 2 BM) and [2 BM, 3 BM)
     // the per-stage hi.hi products (double-buffered); allocation 4 BM.
     static constexpr uint32_t kTmemCols = 4 * BM;
 };
 
-template <int BM>
+template <int BM, int STAGES>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ TcGemmArgs a) {
-    using L = TcLayout<BM>;
+    using L = TcLayout<BM, STAGES>;
     constexpr int S = L::kStages;
     extern __shared__ unsigned char tc_raw[];
     unsigned char* smem = tc_raw + ((1024u - (smem_addr(tc_raw) & 1023u)) & 1023u);
@@ -275,15 +278,21 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-template <int BM>
-fx_status configure_once() {
+template <int BM, int STAGES>
+fx_status launch_variant(const TcGemmArgs& args, dim3 grid, cudaStream_t stream, bool dependent) {
     static std::once_flag once;
     static cudaError_t status = cudaSuccess;
+    constexpr size_t smem = TcLayout<BM, STAGES>::kSmem;
     std::call_once(once, [] {
-        status = cudaFuncSetAttribute(tc_gemm_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(TcLayout<BM>::kSmem));
+        status = cudaFuncSetAttribute(tc_gemm_kernel<BM, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem));
     });
     FX_CUDA_TRY(status, "raising the tensor-core GEMM's shared memory");
+    if (dependent)
+        return launch_dependent(tc_gemm_kernel<BM, STAGES>, grid, dim3(kTcThreads), smem, stream,
+                                "launching the tensor-core GEMM", args);
+    tc_gemm_kernel<BM, STAGES><<<grid, kTcThreads, smem, stream>>>(args);
+    FX_CUDA_TRY(cudaGetLastError(), "launching the tensor-core GEMM");
     return FX_OK;
 }
 
@@ -337,31 +346,19 @@ fx_status tc_split(const float* w, float* hi, float* lo, size_t n, cudaStream_t 
     return FX_OK;
 }
 
-fx_status launch_tc_gemm(const TcGemmArgs& args, int bm, int splits, cudaStream_t stream, bool dependent) {
+fx_status launch_tc_gemm(const TcGemmArgs& args, int bm, int splits, cudaStream_t stream, bool dependent,
+                         int stages) {
     FX_REQUIRE(args.k % kTcTileK == 0 && args.k_per_split % kTcTileK == 0 && args.k_per_split > 0 && splits >= 1 &&
                    args.m > 0 && args.n > 0 && args.ldc >= args.n,
                "tensor-core GEMM: K and its slices must be multiples of 32, M, N > 0");
     const dim3 grid(static_cast<unsigned>((args.n + kTcTileN - 1) / kTcTileN),
                     static_cast<unsigned>((args.m + bm - 1) / bm), static_cast<unsigned>(splits));
-    fx_status st;
-    if (bm == 64) {
-        if ((st = configure_once<64>()) != FX_OK) return st;
-        if (dependent)
-            return launch_dependent(tc_gemm_kernel<64>, grid, dim3(kTcThreads), TcLayout<64>::kSmem, stream,
-                                    "launching the tensor-core GEMM", args);
-        tc_gemm_kernel<64><<<grid, kTcThreads, TcLayout<64>::kSmem, stream>>>(args);
-    } else if (bm == 128) {
-        if ((st = configure_once<128>()) != FX_OK) return st;
-        if (dependent)
-            return launch_dependent(tc_gemm_kernel<128>, grid, dim3(kTcThreads), TcLayout<128>::kSmem, stream,
-                                    "launching the tensor-core GEMM", args);
-        tc_gemm_kernel<128><<<grid, kTcThreads, TcLayout<128>::kSmem, stream>>>(args);
-    } else {
-        set_error("tensor-core GEMM: the activation tile must be 64 or 128 rows");
-        return FX_ERR_INVALID;
-    }
-    FX_CUDA_TRY(cudaGetLastError(), "launching the tensor-core GEMM");
-    return FX_OK;
+    if (stages == 0) stages = tc_default_stages(bm);
+    if (bm == 64 && stages == 4) return launch_variant<64, 4>(args, grid, stream, dependent);
+    if (bm == 64 && stages == 3) return launch_variant<64, 3>(args, grid, stream, dependent);
+    if (bm == 128 && stages == 3) return launch_variant<128, 3>(args, grid, stream, dependent);
+    set_error("tensor-core GEMM: the tile must be 64 rows (3 or 4 stages) or 128 rows (3 stages)");
+    return FX_ERR_INVALID;
 }
 
 fx_status tc_weights_create(const fx_model_desc& model, bool lm_head, TcModelWeights* out, cudaStream_t stream) {

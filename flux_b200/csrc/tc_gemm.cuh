@@ -41,7 +41,11 @@ fx_status tc_encode_map(CUtensorMap* map, const float* base, int64_t rows, int64
 fx_status tc_split(const float* w, float* hi, float* lo, size_t n, cudaStream_t stream);
 
 // One launch: grid (ceil(N / 128), ceil(M / bm), splits); bm is 64 or 128.
-fx_status launch_tc_gemm(const TcGemmArgs& args, int bm, int splits, cudaStream_t stream, bool dependent);
+// `stages` (shared-memory pipeline depth, 48 KB each at bm 64): 0 for the
+// default (4 at bm 64, 3 at bm 128), or 3 at bm 64 so that a CTA (145 KB)
+// shares its SM with a 71 KB attention chunk CTA of a concurrent stream.
+fx_status launch_tc_gemm(const TcGemmArgs& args, int bm, int splits, cudaStream_t stream, bool dependent,
+                         int stages = 0);
 
 // The hi / lo halves of one projection weight and their tensor maps.
 struct TcWeight {
