@@ -261,7 +261,9 @@ FX_API fx_status fx_decode_replay(fx_decode* runtime, const int64_t* token, void
  * launch.  Same capacity rule as fx_decode_replay.  The host-buffer form of
  * NativeSmolLM2Decode::replay followed by a read of the current token
  * (native_decode_runtime_cuda.cu:907-931), for hosts that keep tokens in host
- * memory (an FFI caller feeding tokens one at a time). */
+ * memory (an FFI caller feeding tokens one at a time).  A device-side failure
+ * of the step (a bounded wait that gave up) is reported, as for
+ * fx_decode_replay, by the next fx_decode_read_state. */
 FX_API fx_status fx_decode_replay_host(fx_decode* runtime, const int64_t* host_token, int64_t* host_next,
                                        void* stream);
 
