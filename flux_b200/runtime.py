@@ -92,7 +92,14 @@ def _view(ptr: int, shape, dtype: torch.dtype, owner, device: torch.device) -> t
     return torch.as_tensor(_DeviceView(ptr, shape, typestr, owner), device=device)
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device: torch.device) -> int:
+    """The caller's current CUDA stream on `device` as a raw handle (queried
+    on every call, so it follows `torch.cuda.stream(...)` contexts)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 
