@@ -470,6 +470,29 @@ __device__ unsigned long long poll_word(const StepArgs& a, Shared& sh, const uns
     return v;
 }
 
+// Spin (bounded) until the three words at p[0..2] all carry `tag`; each round
+// reloads only the stale ones, so the three wait on one L2 round trip at a
+// time together instead of one after another.
+__device__ void poll_words3(const StepArgs& a, Shared& sh, const unsigned long long* const (&p)[3],
+                            unsigned long long (&v)[3], uint32_t tag) {
+    const unsigned long long t0 = global_timer();
+    while (word_tag(v[0]) != tag || word_tag(v[1]) != tag || word_tag(v[2]) != tag) {
+#pragma unroll
+        for (int j = 0; j < 3; ++j)
+            if (word_tag(v[j]) != tag) v[j] = ld_word(p[j]);
+        if (sh.abort) break;
+        const unsigned long long dt = global_timer() - t0;
+        if (dt > kPeerCheckNs && ld_error(a.error) != 0) {
+            sh.abort = 1;
+            break;
+        }
+        if (dt > kWaitNs) {
+            fail(a, sh);
+            break;
+        }
+    }
+}
+
 // Phase B's inputs in one poll round and one barrier: q of kv group g (192
 // words) and, for the CTA that owns the new row, that row's k and v (64 each).
 __device__ bool poll_attention_inputs(const StepArgs& a, Shared& sh, const unsigned long long* qkv, int g,
@@ -991,13 +1014,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                         const int j = s.ob[q / kStepBlock] * kStepBlock + q % kStepBlock;
                         const int h = j / kHeadDim, d = j % kHeadDim;
                         const unsigned long long* p = part + (static_cast<size_t>(h) * a.nch + cc) * kStepPartial;
-                        unsigned long long vm = ld_word(p), vl = ld_word(p + 1), vo = ld_word(p + 2 + d);
-                        if (word_tag(vm) != tag) vm = poll_word(a, sh, p, vm, tag);
-                        if (word_tag(vl) != tag) vl = poll_word(a, sh, p + 1, vl, tag);
-                        if (word_tag(vo) != tag) vo = poll_word(a, sh, p + 2 + d, vo, tag);
-                        sh.mm[q][cc] = word_value(vm);
-                        sh.ml[q][cc] = word_value(vl);
-                        sh.mo[q][cc] = word_value(vo);
+                        const unsigned long long* const src[3] = {p, p + 1, p + 2 + d};
+                        unsigned long long v[3] = {ld_word(src[0]), ld_word(src[1]), ld_word(src[2])};
+                        poll_words3(a, sh, src, v, tag);
+                        sh.mm[q][cc] = word_value(v[0]);
+                        sh.ml[q][cc] = word_value(v[1]);
+                        sh.mo[q][cc] = word_value(v[2]);
                     }
                     consumer_sync();
                     if (sh.abort) goto done;
