@@ -47,6 +47,32 @@ def test_registered_operator_schemas():
         assert hasattr(torch.ops.flux, name), name
 
 
+# The native-side names `flux/ops/__init__.py` exports (its plain-PyTorch
+# functions stay with Flux); each must import from flux_b200.operators.
+FLUX_OPS_NATIVE_NAMES = (
+    "CublasLtAlgorithm", "attention_score_softmax_native", "cublaslt_algorithms", "cublaslt_linear_config_out",
+    "cublaslt_linear_out", "gqa_decode_attention_native", "gqa_decode_attention_native_out",
+    "native_attention_score_softmax_is_available", "native_cublaslt_linear_is_available",
+    "native_gqa_decode_attention_is_available", "native_packed_gate_up_gemv_is_available",
+    "native_packed_qkv_rope_cache_is_available", "native_packed_qkv_rope_cache_load_error",
+    "native_packed_swiglu_is_available", "native_residual_rmsnorm_is_available", "native_rmsnorm_is_available",
+    "native_rmsnorm_load_error", "native_rope_is_available", "native_rope_load_error",
+    "native_softmax_is_available", "native_softmax_load_error", "packed_gate_up_swiglu_native_out",
+    "packed_qkv_rope_cache_native", "packed_qkv_rope_cache_native_out", "packed_swiglu_native",
+    "packed_swiglu_native_out", "residual_rmsnorm_native", "residual_rmsnorm_native_out", "rms_norm_native",
+    "rms_norm_native_out", "rope_native", "softmax_native",
+)
+
+
+def test_python_entry_points_cover_flux_ops():
+    from flux_b200 import operators
+    missing = [name for name in FLUX_OPS_NATIVE_NAMES if not hasattr(operators, name)]
+    assert not missing
+    for name in FLUX_OPS_NATIVE_NAMES:
+        if name.endswith("_is_available"):
+            assert getattr(operators, name)() is True, name  # the library is built in-tree
+
+
 def test_operator_error_contracts_on_cpu():
     """``tests/test_ops.py`` error cases; valid CPU inputs are rejected loudly."""
     from flux_b200 import operators as ops
