@@ -34,9 +34,11 @@ typedef int32_t fx_status;
 #define FX_ERR_STATE 4     /* call order violated (e.g. reuse without prefill or reset) */
 #define FX_ERR_DEVICE 5    /* a kernel's own check or bounded wait reported failure */
 
-/* Message of the last failing call on this thread ("" if none). */
+/* Message of the last failing call on this thread ("" if none).  The
+ * reference raises these messages as exceptions (TORCH_CHECK); an FFI caller
+ * reads them here, and the Python layer raises them as RuntimeError. */
 FX_API const char* fx_last_error(void);
-/* Library version string. */
+/* Library version string (no counterpart in the reference). */
 FX_API const char* fx_version(void);
 
 /* ------------------------------------------------------------------------
@@ -288,6 +290,9 @@ FX_API fx_status fx_decode_install_prefill(fx_decode* runtime, const int64_t* to
  * Replaces NativeSmolLM2Decode::wait_for_prefill (native_decode_runtime_cuda.cu:983-989). */
 FX_API fx_status fx_decode_wait(fx_decode* runtime, void* stream);
 
+/* The runtime's stable device buffers (addresses never change).  Replaces
+ * NativeSmolLM2Decode's tensor getters and addresses()
+ * (native_decode_runtime_torch.cpp:61-70; buffers native_decode_runtime_cuda.cu:1162-1224). */
 FX_API fx_status fx_decode_get_buffers(const fx_decode* runtime, fx_decode_buffers* out);
 
 #define FX_STATE_POSITION 0
@@ -304,9 +309,12 @@ typedef struct fx_decode_info {
     int64_t replay_count;    /* graph launches since then */
     int64_t kernels_per_step;/* kernel launches inside one step graph */
 } fx_decode_info;
+/* Host-side sizes and counters.  Replaces NativeSmolLM2Decode::capacity /
+ * replay_count (native_decode_runtime_torch.cpp:73-79). */
 FX_API fx_status fx_decode_get_info(const fx_decode* runtime, fx_decode_info* out);
 
-/* Waits for pending work, then releases everything the runtime owns. */
+/* Waits for pending work, then releases everything the runtime owns.
+ * Replaces the runtime's destructor (native_decode_runtime_cuda.cu:867). */
 FX_API void fx_decode_destroy(fx_decode* runtime);
 
 /* ------------------------------------------------------------------------
@@ -337,10 +345,17 @@ FX_API fx_status fx_prefill_create(const fx_model_desc* model, const int64_t* in
  * Replaces NativeSmolLM2Prefill::prefill (native_prefill_runtime_cuda.cu:540-551). */
 FX_API fx_status fx_prefill_run(fx_prefill* runtime, const int64_t* input_ids, void* stream);
 
-/* The owned decode runtime (borrowed; destroyed with the prefill runtime). */
+/* The owned decode runtime (borrowed; destroyed with the prefill runtime):
+ * the prefill object's replay / generate_greedy / state getters go through it
+ * (native_prefill_runtime_torch.cpp:24-41). */
 FX_API fx_decode* fx_prefill_decode(fx_prefill* runtime);
+/* Prefill-side stable buffers (prefill logits, final hidden state).  Replaces
+ * NativeSmolLM2Prefill::logits / final_hidden (native_prefill_runtime_torch.cpp:26-30). */
 FX_API fx_status fx_prefill_get_buffers(const fx_prefill* runtime, fx_prefill_buffers* out);
+/* Replaces NativeSmolLM2Prefill::prompt_length (native_prefill_runtime_torch.cpp:38). */
 FX_API int64_t fx_prefill_prompt_length(const fx_prefill* runtime);
+/* Waits for pending work, then releases the prefill runtime and its decode
+ * runtime.  Replaces the runtime's destructor (native_prefill_runtime_cuda.cu:447). */
 FX_API void fx_prefill_destroy(fx_prefill* runtime);
 
 /* ------------------------------------------------------------------------
