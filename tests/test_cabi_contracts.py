@@ -115,3 +115,40 @@ def test_static_scratch_attention_refuses_oversized_problems_before_the_gpu():
         FAKE, strides, FAKE, strides, FAKE, strides, None, None, None, None, FAKE, 0.125, 1, 9, 3, capacity, 64,
         None)
     _refused(status, _native.FX_ERR_INVALID, "static array")
+
+
+C_CALLER = r"""
+#include "flux_b200.h"
+#include <stdio.h>
+#include <string.h>
+int main(void) {
+    fx_model_desc m = {0};
+    fx_decode* d = 0;
+    int64_t token = 1;
+    fx_status st = fx_decode_create(&m, &token, 0, 0, 0, 0, 0, &d);
+    puts(fx_last_error());
+    return st == FX_ERR_INVALID && d == 0 && strstr(fx_last_error(), "vocabulary") != 0 ? 0 : 1;
+}
+"""
+
+
+def test_header_is_plain_c_and_links(tmp_path):
+    """A C99 caller (what cgo or any C FFI generator sees) compiles against
+    include/flux_b200.h with -pedantic, links against the library, and reads
+    a refusal through fx_last_error."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    root = Path(__file__).resolve().parent.parent
+    lib_dir = _native.LIBRARY_PATH.parent
+    src, exe = tmp_path / "caller.c", tmp_path / "caller"
+    src.write_text(C_CALLER)
+    build = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", f"-I{root / 'include'}",
+                            str(src), f"-L{lib_dir}", "-lfluxb200", f"-Wl,-rpath,{lib_dir}", "-o", str(exe)],
+                           capture_output=True, text=True)
+    assert build.returncode == 0, build.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stdout + run.stderr
+    assert "vocabulary must be non-empty" in run.stdout
