@@ -64,10 +64,6 @@ def parse_args(argv=None):
     p.add_argument("--no-batched", action="store_true", help="skip the batched configuration")
     p.add_argument("--no-attention", action="store_true", help="skip the isolated-attention sweep")
     p.add_argument("--no-sweep", action="store_true", help="skip the context sweep of the batch-1 decode")
-    p.add_argument("--probe", choices=("batched", "tc-gemm", "prefill"), default=None,
-                   help="run a small fixed workload for a profiler (no JSON line): two batched steps of 64 "
-                        "sequences, three 8192 x 576 -> 3072 tensor-core projections, or one --context-token "
-                        "prefill")
     return p.parse_args(argv)
 
 
@@ -173,15 +169,15 @@ class ClockSampler:
 
 
 def build_models(context: int, steps_total: int, seed: int):
-    from oracle import hf_reference as hf
-    config = hf.smollm2_config(vocab_size=49152, max_positions=max(8320, context + steps_total + 1))
-    return config, hf.build_model(config, seed)
+    from tests.golden.inputs import build_model, smollm2_config
+    config = smollm2_config(vocab_size=49152, max_positions=max(8320, context + steps_total + 1))
+    return config, build_model(config, seed)
 
 
 def run_native(args) -> dict | None:
     import torch.distributed as dist
 
-    from oracle.host import limit_threads
+    from tests.host import limit_threads
     limit_threads()
 
     from flux_b200.integration import FINAL_FLUX_OPERATOR_CATEGORIES, enable_flux_ops
@@ -551,66 +547,9 @@ def run_reference(args) -> dict | None:
     }
 
 
-def run_probe(args) -> None:
-    """Small fixed workloads for ncu captures (the commands in profiles/)."""
-    device = torch.device("cuda", 0)
-    torch.cuda.set_device(device)
-    if args.probe == "tc-gemm":
-        from flux_b200 import _native
-        lib = _native.load()
-        g = torch.Generator(device=device).manual_seed(args.seed)
-        m, k, n = 8192, 576, 3072
-        x = torch.randn(m, k, device=device, generator=g)
-        w = torch.randn(n, k, device=device, generator=g) * 0.02
-        hi, lo, out = torch.empty_like(w), torch.empty_like(w), torch.empty(m, n, device=device)
-        err = torch.zeros(1, dtype=torch.int32, device=device)
-        stream = torch.cuda.current_stream(device).cuda_stream
-        _native.check(lib.fx_tf32_split_f32(w.data_ptr(), hi.data_ptr(), lo.data_ptr(), w.numel(), stream))
-        for _ in range(3):
-            _native.check(lib.fx_linear_3xtf32_f32(x.data_ptr(), hi.data_ptr(), lo.data_ptr(), None, out.data_ptr(),
-                                                   m, k, n, err.data_ptr(), stream))
-        torch.cuda.synchronize()
-        assert int(err.item()) == 0
-    elif args.probe == "prefill":
-        from oracle.host import limit_threads
-        limit_threads()
-        from flux_b200.integration import FINAL_FLUX_OPERATOR_CATEGORIES, enable_flux_ops
-        from flux_b200.runtime import NativeSmolLM2Prefill
-        from tests.golden.inputs import uniform_prompt
-        _, cpu_model = build_models(args.context, 2, args.seed)
-        model = enable_flux_ops(copy.deepcopy(cpu_model).to(device), operators=FINAL_FLUX_OPERATOR_CATEGORIES)
-        with torch.inference_mode():
-            NativeSmolLM2Prefill.capture(model, uniform_prompt(args.context, seed=args.seed).to(device),
-                                         max_decode_steps=1)
-        torch.cuda.synchronize()
-    else:
-        from oracle.host import limit_threads
-        limit_threads()
-        from flux_b200 import sharding
-        from flux_b200.integration import FINAL_FLUX_OPERATOR_CATEGORIES, enable_flux_ops
-        from flux_b200.runtime import NativeSmolLM2BatchedDecode
-        _, cpu_model = build_models(BATCH_CONTEXT[1], 8, args.seed)
-        model = enable_flux_ops(copy.deepcopy(cpu_model).to(device), operators=FINAL_FLUX_OPERATOR_CATEGORIES)
-        lengths, tokens = sharding.shard_contexts(args.seed, sharding.sequence_shard(args.batch, 1, 0), *BATCH_CONTEXT)
-        runtime = NativeSmolLM2BatchedDecode(model, args.batch, BATCH_CONTEXT[1] + 8)
-        dgen = torch.Generator(device=device)
-        for i, n in enumerate(lengths):
-            dgen.manual_seed(args.seed * 1_000_003 + 29 + i)
-            keys = torch.randn(30, 3, n, 64, device=device, generator=dgen) * 0.5
-            values = torch.randn(30, 3, n, 64, device=device, generator=dgen) * 0.5
-            runtime.load(i, tokens[i], list(keys), list(values), n)
-        runtime.step(2)
-        runtime.check()
-        torch.cuda.synchronize()
-    print(f"probe {args.probe} ok", flush=True)
-
-
 def main(argv=None) -> int:
     args = parse_args(argv)
     world, rank, local = dist_info()
-    if args.probe is not None:
-        run_probe(args)
-        return 0
     if args.impl == "reference":
         line = run_reference(args)
         if line is not None:

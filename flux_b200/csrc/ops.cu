@@ -6,10 +6,16 @@
 #include "attention.cuh"
 #include "common.cuh"
 
+#include <cuda.h>
+
 #include <algorithm>
+#include <climits>
 #include <cmath>
+#include <cstdint>
 #include <mutex>
 #include <string>
+#include <utility>
+#include <vector>
 
 namespace fx {
 namespace {
@@ -485,7 +491,13 @@ extern "C" fx_status fx_packed_qkv_rope_cache_f32(const float* packed_qkv, const
 extern "C" int64_t fx_gqa_decode_attention_workspace_floats(int64_t batch, int64_t query_heads, int64_t capacity,
                                                             int64_t head_dim) {
     if (batch <= 0 || query_heads <= 0 || capacity <= 0 || head_dim <= 0) return 0;
-    return batch * query_heads * ((capacity + kOpChunk - 1) / kOpChunk) * (head_dim + 2);
+    // INT64_MAX when the product does not fit: no workspace is large enough.
+    const int64_t chunks = capacity / kOpChunk + (capacity % kOpChunk != 0 ? 1 : 0);
+    int64_t floats = 0, width = 0;
+    if (__builtin_add_overflow(head_dim, int64_t{2}, &width) || __builtin_mul_overflow(batch, query_heads, &floats) ||
+        __builtin_mul_overflow(floats, chunks, &floats) || __builtin_mul_overflow(floats, width, &floats))
+        return INT64_MAX;
+    return floats;
 }
 
 extern "C" fx_status fx_gqa_decode_attention_f32(const float* query, const int64_t* query_strides4,
@@ -624,37 +636,83 @@ extern "C" fx_status fx_greedy_argmax_update_f32(const float* logits, int64_t vo
 // call), but two calls whose kernels overlap on the GPU (different streams
 // without ordering between them) race on it.
 //
-// The device address of the array is looked up once per device, with that
-// device current, on the first call there (cudaGetSymbolAddress); make that
-// first call before any stream capture begins.
+// The array's device address belongs to the CUDA context it was looked up
+// in, so it is looked up (cudaGetSymbolAddress) on the first call in each
+// context -- the device's primary context, or a context the host made current
+// itself -- and cached under that context's unique ID (cuCtxGetId, which a
+// context created after a cudaDeviceReset does not share).  Make the first
+// call in each context before any stream capture begins.
 // ---------------------------------------------------------------------------
 
 namespace fx {
 namespace {
 
 constexpr int64_t kStaticScratchFloats = 262144;
-constexpr int kStaticScratchDevices = 64;
 
 static __device__ __align__(256) float g_gqa_static_scratch[kStaticScratchFloats];
 
-std::mutex g_static_scratch_mutex;
-float* g_static_scratch_address[kStaticScratchDevices] = {};
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
 
-// Device address of g_gqa_static_scratch on the current device (set-up on
-// the first call per device).
-fx_status static_scratch_address(float** out) {
-    int device = -1;
-    FX_CUDA_TRY(cudaGetDevice(&device), "querying the current device");
-    FX_REQUIRE(device >= 0 && device < kStaticScratchDevices,
-               "fx_gqa_decode_attention_static_scratch_f32: device ordinal beyond 63");
-    std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
-    if (g_static_scratch_address[device] == nullptr) {
-        void* address = nullptr;
-        FX_CUDA_TRY(cudaGetSymbolAddress(&address, g_gqa_static_scratch),
-                    "looking up the static GQA scratch address");
-        g_static_scratch_address[device] = static_cast<float*>(address);
+std::mutex g_static_scratch_mutex;
+std::vector<std::pair<unsigned long long, float*>> g_static_scratch_by_context;
+
+// Unique ID of the calling thread's current context (0: none current).
+fx_status current_context_id(unsigned long long* id) {
+    static std::once_flag once;
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    std::call_once(once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult found{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &found) == cudaSuccess &&
+            found == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+        fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &found) == cudaSuccess &&
+            found == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(fn);
+    });
+    if (get_current == nullptr || get_id == nullptr) {
+        set_error("fx_gqa_decode_attention_static_scratch_f32: cuCtxGetCurrent / cuCtxGetId are unavailable");
+        return FX_ERR_CUDA;
     }
-    *out = g_static_scratch_address[device];
+    CUcontext context = nullptr;
+    if (get_current(&context) != CUDA_SUCCESS) {
+        set_error("fx_gqa_decode_attention_static_scratch_f32: cuCtxGetCurrent failed");
+        return FX_ERR_CUDA;
+    }
+    *id = 0;
+    if (context != nullptr && get_id(context, id) != CUDA_SUCCESS) {
+        set_error("fx_gqa_decode_attention_static_scratch_f32: cuCtxGetId failed");
+        return FX_ERR_CUDA;
+    }
+    return FX_OK;
+}
+
+// Device address of g_gqa_static_scratch in the calling thread's current
+// context (looked up on the first call in that context).
+fx_status static_scratch_address(float** out) {
+    unsigned long long id = 0;
+    fx_status status = current_context_id(&id);
+    if (status != FX_OK) return status;
+    std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+    if (id != 0)
+        for (const auto& entry : g_static_scratch_by_context)
+            if (entry.first == id) {
+                *out = entry.second;
+                return FX_OK;
+            }
+    // First call in this context (or none was current yet: the lookup makes
+    // the device's primary context current, whose ID is read afterwards).
+    void* address = nullptr;
+    FX_CUDA_TRY(cudaGetSymbolAddress(&address, g_gqa_static_scratch), "looking up the static GQA scratch address");
+    if (id == 0) {
+        status = current_context_id(&id);
+        if (status != FX_OK) return status;
+    }
+    if (id != 0) g_static_scratch_by_context.emplace_back(id, static_cast<float*>(address));
+    *out = static_cast<float*>(address);
     return FX_OK;
 }
 
@@ -668,6 +726,14 @@ extern "C" fx_status fx_gqa_decode_attention_static_scratch_f32(
     const float* value_cache, const int64_t* value_strides4, const float* mask, const int64_t* mask_sizes4,
     const int64_t* mask_strides4, const int64_t* cache_length, float* output, float scale, int64_t batch,
     int64_t query_heads, int64_t kv_heads, int64_t capacity, int64_t head_dim, void* stream) {
+    // The limits fx_gqa_decode_attention_f32 enforces, checked before the
+    // scratch size is computed (the size helper also refuses on overflow).
+    FX_REQUIRE(batch > 0 && query_heads > 0 && kv_heads > 0 && capacity > 0 && head_dim > 0,
+               "fx_gqa_decode_attention_static_scratch_f32: sizes must be positive");
+    FX_REQUIRE(batch <= 65535 && kv_heads <= 65535 && query_heads % kv_heads == 0 &&
+                   query_heads / kv_heads <= fx::kOpMaxGroup && head_dim <= fx::kOpMaxDim,
+               "fx_gqa_decode_attention_static_scratch_f32: batch and KV heads must be <= 65535, at most 16 "
+               "query heads per KV head, head_dim <= 256");
     const int64_t needed = fx_gqa_decode_attention_workspace_floats(batch, query_heads, capacity, head_dim);
     if (needed > fx::kStaticScratchFloats) {
         fx::set_error("fx_gqa_decode_attention_static_scratch_f32: batch * query_heads * ceil(capacity / 128) * "

@@ -101,7 +101,8 @@ FX_API fx_status fx_packed_qkv_rope_cache_f32(const float* packed_qkv, const int
 
 /* Floats of split-K workspace fx_gqa_decode_attention_f32 needs:
  * batch * query_heads * ceil(capacity / 128) * (head_dim + 2), the layout of
- * the reference's workspace [B, Hq, chunks, D + 2]. */
+ * the reference's workspace [B, Hq, chunks, D + 2]; 0 for non-positive sizes,
+ * INT64_MAX when the product overflows (no workspace is large enough). */
 FX_API int64_t fx_gqa_decode_attention_workspace_floats(int64_t batch, int64_t query_heads, int64_t capacity,
                                                  int64_t head_dim);
 
@@ -133,9 +134,11 @@ FX_API fx_status fx_gqa_decode_attention_f32(const float* query, const int64_t* 
  * counterpart in the reference.  The split-K partials live in a file-scope
  * device array of fx_gqa_decode_attention_static_scratch_floats() floats
  * (1 MiB), resident on every device that loads the library until exit;
- * larger problems are rejected with FX_ERR_INVALID.  All calls on a device
- * share the array (calls that overlap on the GPU race); the first call on a
- * device looks up its address and should come before any stream capture.
+ * larger problems, and sizes beyond fx_gqa_decode_attention_f32's limits, are
+ * rejected with FX_ERR_INVALID.  All calls on a device share the array (calls
+ * that overlap on the GPU race).  The array's address belongs to a CUDA
+ * context: the first call in each context (the primary context, or one the
+ * host made current) looks it up and should come before any stream capture.
  * Calls no allocator. */
 FX_API int64_t fx_gqa_decode_attention_static_scratch_floats(void);
 FX_API fx_status fx_gqa_decode_attention_static_scratch_f32(
@@ -235,7 +238,8 @@ typedef struct fx_decode_buffers {
     float* final_norm_output;    /* [576] */
     float* attention_workspace;  /* split-K partials */
     int64_t stable_buffer_bytes; /* token + logits + generated + step + position + length */
-    uint64_t* timeline;          /* per-CTA %globaltimer stamps of the last step, or NULL
+    uint64_t* timeline;          /* per-CTA stamps of the last step (SM cycle counter in the
+                                    high 32 bits, %globaltimer ns in the low 32), or NULL
                                     (enabled by FLUX_B200_TIMELINE=1 at create) */
     int64_t timeline_ctas;
     int64_t timeline_events;     /* stamps per CTA */

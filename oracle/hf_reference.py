@@ -21,41 +21,12 @@ import time
 
 import numpy as np
 import torch
-from transformers import DynamicCache, LlamaConfig, LlamaForCausalLM
+from transformers import DynamicCache, LlamaForCausalLM
 
 from oracle import smollm2
-
-
-def smollm2_config(vocab_size: int = 49152, max_positions: int = 8320, layers: int = 30) -> LlamaConfig:
-    """SmolLM2-135M geometry (30 x 576, MLP 1536, 9/3 heads x 64, tied)."""
-    config = LlamaConfig(
-        hidden_size=576, intermediate_size=1536, num_hidden_layers=layers,
-        num_attention_heads=9, num_key_value_heads=3, head_dim=64,
-        vocab_size=vocab_size, max_position_embeddings=max_positions,
-        rms_norm_eps=1e-5, rope_theta=1.0e5, tie_word_embeddings=True,
-        attention_bias=False, attention_dropout=0.0, mlp_bias=False,
-    )
-    config._attn_implementation = "eager"
-    return config
-
-
-def reference_runtime_config() -> LlamaConfig:
-    """The full-geometry, vocab-128 configuration of the reference's runtime
-    tests (``tests/test_system.py:318-335``): untied, default RoPE theta."""
-    config = LlamaConfig(
-        hidden_size=576, intermediate_size=1536, num_hidden_layers=30,
-        num_attention_heads=9, num_key_value_heads=3, head_dim=64,
-        vocab_size=128, max_position_embeddings=8192, rms_norm_eps=1e-5,
-        attention_bias=False, attention_dropout=0.0, mlp_bias=False,
-    )
-    config._attn_implementation = "eager"
-    return config
-
-
-def build_model(config: LlamaConfig, seed: int) -> LlamaForCausalLM:
-    """Seeded CPU FP32 model in eval mode (``torch.manual_seed`` then HF init)."""
-    torch.manual_seed(seed)
-    return LlamaForCausalLM(config).float().eval()
+# The seeded workload models are defined beside the other seeded inputs (the
+# GPU path and the benchmark build the same models without importing the oracle).
+from tests.golden.inputs import build_model, reference_runtime_config, smollm2_config  # noqa: F401
 
 
 def numpy_state(model: torch.nn.Module) -> dict[str, np.ndarray]:

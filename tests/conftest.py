@@ -17,7 +17,7 @@ GOLDEN = ROOT / "tests" / "golden"
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a) and the built library")
-    from oracle.host import limit_threads
+    from tests.host import limit_threads
     limit_threads()
 
 

@@ -17,6 +17,46 @@ import torch
 EPSILON = 1e-5
 
 
+# ------------------------------------------------------------ seeded models
+# The real SmolLM2 checkpoint is not available offline; the workloads use the
+# same architecture with seeded random init (transformers' default N(0, 0.02)
+# linear / embedding init, unit norms), built on the CPU in FP32.
+
+def smollm2_config(vocab_size: int = 49152, max_positions: int = 8320, layers: int = 30) -> "LlamaConfig":
+    """SmolLM2-135M geometry (30 x 576, MLP 1536, 9/3 heads x 64, tied)."""
+    from transformers import LlamaConfig
+    config = LlamaConfig(
+        hidden_size=576, intermediate_size=1536, num_hidden_layers=layers,
+        num_attention_heads=9, num_key_value_heads=3, head_dim=64,
+        vocab_size=vocab_size, max_position_embeddings=max_positions,
+        rms_norm_eps=1e-5, rope_theta=1.0e5, tie_word_embeddings=True,
+        attention_bias=False, attention_dropout=0.0, mlp_bias=False,
+    )
+    config._attn_implementation = "eager"
+    return config
+
+
+def reference_runtime_config() -> "LlamaConfig":
+    """The full-geometry, vocab-128 configuration of the reference's runtime
+    tests (``tests/test_system.py:318-335``): untied, default RoPE theta."""
+    from transformers import LlamaConfig
+    config = LlamaConfig(
+        hidden_size=576, intermediate_size=1536, num_hidden_layers=30,
+        num_attention_heads=9, num_key_value_heads=3, head_dim=64,
+        vocab_size=128, max_position_embeddings=8192, rms_norm_eps=1e-5,
+        attention_bias=False, attention_dropout=0.0, mlp_bias=False,
+    )
+    config._attn_implementation = "eager"
+    return config
+
+
+def build_model(config: "LlamaConfig", seed: int) -> "LlamaForCausalLM":
+    """Seeded CPU FP32 model in eval mode (``torch.manual_seed`` then HF init)."""
+    from transformers import LlamaForCausalLM
+    torch.manual_seed(seed)
+    return LlamaForCausalLM(config).float().eval()
+
+
 def wave(shape) -> torch.Tensor:
     """``sin(0.013 i) + cos(0.007 i)`` -- ``tests/test_ops.py:71-73``."""
     values = torch.arange(math.prod(shape), dtype=torch.float32)

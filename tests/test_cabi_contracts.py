@@ -117,6 +117,24 @@ def test_static_scratch_attention_refuses_oversized_problems_before_the_gpu():
     _refused(status, _native.FX_ERR_INVALID, "static array")
 
 
+def test_attention_workspace_size_refuses_overflowing_products():
+    """A product that does not fit int64 reports INT64_MAX (no workspace is
+    large enough) instead of wrapping to a small size that would pass the
+    static-array and workspace checks."""
+    lib = _native.load()
+    int64_max = (1 << 63) - 1
+    assert lib.fx_gqa_decode_attention_workspace_floats(1 << 20, 1 << 20, 1 << 40, 64) == int64_max
+    assert lib.fx_gqa_decode_attention_workspace_floats(1, 9, int64_max, 64) == int64_max
+    assert lib.fx_gqa_decode_attention_workspace_floats(0, 9, 1024, 64) == 0
+    strides = _native.int64_array([1, 1, 1, 1])
+    # query heads up to 16 x KV heads and head_dim <= 256 are checked before any size product
+    for hq, hkv, d in ((1 << 40, 1 << 10, 64), (9, 3, 1 << 20), ((1 << 20) * 16, 1 << 20, 64)):
+        status = lib.fx_gqa_decode_attention_static_scratch_f32(
+            FAKE, strides, FAKE, strides, FAKE, strides, None, None, None, None, FAKE, 0.125, 1, hq, hkv, 1024, d,
+            None)
+        _refused(status, _native.FX_ERR_INVALID, "head_dim <= 256")
+
+
 C_CALLER = r"""
 #include "flux_b200.h"
 #include <stdio.h>

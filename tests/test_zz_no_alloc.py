@@ -22,9 +22,12 @@ pytestmark = pytest.mark.gpu
 
 
 def _call(lib, native, q, k, v, mask, length, out, *, workspace=None):
+    if mask is None:
+        mask_args = (None, None, None)
+    else:
+        mask_args = (mask.data_ptr(), native.int64_array(mask.shape), native.int64_array(mask.stride()))
     args = (q.data_ptr(), native.int64_array(q.stride()), k.data_ptr(), native.int64_array(k.stride()),
-            v.data_ptr(), native.int64_array(v.stride()), mask.data_ptr(), native.int64_array(mask.shape),
-            native.int64_array(mask.stride()), length.data_ptr(), out.data_ptr())
+            v.data_ptr(), native.int64_array(v.stride()), *mask_args, length.data_ptr(), out.data_ptr())
     sizes = (0.125, q.shape[0], q.shape[1], k.shape[1], k.shape[2], q.shape[3],
              torch.cuda.current_stream().cuda_stream)
     if workspace is None:
@@ -32,10 +35,18 @@ def _call(lib, native, q, k, v, mask, length, out, *, workspace=None):
     return lib.fx_gqa_decode_attention_f32(*args, workspace.data_ptr(), workspace.numel(), *sizes)
 
 
-def test_static_scratch_entry_matches_the_allocating_entry():
+@pytest.mark.parametrize("masked", [True, False], ids=["masked", "compact"])
+def test_static_scratch_entry_matches_the_allocating_entry(masked, ops_golden):
+    """Masked calls take the generic partial + merge kernels; unmasked calls
+    over contiguous SmolLM2-shaped caches take the TMA-staged compact chunk
+    kernel, here with the static array as its partials (the allocating entry
+    gets a workspace of exactly the partials, so both run the chunk kernel
+    plus the separate merge kernel)."""
     from flux_b200 import _native
     lib = _native.load()
     q, k, v, mask = (t.cuda() for t in gi.gqa_inputs(1024))
+    if not masked:
+        mask = None
     for length_value in (777, 1024):  # two calls in a row, different valid lengths
         length = torch.tensor(length_value, device="cuda")
         floats = lib.fx_gqa_decode_attention_workspace_floats(1, 9, 1024, 64)
@@ -46,6 +57,9 @@ def test_static_scratch_entry_matches_the_allocating_entry():
         _native.check(_call(lib, _native, q, k, v, mask, length, actual))
         torch.cuda.synchronize()
         np.testing.assert_allclose(actual.cpu().numpy(), expected.cpu().numpy(), rtol=2e-5, atol=1e-6)
+        if masked and length_value == 777:
+            # the reference's own operator oracle on the same seeded inputs
+            np.testing.assert_allclose(actual.cpu().numpy(), ops_golden["gqa1024_len777"], rtol=2e-5, atol=1e-6)
 
 
 def test_static_scratch_entry_rejects_sizes_beyond_its_array():
