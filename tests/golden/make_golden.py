@@ -3,7 +3,11 @@
 Run in a container that has the reference checkout (it is read-only and not
 available on the GPU box):
 
-    PYTHONPATH=/path/to/reference:. python tests/golden/make_golden.py
+    FLUX_REFERENCE=<reference checkout> python tests/golden/make_golden.py
+
+(``FLUX_REFERENCE`` defaults to a ``reference`` directory beside this
+repository.  The reference's ``flux`` package is put first on ``sys.path``, so
+it, not this repository's ``flux`` compatibility package, is the one run.)
 
 Op-level goldens come from the reference's own Python operator oracles
 (``flux/ops/*.py``) and transformers' ``apply_rotary_pos_emb``.  Model-level
@@ -17,6 +21,7 @@ inputs are stored.  Large bit-exact outputs are stored as SHA-256 digests.
 from __future__ import annotations
 
 import hashlib
+import os
 import sys
 from pathlib import Path
 
@@ -27,11 +32,17 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parents[1]))
 
 from tests.golden import inputs as gi  # noqa: E402
-
-import flux.ops as ref_ops  # noqa: E402  (the reference package)
+from oracle import hf_reference as hf  # noqa: E402
 from transformers.models.llama.modeling_llama import apply_rotary_pos_emb  # noqa: E402
 
-from oracle import hf_reference as hf  # noqa: E402
+REFERENCE = Path(os.environ.get("FLUX_REFERENCE") or HERE.parents[2] / "reference").resolve()
+sys.path.insert(0, str(REFERENCE))
+for _name in [m for m in sys.modules if m == "flux" or m.startswith("flux.")]:
+    del sys.modules[_name]
+import flux.ops as ref_ops  # noqa: E402  (the reference package)
+
+if not Path(ref_ops.__file__).resolve().is_relative_to(REFERENCE):
+    raise SystemExit(f"flux.ops resolved to {ref_ops.__file__}, not the reference checkout at {REFERENCE}")
 
 
 def digest(t: torch.Tensor) -> str:
