@@ -27,8 +27,9 @@
 // then the LM head (its vocab rows and greedy candidate; the last CTA to
 // arrive picks the token, advances the device state and the step epoch).
 //
-// The split-K sums are exact integer adds of values rounded to 2^-32, so the
-// result does not depend on the order the CTAs arrive in.  Every wait
+// The split-K sums are exact integer adds of values rounded to 2^-29, so the
+// result does not depend on the order the CTAs arrive in (partials of 2^13 or
+// more in magnitude go through an FP64 overflow word instead).  Every wait
 // (mbarrier, tagged word, counter) is bounded by %globaltimer; on expiry the
 // CTA sets error bit 2, drains its copies in flight and returns, and the
 // other CTAs give up at their next wait once they see the error word.
@@ -59,24 +60,29 @@ constexpr float kLog2e = 1.4426950408889634f;            // log2(e): scores kept
 constexpr float kLn2 = 0.6931471805599453f;              // ln(2)
 constexpr int kMaxOBlocks = 2;                           // needs >= 24 chunks per kv head
 constexpr int kMaxFeatures = 12;                         // needs grid >= 128
-// Tally words of the split-K sums: [7-bit contributor count | 5-bit count
-// of out-of-range contributors | 52-bit sum of biased fixed-point terms].  A
-// contributor adds 2^57 + 2^44 + round(y * 2^30) for |y| < 2^14, or
-// 2^57 + 2^52 when y is out of range or not finite; the 2^44 bias keeps
-// every term in (0, 2^45), so up to 127 terms never carry out of the sum.
-// The count and the sum travel in one atomic word: a reader that sees the
-// full count has the full sum.  More than 31 out-of-range contributors to
-// one word carry into the count, which a reader also reports as NaN.
+// Tally words of the split-K sums: [7-bit contributor count | 7-bit count
+// of contributors routed to the overflow word | 50-bit sum of biased
+// fixed-point terms].  A contributor with |y| < 2^13 adds
+// 2^57 + 2^42 + round(y * 2^29): the 2^42 bias keeps every term in (0, 2^43),
+// so up to 127 terms never carry out of the sum.  A contributor with a
+// larger (or non-finite) y adds y to the element's FP64 overflow word first,
+// then 2^57 + 2^50 to the tally word with release semantics, so a reader that
+// sees a non-zero overflow count and then fences reads the complete overflow
+// word.  The count and the sum travel in one atomic word: a reader that sees
+// the full count has the full sum.  Both counts fit 7 bits (at most 127
+// contributors per replica word), so neither carries into the other.
 constexpr int kTallyCountShift = 57;
-constexpr int kTallyBadShift = 52;
+constexpr int kTallyBadShift = 50;
 constexpr unsigned long long kTallyOne = 1ull << kTallyCountShift;
 constexpr unsigned long long kTallyBadOne = 1ull << kTallyBadShift;
 constexpr unsigned long long kTallyValueMask = kTallyBadOne - 1;
-constexpr long long kTallyBias = 1ll << 44;
-constexpr float kTallyScale = 1073741824.0f;                 // 2^30
-constexpr double kTallyUnit = 9.31322574615478515625e-10;    // 2^-30
-constexpr float kTallyLimit = 16384.0f;                      // |y| < 2^14
+constexpr unsigned long long kTallyCountMask = 0x7f;
+constexpr long long kTallyBias = 1ll << 42;
+constexpr float kTallyScale = 536870912.0f;                  // 2^29
+constexpr double kTallyUnit = 1.862645149230957031e-09;      // 2^-29
+constexpr float kTallyLimit = 8192.0f;                       // |y| < 2^13 in the fixed-point sum
 constexpr int kTallyWords = 2 * kStepAccReplicas * kHidden;  // one layer: (o_proj, down) x replicas x 576
+constexpr int kOverflowWords = 2 * kHidden;                  // one layer: (o_proj, down) x 576 FP64 overflow words
 
 // ------------------------------------------------------------- PTX helpers
 
@@ -159,6 +165,17 @@ __device__ __forceinline__ void red_tally(unsigned long long* p, unsigned long l
     asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+// Tally add that orders this thread's earlier writes (its overflow add) before it.
+__device__ __forceinline__ void red_tally_release(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ double ld_overflow(const double* p) {
+    double v;
+    asm volatile("ld.relaxed.gpu.global.f64 %0, [%1];" : "=d"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ uint32_t word_tag(unsigned long long v) { return static_cast<uint32_t>(v >> 32); }
 __device__ __forceinline__ float word_value(unsigned long long v) {
     return __uint_as_float(static_cast<uint32_t>(v));
@@ -169,10 +186,15 @@ __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 480;
 
 __device__ __forceinline__ int64_t min64(int64_t x, int64_t y) { return x < y ? x : y; }
 
+// A stamp packs the SM cycle counter (high 32 bits: precise durations
+// within a CTA) with %globaltimer in ns (low 32 bits: the common clock that
+// orders events across CTAs, coarse on some GPUs); both wrap after seconds.
 #define STEP_MARK(event)                                                                                  \
     do {                                                                                                  \
         if (a.timeline != nullptr && threadIdx.x == 0)                                                     \
-            a.timeline[static_cast<size_t>(blockIdx.x) * kStepTimelineEvents + (event)] = global_timer(); \
+            a.timeline[static_cast<size_t>(blockIdx.x) * kStepTimelineEvents + (event)] =                  \
+                (static_cast<unsigned long long>(static_cast<uint32_t>(clock64())) << 32) |                \
+                static_cast<uint32_t>(global_timer());                                                     \
     } while (0)
 #define LAYER_MARK(event) STEP_MARK(1 + kStepTimelinePerLayer * l + (event))
 
@@ -187,7 +209,48 @@ struct AttnScratch {
     float l[kConsumerWarps][kGroup];
 };
 
+// The CTA's fixed share of every phase, derived from (grid, CTA, position).
+struct Sched {
+    int t0, t1;          // QKV row-pair tasks
+    int replica;         // tally replica this CTA adds into (word offset)
+    int f0, f1;          // MLP feature blocks (4 features each)
+    int ob[kMaxOBlocks]; // attention-dim blocks (4 dims each) of kv head g
+    int nob;
+    int64_t v0, v1;      // vocab rows
+    int g, c;            // attention kv head / chunk (g < 0: none)
+    int64_t a0, a1;      // rows [a0, a1) of the valid length
+    int64_t cached_end;  // rows [a0, cached_end) stream through the ring
+    bool owns_new;       // the chunk holds row `pos` (read from the exchange)
+    bool has_rows;
+    int active;          // active chunks per kv head
+    int n_att, n_lm, per_layer, total;
+    int64_t pos, tok;
+    uint32_t epoch;
+};
+
+// Kernel parameters read inside the layer loop, copied to shared memory at
+// the start: the parameter block (~9 KB with the 60 tensor maps) does not
+// stay in the SM's constant cache, and a miss there costs an L2 round trip.
+struct HotParams {
+    const float* input_norm[kLayers];
+    const float* qkv[kLayers];
+    const float* post_norm[kLayers];
+    const float* gate_up[kLayers];
+    float scale[kLayers];
+    const float* key_cache;
+    const float* value_cache;
+    const float* final_norm;
+    const float* lm_head;
+    unsigned long long* x_qkv;
+    unsigned long long* x_partial;
+    int64_t capacity;
+    float eps;
+    int nch;
+};
+
 struct Shared {
+    HotParams hp;
+    Sched s;
     uint64_t full[kStepSlots];
     uint64_t empty[kStepSlots];
     alignas(16) float hraw[kHidden];          // layer input h
@@ -218,24 +281,7 @@ struct Shared {
 
 constexpr size_t kRingOffset = (sizeof(Shared) + 127) / 128 * 128;
 
-// The CTA's fixed share of every phase, derived from (grid, CTA, position).
-struct Sched {
-    int t0, t1;          // QKV row-pair tasks
-    int replica;         // tally replica this CTA adds into (word offset)
-    int f0, f1;          // MLP feature blocks (4 features each)
-    int ob[kMaxOBlocks]; // attention-dim blocks (4 dims each) of kv head g
-    int nob;
-    int64_t v0, v1;      // vocab rows
-    int g, c;            // attention kv head / chunk (g < 0: none)
-    int64_t a0, a1;      // rows [a0, a1) of the valid length
-    int64_t cached_end;  // rows [a0, cached_end) stream through the ring
-    bool owns_new;       // the chunk holds row `pos` (read from the exchange)
-    bool has_rows;
-    int active;          // active chunks per kv head
-    int n_att, n_lm, per_layer, total;
-    int64_t pos, tok;
-    uint32_t epoch;
-};
+
 
 // QKV task -> its two rows.  Tasks 0..287: q (head, d < 32) with partner
 // d + 32; 288..383: k likewise; 384..479: v rows 2t, 2t + 1.
@@ -300,8 +346,8 @@ __device__ void make_sched(const StepArgs& a, int G, int cta, Sched& s) {
 // feature block, 576 x 4].  LM head: [final norm], then 12-row vocab tiles.
 enum class TileOp { kCount, kLoad };
 
-__device__ uint32_t issue_tile(const StepArgs& a, const Sched& s, int k, unsigned char* dst, uint64_t* bar,
-                               TileOp op) {
+__device__ uint32_t issue_tile(const StepArgs& a, const HotParams& hp, const Sched& s, int k, unsigned char* dst,
+                               uint64_t* bar, TileOp op) {
     uint32_t off = 0;
     auto row_copy = [&](const float* src, uint32_t bytes) {
         if (op == TileOp::kLoad) bulk_load(dst + off, src, bytes, bar);
@@ -316,14 +362,14 @@ __device__ uint32_t issue_tile(const StepArgs& a, const Sched& s, int k, unsigne
     if (k < kLayers * s.per_layer) {
         const int l = k / s.per_layer;
         int sub = k % s.per_layer;
-        const StepLayer& L = a.layer[l];
+        const StepLayer& L = a.layer[l];  // only the tensor maps (their addresses) are used from here
         if (sub == 0) {
-            row_copy(L.input_norm, kRowBytes);
+            row_copy(hp.input_norm[l], kRowBytes);
             for (int task = s.t0; task < s.t1; ++task) {
                 int ra, rb, kind;
                 task_rows(task, ra, rb, kind);
-                row_copy(L.qkv + static_cast<int64_t>(ra) * kHidden, kRowBytes);
-                row_copy(L.qkv + static_cast<int64_t>(rb) * kHidden, kRowBytes);
+                row_copy(hp.qkv[l] + static_cast<int64_t>(ra) * kHidden, kRowBytes);
+                row_copy(hp.qkv[l] + static_cast<int64_t>(rb) * kHidden, kRowBytes);
             }
             return off;
         }
@@ -331,20 +377,20 @@ __device__ uint32_t issue_tile(const StepArgs& a, const Sched& s, int k, unsigne
         if (sub < s.n_att) {
             const int64_t r0 = s.a0 + static_cast<int64_t>(sub) * kStepAttnRows;
             const int64_t n = min64(kStepAttnRows, s.cached_end - r0);
-            const int64_t base = ((static_cast<int64_t>(l) * kKVHeads + s.g) * a.capacity + r0) * kHeadDim;
-            row_copy(a.key_cache + base, static_cast<uint32_t>(n * kHeadDim * 4));
-            row_copy(a.value_cache + base, static_cast<uint32_t>(n * kHeadDim * 4));
+            const int64_t base = ((static_cast<int64_t>(l) * kKVHeads + s.g) * hp.capacity + r0) * kHeadDim;
+            row_copy(hp.key_cache + base, static_cast<uint32_t>(n * kHeadDim * 4));
+            row_copy(hp.value_cache + base, static_cast<uint32_t>(n * kHeadDim * 4));
             return off;
         }
         sub -= s.n_att;
         const int nf = (s.f1 - s.f0) * kStepBlock;
         if (sub == 0) {
-            row_copy(L.post_norm, kRowBytes);
+            row_copy(hp.post_norm[l], kRowBytes);
             for (int j = 0; j < s.nob; ++j) strip_copy(&L.o_map, s.g * kGroup * kHeadDim + s.ob[j] * kStepBlock);
         } else if (sub == 1) {
-            row_copy(L.gate_up + static_cast<int64_t>(s.f0) * kStepBlock * kHidden, nf * kRowBytes);
+            row_copy(hp.gate_up[l] + static_cast<int64_t>(s.f0) * kStepBlock * kHidden, nf * kRowBytes);
         } else if (sub == 2) {
-            row_copy(L.gate_up + static_cast<int64_t>(kInter + s.f0 * kStepBlock) * kHidden, nf * kRowBytes);
+            row_copy(hp.gate_up[l] + static_cast<int64_t>(kInter + s.f0 * kStepBlock) * kHidden, nf * kRowBytes);
         } else {
             for (int f = s.f0; f < s.f1; ++f) strip_copy(&L.down_map, f * kStepBlock);
         }
@@ -352,12 +398,12 @@ __device__ uint32_t issue_tile(const StepArgs& a, const Sched& s, int k, unsigne
     }
     const int j = k - kLayers * s.per_layer;
     if (j == 0) {
-        row_copy(a.final_norm, kRowBytes);
+        row_copy(hp.final_norm, kRowBytes);
         return off;
     }
     const int64_t r0 = s.v0 + static_cast<int64_t>(j - 1) * kStepLmRows;
     const int64_t n = min64(kStepLmRows, s.v1 - r0);
-    row_copy(a.lm_head + r0 * kHidden, static_cast<uint32_t>(n * kRowBytes));
+    row_copy(hp.lm_head + r0 * kHidden, static_cast<uint32_t>(n * kRowBytes));
     return off;
 }
 
@@ -527,13 +573,14 @@ __device__ __forceinline__ unsigned long long tally_expected(int G, int r) {
 
 // dst[i] = base[i] + the split-K sum i, once every contributor's add has
 // landed in every replica word (bounded polls; no fence needed: count and
-// sum share the word).  NaN where a contributor's partial was out of range.
-// The per-warp sums of squares of dst are left in sh.scratch for normalise()
-// / norm_inverse(); with `norm_w`, also xg[i] = dst[i] * norm_w[i] (the
-// RMSNorm weight applied, the 1 / rms factor left to the caller's dot
-// products).
-__device__ bool tally_read(const StepArgs& a, Shared& sh, const unsigned long long* acc, const float* base,
-                           float* dst, int G, const float* norm_w = nullptr, float* xg = nullptr) {
+// sum share the word).  Where contributors were out of the fixed-point range,
+// their FP64 overflow word is added after an acquire fence.  The per-warp
+// sums of squares of dst are left in sh.scratch for normalise() /
+// norm_inverse(); with `norm_w`, also xg[i] = dst[i] * norm_w[i] (the RMSNorm
+// weight applied, the 1 / rms factor left to the caller's dot products).
+__device__ bool tally_read(const StepArgs& a, Shared& sh, const unsigned long long* acc, const double* overflow,
+                           const float* base, float* dst, int G, const float* norm_w = nullptr,
+                           float* xg = nullptr) {
     float ss = 0.0f;  // sum of squares of dst (per-warp partials left in scratch for the RMSNorm)
     for (int i = threadIdx.x; i < kHidden; i += kStepConsumers) {
         unsigned long long w[kStepAccReplicas];
@@ -565,13 +612,20 @@ __device__ bool tally_read(const StepArgs& a, Shared& sh, const unsigned long lo
             }
         }
         long long total = 0;
-        bool bad = false;
+        unsigned long long routed = 0;  // contributors whose value went to the overflow word
 #pragma unroll
         for (int r = 0; r < kStepAccReplicas; ++r) {
-            bad = bad || (w[r] >> kTallyBadShift) != (tally_expected(G, r) << (kTallyCountShift - kTallyBadShift));
-            total += static_cast<long long>(w[r] & kTallyValueMask) - static_cast<long long>(tally_expected(G, r)) * kTallyBias;
+            const unsigned long long bad = (w[r] >> kTallyBadShift) & kTallyCountMask;
+            routed += bad;
+            total += static_cast<long long>(w[r] & kTallyValueMask) -
+                     static_cast<long long>(tally_expected(G, r) - bad) * kTallyBias;
         }
-        dst[i] = bad ? __int_as_float(0x7fc00000) : base[i] + static_cast<float>(static_cast<double>(total) * kTallyUnit);
+        double sum = static_cast<double>(total) * kTallyUnit;
+        if (routed != 0) {
+            asm volatile("fence.acq_rel.gpu;" ::: "memory");
+            sum += ld_overflow(overflow + i);
+        }
+        dst[i] = base[i] + static_cast<float>(sum);
         ss = fmaf(dst[i], dst[i], ss);
         if (xg != nullptr) xg[i] = dst[i] * norm_w[i];
     }
@@ -620,8 +674,10 @@ __device__ __forceinline__ float row_dot(const float* row, const float* xs, int 
 }
 
 // Split-K slice: y[r] = sum_j coef[j] * strip[j / 4][r][j % 4] for the 576
-// rows r (blocks = 0: zeros), added into this CTA's replica of the tally.
-__device__ void tally_products(const float* strips, const float* coef, int blocks, unsigned long long* acc) {
+// rows r (blocks = 0: zeros), added into this CTA's replica of the tally;
+// values outside the fixed-point range go through the FP64 overflow word.
+__device__ void tally_products(const float* strips, const float* coef, int blocks, unsigned long long* acc,
+                               double* overflow) {
     for (int r = threadIdx.x; r < kHidden; r += kStepConsumers) {
         float y = 0.0f;
         for (int b = 0; b < blocks; ++b) {
@@ -632,11 +688,12 @@ __device__ void tally_products(const float* strips, const float* coef, int block
             y = fmaf(w.z, c.z, y);
             y = fmaf(w.w, c.w, y);
         }
-        const unsigned long long term =
-            fabsf(y) < kTallyLimit
-                ? kTallyOne + static_cast<unsigned long long>(kTallyBias + __float2ll_rn(y * kTallyScale))
-                : kTallyOne + kTallyBadOne;
-        red_tally(acc + r, term);
+        if (fabsf(y) < kTallyLimit) {
+            red_tally(acc + r, kTallyOne + static_cast<unsigned long long>(kTallyBias + __float2ll_rn(y * kTallyScale)));
+        } else {
+            atomicAdd(overflow + r, static_cast<double>(y));
+            red_tally_release(acc + r, kTallyOne + kTallyBadOne);
+        }
     }
 }
 
@@ -659,11 +716,27 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     const int G = gridDim.x, cta = blockIdx.x;
 
     if (*reinterpret_cast<volatile int*>(a.stop) != 0) return;  // generation already ended on EOS (uniform)
-    Sched s;
-    make_sched(a, G, cta, s);
-    if (s.pos < 0 || s.pos >= a.capacity) {
-        if (cta == 0 && tid == 0) atomicOr(a.error, 1);
-        return;
+    // The schedule is uniform over the CTA and read throughout the step: it
+    // lives in shared memory (as a per-thread struct it was spilled to local
+    // memory, 64 KB per CTA, more than the L1 left beside the ring).
+    if (tid == 0) make_sched(a, G, cta, sh.s);
+    if (tid < kLayers) {
+        const StepLayer& L = a.layer[tid];
+        sh.hp.input_norm[tid] = L.input_norm;
+        sh.hp.qkv[tid] = L.qkv;
+        sh.hp.post_norm[tid] = L.post_norm;
+        sh.hp.gate_up[tid] = L.gate_up;
+        sh.hp.scale[tid] = L.scale;
+    } else if (tid == 32) {
+        sh.hp.key_cache = a.key_cache;
+        sh.hp.value_cache = a.value_cache;
+        sh.hp.final_norm = a.final_norm;
+        sh.hp.lm_head = a.lm_head;
+        sh.hp.x_qkv = a.x.qkv;
+        sh.hp.x_partial = a.x.partial;
+        sh.hp.capacity = a.capacity;
+        sh.hp.eps = a.eps;
+        sh.hp.nch = a.nch;
     }
     if (tid == 0) {
         for (int i = 0; i < kStepSlots; ++i) {
@@ -674,9 +747,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         sh.abort = 0;
         sh.consumed = 0;
         sh.issued = 0;
-        if (cta == 0) *a.length = s.pos + 1;
     }
     __syncthreads();
+    const Sched& s = sh.s;
+    if (s.pos < 0 || s.pos >= a.capacity) {  // uniform
+        if (cta == 0 && tid == 0) atomicOr(a.error, 1);
+        return;
+    }
+    if (cta == 0 && tid == 0) *a.length = s.pos + 1;
     STEP_MARK(0);
 
     if (warp == kProducerWarp) {
@@ -686,10 +764,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 const int slot = k % kStepSlots;
                 if (!producer_wait(a, sh, &sh.empty[slot], (static_cast<uint32_t>(k / kStepSlots) & 1u) ^ 1u)) break;
                 unsigned char* dst = ring + static_cast<size_t>(slot) * kStepSlotBytes;
-                const uint32_t bytes = issue_tile(a, s, k, dst, &sh.full[slot], TileOp::kCount);
+                const uint32_t bytes = issue_tile(a, sh.hp, s, k, dst, &sh.full[slot], TileOp::kCount);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 mbar_arrive_expect_tx(&sh.full[slot], bytes);
-                issue_tile(a, s, k, dst, &sh.full[slot], TileOp::kLoad);
+                issue_tile(a, sh.hp, s, k, dst, &sh.full[slot], TileOp::kLoad);
                 sh.issued = k + 1;
             }
         }
@@ -699,15 +777,25 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         const int64_t cap = a.capacity;
         // This step's tallies: set (epoch & 1), [layer][o_proj | down][replica][576].
         unsigned long long* tallies = a.x.tally + static_cast<size_t>(s.epoch & 1u) * kLayers * kTallyWords;
+        double* overflows = a.x.overflow + static_cast<size_t>(s.epoch & 1u) * kLayers * kOverflowWords;
         auto mid_tally = [&](int l) { return tallies + static_cast<size_t>(l) * kTallyWords; };
         auto down_tally = [&](int l) { return tallies + static_cast<size_t>(l) * kTallyWords + kTallyWords / 2; };
-        // Zero the other set for the next step (it was last read by the previous launch).
+        auto mid_overflow = [&](int l) { return overflows + static_cast<size_t>(l) * kOverflowWords; };
+        auto down_overflow = [&](int l) { return overflows + static_cast<size_t>(l) * kOverflowWords + kHidden; };
+        // Zero the other set (tallies and overflow words) for the next step
+        // (it was last read by the previous launch).
         {
-            unsigned long long* next = a.x.tally + static_cast<size_t>((s.epoch + 1u) & 1u) * kLayers * kTallyWords;
-            const size_t n = static_cast<size_t>(kLayers) * kTallyWords;
+            const uint32_t next = (s.epoch + 1u) & 1u;
+            unsigned long long* words = a.x.tally + static_cast<size_t>(next) * kLayers * kTallyWords;
+            size_t n = static_cast<size_t>(kLayers) * kTallyWords;
             for (size_t i = static_cast<size_t>(cta) * n / G + tid; i < static_cast<size_t>(cta + 1) * n / G;
                  i += kStepConsumers)
-                st_zero(next + i);
+                st_zero(words + i);
+            words = reinterpret_cast<unsigned long long*>(a.x.overflow + static_cast<size_t>(next) * kLayers * kOverflowWords);
+            n = static_cast<size_t>(kLayers) * kOverflowWords;
+            for (size_t i = static_cast<size_t>(cta) * n / G + tid; i < static_cast<size_t>(cta + 1) * n / G;
+                 i += kStepConsumers)
+                st_zero(words + i);
         }
         int k = 0;
         const int inject = *a.inject;
@@ -746,12 +834,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 }
                 consumer_sync();
                 if (sh.abort) goto done;
-            } else if (!tally_read(a, sh, down_tally(l - 1), sh.mid, sh.hraw, G, t, sh.xs)) {
+            } else if (!tally_read(a, sh, down_tally(l - 1), down_overflow(l - 1), sh.mid, sh.hraw, G, t, sh.xs)) {
                 goto done;
             }
             LAYER_MARK(0);
             {
-                const float inv = norm_inverse(sh, a.eps);
+                const float inv = norm_inverse(sh, sh.hp.eps);
                 if (warp < s.t1 - s.t0) {
                     int ra, rb, kind;
                     task_rows(s.t0 + warp, ra, rb, kind);
@@ -779,7 +867,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     }
                     // lanes 0..3 of each half publish the replicas
                     if (l16 < kStepReplicas)
-                        st_word(a.x.qkv + (parity(l) * kStepReplicas + l16) * kQKV + row, tag, out);
+                        st_word(sh.hp.x_qkv + (parity(l) * kStepReplicas + l16) * kQKV + row, tag, out);
                 }
                 release(sh, k++);
             }
@@ -787,11 +875,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 
             // ------------------------------------------------------ phase B
             if (s.has_rows) {
-                const unsigned long long* qkv = a.x.qkv + (parity(l) * kStepReplicas + cta % kStepReplicas) * kQKV;
+                const unsigned long long* qkv = sh.hp.x_qkv + (parity(l) * kStepReplicas + cta % kStepReplicas) * kQKV;
                 if (!poll_attention_inputs(a, sh, qkv, s.g, s.owns_new, tag)) goto done;
                 LAYER_MARK(2);
                 // Scores in base-2 units: s2 = (q . k) * scale * log2(e), so p = exp2(s2 - max).
-                const float scale2 = a.layer[l].scale * kLog2e;
+                const float scale2 = sh.hp.scale[l] * kLog2e;
                 // Score groups of 4 lanes; lane (gl, l4) of a warp covers the 16-byte
                 // chunks l4 + 4 m of a row, visiting m = (j + gl) % 4 at step j so the
                 // 32 lanes of one load hit 8 distinct bank groups.
@@ -828,10 +916,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     const int rows = cached + (with_new ? 1 : 0);
                     // The first batch needs no barrier of its own (the poll's barrier
                     // precedes it; an abort is read after the score barrier below).
-                    if (j == 0)
+                    if (j == 0) {
                         wait_tiles(a, sh, k, nb);
-                    else if (!acquire_batch(a, sh, k, nb))
+                        LAYER_MARK(3);
+                    } else if (!acquire_batch(a, sh, k, nb)) {
                         goto done;
+                    }
                     auto tile_base = [&](int gi) {
                         return reinterpret_cast<const float*>(
                             ring + static_cast<size_t>((k + gi / kStepAttnRows) % kStepSlots) * kStepSlotBytes);
@@ -958,7 +1048,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     }
                     j += nb;
                 } while (j < s.n_att);
-                LAYER_MARK(3);
+                LAYER_MARK(4);
                 // Sum the row splits: the warp's two halves by a shuffle, then the
                 // 15 warps' sums.
 #pragma unroll
@@ -986,8 +1076,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                         total += sh.att.l[w][h];
                         acc += sh.att.o[w][h][d];
                     }
-                    unsigned long long* pw = a.x.partial + parity(l) * (static_cast<size_t>(kQHeads) * a.nch * kStepPartial) +
-                                             ((static_cast<size_t>(s.g) * kGroup + h) * a.nch + s.c) * kStepPartial;
+                    const int nch = sh.hp.nch;
+                    unsigned long long* pw = sh.hp.x_partial + parity(l) * (static_cast<size_t>(kQHeads) * nch * kStepPartial) +
+                                             ((static_cast<size_t>(s.g) * kGroup + h) * nch + s.c) * kStepPartial;
                     st_word(pw + 2 + d, tag, acc);
                     if (d == 0) {
                         st_word(pw, tag, mx);
@@ -997,7 +1088,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 // no barrier: phase M uses other shared arrays, and the next writes of
                 // sh.att come after many barriers (next layer)
             }
-            LAYER_MARK(4);
+            LAYER_MARK(5);
 
             // ------------------------------------------------------ phase M
             // Merge the owned attention dims over all chunks, then add their
@@ -1005,15 +1096,16 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             {
                 const int nd = s.nob * kStepBlock;
                 if (nd > 0) {
-                    const unsigned long long* part = a.x.partial +
-                                                     parity(l) * (static_cast<size_t>(kQHeads) * a.nch * kStepPartial) +
-                                                     static_cast<size_t>(s.g) * kGroup * a.nch * kStepPartial;
+                    const int nch = sh.hp.nch;
+                    const unsigned long long* part = sh.hp.x_partial +
+                                                     parity(l) * (static_cast<size_t>(kQHeads) * nch * kStepPartial) +
+                                                     static_cast<size_t>(s.g) * kGroup * nch * kStepPartial;
                     const int act = s.active;
                     for (int it = tid; it < nd * act; it += kStepConsumers) {
                         const int q = it / act, cc = it % act;
                         const int j = s.ob[q / kStepBlock] * kStepBlock + q % kStepBlock;
                         const int h = j / kHeadDim, d = j % kHeadDim;
-                        const unsigned long long* p = part + (static_cast<size_t>(h) * a.nch + cc) * kStepPartial;
+                        const unsigned long long* p = part + (static_cast<size_t>(h) * nch + cc) * kStepPartial;
                         const unsigned long long* const src[3] = {p, p + 1, p + 2 + d};
                         unsigned long long v[3] = {ld_word(src[0]), ld_word(src[1]), ld_word(src[2])};
                         poll_words3(a, sh, src, v, tag);
@@ -1023,7 +1115,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     }
                     consumer_sync();
                     if (sh.abort) goto done;
-                    LAYER_MARK(5);
+                    LAYER_MARK(6);
                     if (warp < nd) {
                         float mx = -INFINITY;
                         for (int cc = lane; cc < act; cc += 32) mx = fmaxf(mx, sh.mm[warp][cc]);
@@ -1041,21 +1133,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 }
                 const float* t = acquire(a, sh, ring, k);
                 if (t == nullptr) goto done;
+                LAYER_MARK(7);
                 for (int i = tid; i < kHidden; i += kStepConsumers) sh.wpost[i] = t[i];
-                tally_products(t + kHidden, sh.attn, s.nob, mid_tally(l) + s.replica);
+                tally_products(t + kHidden, sh.attn, s.nob, mid_tally(l) + s.replica, mid_overflow(l));
                 release(sh, k++);
             }
-            LAYER_MARK(6);
+            LAYER_MARK(8);
 
             // ------------------------------------------------------ phase D
             // gate, up and down tiles together; the barrier of the h' read also
             // publishes these waits (xs = h' * post-norm weight).
             wait_tiles(a, sh, k, 3);
-            if (!tally_read(a, sh, mid_tally(l), sh.hraw, sh.mid, G, sh.wpost, sh.xs)) goto done;
-            LAYER_MARK(7);
+            if (!tally_read(a, sh, mid_tally(l), mid_overflow(l), sh.hraw, sh.mid, G, sh.wpost, sh.xs)) goto done;
+            LAYER_MARK(9);
             {
                 const int nf = (s.f1 - s.f0) * kStepBlock;
-                const float inv = norm_inverse(sh, a.eps);
+                const float inv = norm_inverse(sh, sh.hp.eps);
                 // warp f: gate row f on lanes 0-15, up row f on lanes 16-31, SwiGLU on lane 0.
                 if (warp < nf) {
                     const float y = row_dot(slot_ptr(ring, k + half) + warp * kHidden, sh.xs, l16) * inv;
@@ -1063,12 +1156,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     if (lane == 0) sh.act[warp] = swiglu(y, up);
                 }
                 consumer_sync();
-                LAYER_MARK(8);
-                tally_products(slot_ptr(ring, k + 2), sh.act, s.f1 - s.f0, down_tally(l) + s.replica);
+                LAYER_MARK(10);
+                tally_products(slot_ptr(ring, k + 2), sh.act, s.f1 - s.f0, down_tally(l) + s.replica, down_overflow(l));
                 release_batch(sh, k, 3);
                 k += 3;
             }
-            LAYER_MARK(9);
+            LAYER_MARK(11);
         }
 
         // ---------------------------------------------------------- LM head
@@ -1077,10 +1170,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             float bv = 0.0f;
             long long bi = -1;
             if (s.n_lm > 0) {
-                if (!tally_read(a, sh, down_tally(kLayers - 1), sh.mid, sh.hraw, G)) goto done;
+                if (!tally_read(a, sh, down_tally(kLayers - 1), down_overflow(kLayers - 1), sh.mid, sh.hraw, G)) goto done;
                 wait_tiles(a, sh, k, 1);
                 const float* t = slot_ptr(ring, k);
-                normalise(sh, sh.hraw, t, a.eps);
+                normalise(sh, sh.hraw, t, sh.hp.eps);
                 if (sh.abort) goto done;
                 if (s.v0 == 0)
                     for (int i = tid; i < kHidden; i += kStepConsumers) a.final_norm_out[i] = sh.xs[i];
@@ -1194,7 +1287,7 @@ fx_status encode_strip_map(CUtensorMap* map, const float* base, uint64_t columns
 size_t step_exchange_words(int nch) {
     auto up = [](size_t w) { return (w + 31) / 32 * 32; };  // 256-byte sections
     return up(2ull * kStepReplicas * kQKV) + up(2ull * kQHeads * nch * kStepPartial) +
-           up(2ull * kLayers * kTallyWords);
+           up(2ull * kLayers * kTallyWords) + up(2ull * kLayers * kOverflowWords);
 }
 
 StepExchange step_exchange_views(unsigned long long* base, int nch) {
@@ -1206,6 +1299,8 @@ StepExchange step_exchange_views(unsigned long long* base, int nch) {
     x.partial = p;
     p += up(2ull * kQHeads * nch * kStepPartial);
     x.tally = p;
+    p += up(2ull * kLayers * kTallyWords);
+    x.overflow = reinterpret_cast<double*>(p);
     return x;
 }
 

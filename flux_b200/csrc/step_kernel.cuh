@@ -38,17 +38,21 @@ struct StepLayer {
 //    reader polls a word until it carries the tag of the current (step,
 //    layer), so one L2 round trip both waits for and delivers it.
 //  * o_proj and down are split-K over the CTAs; their partial sums meet in
-//    64-bit tally words [contributor count | out-of-range count | sum of
-//    biased 2^-30 fixed-point terms] -- integer adds, so the sum is exact
-//    and order-independent, and count and sum arrive in one atomic word: a
+//    64-bit tally words [contributor count | overflow count | sum of biased
+//    2^-29 fixed-point terms] -- integer adds, so the sum is exact and
+//    order-independent, and count and sum arrive in one atomic word: a
 //    reader polls until every word's count is complete, no fence needed.
-//    CTA c adds into replica c % 2; readers sum the replicas.  Every layer
-//    has its own tally words and the steps alternate between two sets; each
-//    step zeroes the set of the next step, which only a later launch reads.
+//    A partial outside the fixed-point range (|y| >= 2^13) is added to the
+//    element's FP64 overflow word instead (then counted with a release add).
+//    CTA c adds into replica c % kStepAccReplicas; readers sum the replicas.  Every layer
+//    has its own tally and overflow words and the steps alternate between two
+//    sets; each step zeroes the set of the next step, which only a later
+//    launch reads.
 struct StepExchange {
     unsigned long long* qkv;       // [2][kStepReplicas][960]
     unsigned long long* partial;   // [2][3][3][nch][66]
-    unsigned long long* tally;     // [2 steps][30][o_proj, down][2 replicas][576]
+    unsigned long long* tally;     // [2 steps][30][o_proj, down][kStepAccReplicas][576]
+    double* overflow;              // [2 steps][30][o_proj, down][576]
 };
 
 struct StepArgs {
@@ -79,14 +83,14 @@ struct StepArgs {
     int* stop;                // [0] set once a step produced the EOS token: later steps return at once
                               // [1] EOS token + 1 (0: no EOS)
     int nch;                  // attention chunks per kv head
-    unsigned long long* timeline;  // optional [grid][kStepTimelineEvents] %globaltimer stamps
+    unsigned long long* timeline;  // optional [grid][kStepTimelineEvents] (cycle << 32 | globaltimer) stamps
 };
 
-// Timeline events per CTA: 0 = start, then per layer 10 stamps (A: h ready,
-// done; B: q polled, cache tiles done, partial published; M: partials
-// polled, o_proj partial added; D: h' ready, gate/up done, down partial
-// added), then LM-head start and end.
-constexpr int kStepTimelinePerLayer = 10;
+// Timeline events per CTA: 0 = start, then per layer 12 stamps (A: h ready,
+// done; B: q polled, first cache tiles landed, cache tiles done, partial
+// published; M: partials polled, o_proj tile landed, o_proj partial added;
+// D: h' ready, gate/up done, down partial added), then LM-head start and end.
+constexpr int kStepTimelinePerLayer = 12;
 constexpr int kStepTimelineEvents = 1 + kStepTimelinePerLayer * kLayers + 2;
 
 // 64-bit words of the exchange region for `nch` chunks per kv head.

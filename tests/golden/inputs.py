@@ -10,11 +10,13 @@ with the same seed (CUDA RNG streams cannot be reproduced on a CPU host).
 from __future__ import annotations
 
 import math
+from pathlib import Path
 
 import numpy as np
 import torch
 
 EPSILON = 1e-5
+GOLDEN_DIR = Path(__file__).resolve().parent  # the committed .npz fixtures
 
 
 # ------------------------------------------------------------ seeded models
