@@ -64,6 +64,8 @@ def parse_args(argv=None):
     p.add_argument("--no-batched", action="store_true", help="skip the batched configuration")
     p.add_argument("--no-attention", action="store_true", help="skip the isolated-attention sweep")
     p.add_argument("--no-sweep", action="store_true", help="skip the context sweep of the batch-1 decode")
+    p.add_argument("--no-generation", action="store_true",
+                   help="skip configs[0] (128-token prompt, 128 greedy tokens end to end)")
     return p.parse_args(argv)
 
 
@@ -177,14 +179,14 @@ def build_models(context: int, steps_total: int, seed: int):
 def run_native(args) -> dict | None:
     import torch.distributed as dist
 
-    from tests.host import limit_threads
-    limit_threads()
+    from tests.host import limit_threads, usable_cpus
+    world, rank, local = dist_info()
+    limit_threads(max(1, usable_cpus() // world))  # one process per GPU share the host cores
 
     from flux_b200.integration import FINAL_FLUX_OPERATOR_CATEGORIES, enable_flux_ops
     from flux_b200.runtime import NativeSmolLM2Prefill
     from tests.golden.inputs import uniform_prompt
 
-    world, rank, local = dist_info()
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     K, W, ctx = args.steps, args.warmup, args.context
@@ -337,8 +339,11 @@ def run_native(args) -> dict | None:
         line["attention"] = run_attention_sweep(device, peak)
     if world == 1 and not args.no_sweep:
         line["sweep"] = run_context_sweep(model, device, args.seed, peak)
+    if world == 1 and not args.no_generation:
+        line["generation"] = run_generation(model, device, args.seed)
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(cpu_model, config, ctx)
+        line["cpu_baseline"] = cpu_baseline(cpu_model, config, ctx, sweep=not args.no_sweep,
+                                            generation=line.get("generation"), seed=args.seed)
     return line
 
 
@@ -505,14 +510,83 @@ def run_attention_sweep(device, peak: float) -> dict:
             "rows": rows}
 
 
-def cpu_baseline(cpu_model, config, ctx: int, budget_s: float = 15.0) -> dict:
+GENERATION_PROMPT, GENERATION_TOKENS = 128, 128   # configs[0]
+
+
+def run_generation(model, device, seed: int, rounds: int = 5) -> dict:
+    """a seeded 128-token prompt, then 128 greedy tokens, on the
+    GPU.  Two timings, median of ``rounds``: the reference's generation number
+    (native prefill + ``generate_greedy``, runtime set-up excluded,
+    ``benchmarks/benchmark_flux.py:685-702``), and the whole public call
+    ``native_smollm2_greedy_generate`` with the prompt copied from pinned host
+    memory and the tokens read back (set-up included)."""
+    from flux_b200.runtime import NativeSmolLM2Prefill, native_smollm2_greedy_generate
+    from tests.golden.inputs import uniform_prompt
+    prompt_host = uniform_prompt(GENERATION_PROMPT, seed=seed + 1).pin_memory()
+    prompt = prompt_host.to(device)
+    reference_ms, prefill_ms, e2e_ms = [], [], []
+    with torch.inference_mode():
+        for _ in range(rounds):
+            runtime = NativeSmolLM2Prefill.capture(model, prompt, max_decode_steps=GENERATION_TOKENS - 1)
+            torch.cuda.synchronize()
+            s, m, e = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            s.record()
+            runtime.prefill(prompt)
+            m.record()
+            tokens = runtime.generate_greedy(GENERATION_TOKENS)
+            e.record()
+            e.synchronize()
+            prefill_ms.append(s.elapsed_time(m))
+            reference_ms.append(s.elapsed_time(e))
+            del runtime
+            t0 = time.perf_counter()
+            out = native_smollm2_greedy_generate(model, prompt_host.to(device, non_blocking=True),
+                                                 max_new_tokens=GENERATION_TOKENS).cpu()
+            e2e_ms.append((time.perf_counter() - t0) * 1e3)
+    return {"metric": "configs[0] greedy generation ms (128-token prompt, 128 new tokens, incl. native prefill)",
+            "unit": "ms", "value": round(statistics.median(reference_ms), 3),
+            "prefill_ms": round(statistics.median(prefill_ms), 3),
+            "ms_per_token": round(statistics.median(reference_ms) / GENERATION_TOKENS, 4),
+            "e2e_ms": round(statistics.median(e2e_ms), 3),
+            "e2e": "native_smollm2_greedy_generate(prompt from pinned host memory) -> tokens on the host, "
+                   "runtime set-up (weights, graph capture) included",
+            "rounds": rounds, "tokens": [int(t) for t in tokens.reshape(-1).tolist()[:8]],
+            "h2d_bytes": GENERATION_PROMPT * 8, "d2h_bytes": (GENERATION_PROMPT + GENERATION_TOKENS) * 8}
+
+
+CPU_SWEEP_STEPS = 16
+
+
+def cpu_baseline(cpu_model, config, ctx: int, budget_s: float = 15.0, sweep: bool = True,
+                 generation: dict | None = None, seed: int = 0) -> dict:
+    """The reference's FP32 path (transformers eager) on the host cores: decode
+    at the benchmark context (the headline sample), at every sweep context
+    (median of up to 16 steps each) and, with the GPU's configs[0] result
+    beside it, the 128 + 128 greedy generation."""
     from oracle import hf_reference as hf
-    from oracle.host import usable_cpus
+    from oracle.host import cpu_model_name, usable_cpus
+    from tests.golden.inputs import uniform_prompt
     threads = usable_cpus()
     result = hf.time_cpu_decode(cpu_model, config, ctx, steps=64, threads=threads, budget_s=budget_s)
-    return {"value": round(result["ms_per_token"], 3), "unit": "ms/token", "cores": threads, "kind": "reference",
+    line = {"value": round(result["ms_per_token"], 3), "unit": "ms/token", "cores": threads, "kind": "reference",
+            "cpu": cpu_model_name(),
             "sample": (f"transformers LlamaForCausalLM eager FP32 decode (the reference's CPU path), "
                        f"{result['steps']} greedy steps over a {ctx}-row seeded synthetic cache, median")}
+    if sweep:
+        rows = []
+        for context in SWEEP_CONTEXTS:
+            r = hf.time_cpu_decode(cpu_model, config, context, steps=CPU_SWEEP_STEPS, threads=threads, budget_s=4.0)
+            rows.append({"context": context, "ms_per_token": round(r["ms_per_token"], 3), "steps": r["steps"]})
+        line["sweep"] = rows
+    if generation is not None:
+        g = hf.time_cpu_generation(cpu_model, uniform_prompt(GENERATION_PROMPT, seed=seed + 1), GENERATION_TOKENS,
+                                   threads=threads)
+        line["generation"] = {"total_ms": round(g["total_ms"], 1), "prefill_ms": round(g["prefill_ms"], 1),
+                              "decode_ms": round(g["decode_ms"], 1),
+                              "sample": "configs[0]: transformers eager prefill of the same 128-token prompt, "
+                                        "then 127 greedy steps (128 tokens), wall clock",
+                              "tokens_match_gpu": g["tokens"][:8] == generation.get("tokens")}
+    return line
 
 
 def run_reference(args) -> dict | None:

@@ -337,16 +337,12 @@ __global__ void __launch_bounds__(kHeadDim) compact_merge_kernel(const __grid_co
 }  // namespace
 
 fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream, bool dependent) {
-    static bool configured = false;
-    if (!configured) {
-        FX_CUDA_TRY(cudaFuncSetAttribute(compact_chunk_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(chunk_smem<128>())),
-                    "raising attention shared memory");
-        FX_CUDA_TRY(cudaFuncSetAttribute(compact_chunk_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(chunk_smem<64>())),
-                    "raising attention shared memory");
-        configured = true;
-    }
+    fx_status st = raise_smem_limit(reinterpret_cast<const void*>(compact_chunk_kernel<128>), chunk_smem<128>(),
+                                    "raising attention shared memory");
+    if (st == FX_OK)
+        st = raise_smem_limit(reinterpret_cast<const void*>(compact_chunk_kernel<64>), chunk_smem<64>(),
+                              "raising attention shared memory");
+    if (st != FX_OK) return st;
     FX_REQUIRE(a.chunk_rows == 64 || a.chunk_rows == 128, "flux attention: chunks are 64 or 128 rows");
     FX_REQUIRE(a.batch >= 1 && a.batch <= 65535 && a.chunks >= 1 && a.chunks <= kMergeMaxChunks &&
                    a.chunks * a.chunk_rows >= a.cap,

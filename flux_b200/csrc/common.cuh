@@ -51,6 +51,16 @@ fx_status cuda_failure(const char* what, cudaError_t error);
 
 inline cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
 
+// Unique ID (cuCtxGetId) of the calling thread's current CUDA context; 0 when
+// none is current yet.  A context created after cudaDeviceReset gets a new ID.
+fx_status current_context_id(unsigned long long* id);
+
+// Raise `kernel`'s dynamic shared-memory limit to `bytes` in the current
+// context, once per (kernel, context, bytes): the attribute belongs to the
+// context, so a process that drives several GPUs (or re-creates a context)
+// sets it in each.  Thread-safe.
+fx_status raise_smem_limit(const void* kernel, size_t bytes, const char* what);
+
 // Device error word of a decode runtime; the prefill's kernels report into
 // it (bit 8: a tensor-core projection's bounded wait gave up).
 int* decode_error_word(fx_decode* runtime);

@@ -809,10 +809,11 @@ fx_status create_impl(fx_decode* r, const int64_t* token, const float* const* ks
         }
     }
     const size_t attn_smem = static_cast<size_t>(kGroup) * r->chunk_max * sizeof(float);
-    if (attn_smem > 48 * 1024)
-        FX_CUDA_TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(attn_smem)),
-                    "raising attention shared memory");
+    if (attn_smem > 48 * 1024) {
+        const fx_status raised = raise_smem_limit(reinterpret_cast<const void*>(attention_kernel), attn_smem,
+                                                  "raising attention shared memory");
+        if (raised != FX_OK) return raised;
+    }
     fx_status st = allocate(r);
     if (st != FX_OK) return st;
     FX_CUDA_TRY(cudaStreamCreateWithFlags(&r->capture_stream, cudaStreamNonBlocking), "creating capture stream");

@@ -651,44 +651,8 @@ constexpr int64_t kStaticScratchFloats = 262144;
 
 static __device__ __align__(256) float g_gqa_static_scratch[kStaticScratchFloats];
 
-using CtxGetCurrentFn = CUresult (*)(CUcontext*);
-using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
-
 std::mutex g_static_scratch_mutex;
 std::vector<std::pair<unsigned long long, float*>> g_static_scratch_by_context;
-
-// Unique ID of the calling thread's current context (0: none current).
-fx_status current_context_id(unsigned long long* id) {
-    static std::once_flag once;
-    static CtxGetCurrentFn get_current = nullptr;
-    static CtxGetIdFn get_id = nullptr;
-    std::call_once(once, [] {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult found{};
-        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &found) == cudaSuccess &&
-            found == cudaDriverEntryPointSuccess)
-            get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
-        fn = nullptr;
-        if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &found) == cudaSuccess &&
-            found == cudaDriverEntryPointSuccess)
-            get_id = reinterpret_cast<CtxGetIdFn>(fn);
-    });
-    if (get_current == nullptr || get_id == nullptr) {
-        set_error("fx_gqa_decode_attention_static_scratch_f32: cuCtxGetCurrent / cuCtxGetId are unavailable");
-        return FX_ERR_CUDA;
-    }
-    CUcontext context = nullptr;
-    if (get_current(&context) != CUDA_SUCCESS) {
-        set_error("fx_gqa_decode_attention_static_scratch_f32: cuCtxGetCurrent failed");
-        return FX_ERR_CUDA;
-    }
-    *id = 0;
-    if (context != nullptr && get_id(context, id) != CUDA_SUCCESS) {
-        set_error("fx_gqa_decode_attention_static_scratch_f32: cuCtxGetId failed");
-        return FX_ERR_CUDA;
-    }
-    return FX_OK;
-}
 
 // Device address of g_gqa_static_scratch in the calling thread's current
 // context (looked up on the first call in that context).

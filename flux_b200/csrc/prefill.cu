@@ -387,13 +387,10 @@ namespace fx {
 namespace {
 
 fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
-    static bool configured = false;  // the flash tiles need more than the default 48 KB of shared memory
-    if (!configured) {
-        FX_CUDA_TRY(cudaFuncSetAttribute(prefill_flash_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kFlashSmem)),
-                    "raising prefill attention shared memory");
-        configured = true;
-    }
+    // the flash tiles need more than the default 48 KB of shared memory
+    const fx_status raised = raise_smem_limit(reinterpret_cast<const void*>(prefill_flash_kernel), kFlashSmem,
+                                              "raising prefill attention shared memory");
+    if (raised != FX_OK) return raised;
     const fx_model_desc& m = p->model;
     fx_decode_buffers db{};
     fx_status st = fx_decode_get_buffers(p->decode, &db);

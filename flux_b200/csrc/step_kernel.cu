@@ -269,9 +269,9 @@ struct Shared {
     float scratch[32];
     float cv[kConsumerWarps];
     long long ci[kConsumerWarps];
-    float mm[kMaxOBlocks * kStepBlock][kMaxChunks];  // phase M: m, l, o[d] per (dim, chunk)
-    float ml[kMaxOBlocks * kStepBlock][kMaxChunks];
-    float mo[kMaxOBlocks * kStepBlock][kMaxChunks];
+    float mm[kMaxOBlocks][kMaxChunks];               // phase M: m, l per (owned block's head, chunk)
+    float ml[kMaxOBlocks][kMaxChunks];
+    float mo[kMaxOBlocks * kStepBlock][kMaxChunks];  //          o[d] per (owned dim, chunk)
     AttnScratch att;
     volatile int abort;
     int is_last;
@@ -516,15 +516,22 @@ __device__ unsigned long long poll_word(const StepArgs& a, Shared& sh, const uns
     return v;
 }
 
-// Spin (bounded) until the three words at p[0..2] all carry `tag`; each round
-// reloads only the stale ones, so the three wait on one L2 round trip at a
-// time together instead of one after another.
-__device__ void poll_words3(const StepArgs& a, Shared& sh, const unsigned long long* const (&p)[3],
-                            unsigned long long (&v)[3], uint32_t tag) {
-    const unsigned long long t0 = global_timer();
-    while (word_tag(v[0]) != tag || word_tag(v[1]) != tag || word_tag(v[2]) != tag) {
+// Spin (bounded) until the N words at p[0..N-1] all carry `tag`; each round
+// reloads only the stale ones, so they wait on one L2 round trip at a time
+// together instead of one after another.
+template <int N>
+__device__ void poll_words(const StepArgs& a, Shared& sh, const unsigned long long* const (&p)[N],
+                           unsigned long long (&v)[N], uint32_t tag) {
+    auto stale = [&] {
+        bool any = false;
 #pragma unroll
-        for (int j = 0; j < 3; ++j)
+        for (int j = 0; j < N; ++j) any = any || word_tag(v[j]) != tag;
+        return any;
+    };
+    const unsigned long long t0 = global_timer();
+    while (stale()) {
+#pragma unroll
+        for (int j = 0; j < N; ++j)
             if (word_tag(v[j]) != tag) v[j] = ld_word(p[j]);
         if (sh.abort) break;
         const unsigned long long dt = global_timer() - t0;
@@ -1100,30 +1107,43 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     const unsigned long long* part = sh.hp.x_partial +
                                                      parity(l) * (static_cast<size_t>(kQHeads) * nch * kStepPartial) +
                                                      static_cast<size_t>(s.g) * kGroup * nch * kStepPartial;
-                    const int act = s.active;
-                    for (int it = tid; it < nd * act; it += kStepConsumers) {
-                        const int q = it / act, cc = it % act;
-                        const int j = s.ob[q / kStepBlock] * kStepBlock + q % kStepBlock;
-                        const int h = j / kHeadDim, d = j % kHeadDim;
-                        const unsigned long long* p = part + (static_cast<size_t>(h) * nch + cc) * kStepPartial;
-                        const unsigned long long* const src[3] = {p, p + 1, p + 2 + d};
-                        unsigned long long v[3] = {ld_word(src[0]), ld_word(src[1]), ld_word(src[2])};
-                        poll_words3(a, sh, src, v, tag);
-                        sh.mm[q][cc] = word_value(v[0]);
-                        sh.ml[q][cc] = word_value(v[1]);
-                        sh.mo[q][cc] = word_value(v[2]);
+                    // One poll item per thread: the o[d] word of each (owned dim,
+                    // chunk), and the (m, l) pair of each (owned block, chunk) --
+                    // polled once per block, not once per dim.  At most
+                    // 5 * nob * active <= 480 items (nob = 2 needs nch < 48).
+                    const int act = s.active, n_o = nd * act, n_ml = s.nob * act;
+                    for (int it = tid; it < n_o + n_ml; it += kStepConsumers) {
+                        if (it < n_o) {
+                            const int q = it / act, cc = it % act;
+                            const int j = s.ob[q / kStepBlock] * kStepBlock + q % kStepBlock;
+                            const unsigned long long* p =
+                                part + (static_cast<size_t>(j / kHeadDim) * nch + cc) * kStepPartial + 2 + j % kHeadDim;
+                            unsigned long long v = ld_word(p);
+                            if (word_tag(v) != tag) v = poll_word(a, sh, p, v, tag);
+                            sh.mo[q][cc] = word_value(v);
+                        } else {
+                            const int b = (it - n_o) / act, cc = (it - n_o) % act;
+                            const int h = s.ob[b] * kStepBlock / kHeadDim;
+                            const unsigned long long* p = part + (static_cast<size_t>(h) * nch + cc) * kStepPartial;
+                            const unsigned long long* const src[2] = {p, p + 1};
+                            unsigned long long v[2] = {ld_word(src[0]), ld_word(src[1])};
+                            poll_words<2>(a, sh, src, v, tag);
+                            sh.mm[b][cc] = word_value(v[0]);
+                            sh.ml[b][cc] = word_value(v[1]);
+                        }
                     }
                     consumer_sync();
                     if (sh.abort) goto done;
                     LAYER_MARK(6);
                     if (warp < nd) {
+                        const int b = warp / kStepBlock;
                         float mx = -INFINITY;
-                        for (int cc = lane; cc < act; cc += 32) mx = fmaxf(mx, sh.mm[warp][cc]);
+                        for (int cc = lane; cc < act; cc += 32) mx = fmaxf(mx, sh.mm[b][cc]);
                         mx = warp_max(mx);
                         float total = 0.0f, acc = 0.0f;
                         for (int cc = lane; cc < act; cc += 32) {
-                            const float w = expf(sh.mm[warp][cc] - mx);
-                            total = fmaf(w, sh.ml[warp][cc], total);
+                            const float w = expf(sh.mm[b][cc] - mx);
+                            total = fmaf(w, sh.ml[b][cc], total);
                             acc = fmaf(w, sh.mo[warp][cc], acc);
                         }
                         total = warp_sum(total);
@@ -1329,9 +1349,9 @@ fx_status launch_step_kernel(const StepArgs& args, int grid, cudaStream_t stream
 
 fx_status prepare_step_kernel(int device, int* grid) {
     const size_t smem = step_kernel_smem_bytes();
-    FX_CUDA_TRY(cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(smem)),
-                "raising the step kernel's shared memory");
+    const fx_status raised = raise_smem_limit(reinterpret_cast<const void*>(decode_step_kernel), smem,
+                                              "raising the step kernel's shared memory");
+    if (raised != FX_OK) return raised;
     int per_sm = 0;
     FX_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_step_kernel, kStepThreads, smem),
                 "querying step kernel occupancy");

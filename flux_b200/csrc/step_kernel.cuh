@@ -17,7 +17,7 @@ constexpr int kStepPartial = 66;           // m, l, o[64] per (head, chunk)
 constexpr int kStepBlock = 4;              // columns per split-K strip (one 16-byte TMA box row)
 constexpr int kStepStripRows = 192;        // rows per 2-D TMA box of a strip
 constexpr int kStepReplicas = 4;           // copies of the published q | k | v words
-constexpr int kStepAccReplicas = 4;        // copies of each split-K accumulator (spreads the atomics: 2 0.514, 4 0.502, 8 0.511 ms at ctx 8192)
+constexpr int kStepAccReplicas = 4;        // copies of each split-K accumulator (spreads the atomics; 1 / 2 / 4 replicas: 1.02 / 0.445 / 0.428 ms at ctx 8192)
 constexpr int kStepFullGridRows = 6144;   // caches of at least this many rows run on every SM
 constexpr int kStepMinGrid = 128;          // the per-CTA slices must fit one slot (12 SwiGLU features)
 constexpr int kStepMaxGrid = 384;          // every CTA owns at least one block of 4 MLP features

@@ -343,13 +343,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
 }  // namespace
 
 fx_status launch_tc_prefill_attention(const TcAttentionArgs& args, cudaStream_t stream) {
-    static std::once_flag once;
-    static cudaError_t status = cudaSuccess;
-    std::call_once(once, [] {
-        status = cudaFuncSetAttribute(tc_prefill_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(kAttnSmem));
-    });
-    FX_CUDA_TRY(status, "raising the tensor-core attention's shared memory");
+    const fx_status raised = raise_smem_limit(reinterpret_cast<const void*>(tc_prefill_attention_kernel), kAttnSmem,
+                                              "raising the tensor-core attention's shared memory");
+    if (raised != FX_OK) return raised;
     FX_REQUIRE(args.rows > 0 && args.padded >= args.rows && args.padded % kTcAttnKeys == 0,
                "tensor-core attention: bad row counts");
     FX_REQUIRE(args.scale > 0.0f, "tensor-core attention: the attention scale must be positive");

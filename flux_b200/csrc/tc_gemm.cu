@@ -280,14 +280,10 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 
 template <int BM, int STAGES>
 fx_status launch_variant(const TcGemmArgs& args, dim3 grid, cudaStream_t stream, bool dependent) {
-    static std::once_flag once;
-    static cudaError_t status = cudaSuccess;
     constexpr size_t smem = TcLayout<BM, STAGES>::kSmem;
-    std::call_once(once, [] {
-        status = cudaFuncSetAttribute(tc_gemm_kernel<BM, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(smem));
-    });
-    FX_CUDA_TRY(status, "raising the tensor-core GEMM's shared memory");
+    const fx_status raised = raise_smem_limit(reinterpret_cast<const void*>(tc_gemm_kernel<BM, STAGES>), smem,
+                                              "raising the tensor-core GEMM's shared memory");
+    if (raised != FX_OK) return raised;
     if (dependent)
         return launch_dependent(tc_gemm_kernel<BM, STAGES>, grid, dim3(kTcThreads), smem, stream,
                                 "launching the tensor-core GEMM", args);

@@ -115,8 +115,30 @@ def time_cpu_decode(model, config: LlamaConfig, context: int, steps: int, seed: 
     }
 
 
+def time_cpu_generation(model, prompt: torch.Tensor, new_tokens: int, threads: int | None = None) -> dict:
+    """configs[0] on the host cores: HF eager FP32 prefill of ``prompt`` then
+    ``new_tokens - 1`` greedy decode steps (``new_tokens`` generated tokens, the
+    first from the prefill), as ``benchmarks/benchmark_flux.py:633-660`` drives
+    the eager generation; wall-clock prefill and decode times and the tokens."""
+    from oracle.host import limit_threads
+    threads = limit_threads(threads)
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        out = model(input_ids=prompt, use_cache=True, logits_to_keep=1)
+        token = out.logits[:, -1].argmax(dim=-1, keepdim=True)
+        t1 = time.perf_counter()
+        cache, tokens = out.past_key_values, [int(token)]
+        for _ in range(new_tokens - 1):
+            out = model(input_ids=token, past_key_values=cache, use_cache=True, logits_to_keep=1)
+            token = out.logits[:, -1].argmax(dim=-1, keepdim=True)
+            tokens.append(int(token))
+        t2 = time.perf_counter()
+    return {"prefill_ms": (t1 - t0) * 1e3, "decode_ms": (t2 - t1) * 1e3, "total_ms": (t2 - t0) * 1e3,
+            "tokens": tokens, "threads": threads}
+
+
 __all__ = [
     "build_model", "decode_step", "dynamic_cache", "numpy_state", "oracle_weights",
     "reference_runtime_config", "rope_tables", "smollm2_config", "synthetic_cache",
-    "time_cpu_decode",
+    "time_cpu_decode", "time_cpu_generation",
 ]

@@ -40,3 +40,15 @@ def limit_threads(threads: int | None = None) -> int:
     except ImportError:
         pass
     return threads
+
+
+def cpu_model_name() -> str:
+    """The host CPU's model string (``/proc/cpuinfo``), or the platform's."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or platform.machine()
