@@ -6,7 +6,10 @@
   through ``fx_linear_3xtf32_f32`` (the prefill's largest GEMM shape).
 * ``prefill``: one native prefill of a seeded ``--context``-token prompt.
 * ``batched``: two batched decode steps of ``--batch`` sequences with ragged
-  seeded contexts in [512, 4096] (the benchmark's batched configuration).
+  seeded contexts in ``--contexts LOW HIGH`` (default [512, 4096], the
+  benchmark's batched configuration; a multi-pass capture of the projections
+  uses short contexts, since the GEMMs do not depend on them and the caches
+  then stay small).
 
 Each prints ``<name> ok`` and exits 0; nothing is timed here (a number printed
 by a run under a profiler is not a measurement).
@@ -68,8 +71,9 @@ def batched(args, device) -> None:
     from flux_b200 import sharding
     from flux_b200.runtime import NativeSmolLM2BatchedDecode
     model = _model(BATCH_CONTEXT[1], args.seed, device)
-    lengths, tokens = sharding.shard_contexts(args.seed, sharding.sequence_shard(args.batch, 1, 0), *BATCH_CONTEXT)
-    runtime = NativeSmolLM2BatchedDecode(model, args.batch, BATCH_CONTEXT[1] + 8)
+    low, high = args.contexts
+    lengths, tokens = sharding.shard_contexts(args.seed, sharding.sequence_shard(args.batch, 1, 0), low, high)
+    runtime = NativeSmolLM2BatchedDecode(model, args.batch, high + 8)
     dgen = torch.Generator(device=device)
     with torch.inference_mode():
         for i, n in enumerate(lengths):
@@ -91,6 +95,7 @@ def main(argv=None) -> int:
     p.add_argument("--context", type=int, default=8192)
     p.add_argument("--batch", type=int, default=64)
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--contexts", type=int, nargs=2, default=list(BATCH_CONTEXT), metavar=("LOW", "HIGH"))
     args = p.parse_args(argv)
     from tests.host import limit_threads
     limit_threads()
