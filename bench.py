@@ -11,8 +11,10 @@ events on the launching stream between barriers, max over ranks.  Every step
 streams ~0.92 GB (> the 126 MB L2), so no L2 flush is needed.
 
 Under torchrun with N > 1 every rank runs an independent replica (the batch-1
-path does not shard; no collective is on the data path) and the value is the
-max over ranks.
+path does not shard; no collective is on the data path): the job decodes N
+tokens per step, so ``value`` is the max-over-ranks step time divided by N
+(ms per token of the whole job; ``config.per_replica_ms_per_token`` keeps the
+per-GPU figure).
 
 The line also carries ``sweep`` (configs[2]: the batch-1 step after a
 native prefill at each context 128 ... 8192, N = 1), ``batched`` (configs[3]: 64 ragged sequences per GPU,
@@ -293,9 +295,13 @@ def run_native(args) -> dict | None:
     mean_len = first_len + (K - 1) / 2.0
     bytes_per_step = WEIGHT_BYTES + KV_BYTES_PER_ROW * mean_len + KV_BYTES_PER_ROW
     achieved = bytes_per_step / (ms_per_step * 1e-3) / 1e9
+    # Whole-job aggregate: with N replicas (one sequence per GPU, no collective)
+    # the job decodes N tokens per step time, so ms per token of the job is the
+    # max-over-ranks step time over N (at N = 1, the step time itself).
+    aggregate_ms = ms_per_step / world
     line = {
         "metric": METRIC,
-        "value": round(ms_per_step, 5),
+        "value": round(aggregate_ms, 5),
         "unit": "ms/token",
         "n_gpus": world,
         "steps": K,
@@ -311,6 +317,8 @@ def run_native(args) -> dict | None:
             "model": "SmolLM2-135M architecture (30x576, 9/3 heads, vocab 49152, tied)",
             "context_start": ctx + W, "context_end": ctx + W + K,
             "tokens_per_s_per_gpu": round(1e3 / ms_per_step, 1),
+            "tokens_per_s_aggregate": round(world * 1e3 / ms_per_step, 1),
+            "per_replica_ms_per_token": round(ms_per_step, 5),
             "prefill_ms": round(prefill_ms, 2),
             "parallelism": "replicas" if world > 1 else "single",
             "l2": "inputs larger than L2 (~0.92 GB streamed per step)",
@@ -323,8 +331,8 @@ def run_native(args) -> dict | None:
             "kernel": "decode step (one CUDA graph replay)",
             "algorithmic_bytes_per_launch": int(bytes_per_step), "peak_source": peak_src,
         },
-        "e2e": {"value": round(e2e_ms / e2e_steps, 5), "unit": "ms/token", "h2d_bytes_per_step": 8,
-                "d2h_bytes_per_step": 8,
+        "e2e": {"value": round(e2e_ms / e2e_steps / world, 5), "unit": "ms/token", "h2d_bytes_per_step": 8 * world,
+                "d2h_bytes_per_step": 8 * world, "per_replica_ms_per_token": round(e2e_ms / e2e_steps, 5),
                 "api": "NativeSmolLM2Prefill.replay_host(token) -> next token (C-ABI fx_decode_replay_host: host "
                        "token in, one replay, sampled token back in host memory, every step)",
                 "tensor_api_value": round(e2e_tensor_ms / e2e_steps, 5),
