@@ -881,7 +881,136 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             LAYER_MARK(1);
 
             // ------------------------------------------------------ phase B
-            if (s.has_rows) {
+            if (s.has_rows && s.a1 - s.a0 <= 32) {
+                // A chunk of at most 32 rows (one cache tile at most): warp 0 does
+                // it all -- lane r scores row r for the three heads, softmax within
+                // the warp, P.V with each lane on two dims -- and publishes the
+                // partial itself; the other warps wait at the barrier below (they
+                // do not spin on phase M's polls meanwhile: spinning polls load the
+                // L2 that every CTA's exchanges go through).
+                if (warp == 0) {
+                    const unsigned long long* qkv =
+                        sh.hp.x_qkv + (parity(l) * kStepReplicas + cta % kStepReplicas) * kQKV;
+                    // q of the kv head (192 words) and the new row's k, v (64 + 64):
+                    // each lane's up to 10 words are loaded together and only the
+                    // stale ones reloaded, one L2 round trip per round.
+                    constexpr int kQ = kGroup * kHeadDim;
+                    constexpr int kPer = (kQ + 2 * kHeadDim + 31) / 32;  // 10
+                    const int nq = kQ + (s.owns_new ? 2 * kHeadDim : 0);
+                    auto word_src = [&](int i) -> const unsigned long long* {
+                        if (i < kQ) return qkv + s.g * kQ + i;
+                        if (i < kQ + kHeadDim) return qkv + kHidden + s.g * kHeadDim + (i - kQ);
+                        return qkv + kHidden + kKVHeads * kHeadDim + s.g * kHeadDim + (i - kQ - kHeadDim);
+                    };
+                    unsigned long long w[kPer];
+#pragma unroll
+                    for (int j = 0; j < kPer; ++j) {
+                        const int i = lane + 32 * j;
+                        w[j] = i < nq ? ld_word(word_src(i)) : (static_cast<unsigned long long>(tag) << 32);
+                    }
+                    {
+                        const unsigned long long t0 = global_timer();
+                        while (true) {
+                            bool stale = false;
+#pragma unroll
+                            for (int j = 0; j < kPer; ++j) {
+                                if (word_tag(w[j]) != tag) {
+                                    w[j] = ld_word(word_src(lane + 32 * j));
+                                    stale = true;
+                                }
+                            }
+                            if (!stale || sh.abort) break;
+                            const unsigned long long dt = global_timer() - t0;
+                            if (dt > kPeerCheckNs && ld_error(a.error) != 0) {
+                                sh.abort = 1;
+                                break;
+                            }
+                            if (dt > kWaitNs) {
+                                fail(a, sh);
+                                break;
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < kPer; ++j) {
+                        const int i = lane + 32 * j;
+                        if (i < kQ)
+                            sh.qs[i] = word_value(w[j]);
+                        else if (i < kQ + kHeadDim)
+                            sh.knew[i - kQ] = word_value(w[j]);
+                        else if (i < nq)
+                            sh.vnew[i - kQ - kHeadDim] = word_value(w[j]);
+                    }
+                    __syncwarp();
+                    LAYER_MARK(2);
+                    if (s.n_att > 0) wait_bar(a, sh, &sh.full[k % kStepSlots], static_cast<uint32_t>(k / kStepSlots) & 1u);
+                    LAYER_MARK(3);
+                    const int cached = static_cast<int>(s.cached_end - s.a0);  // rows in the tile (K, then V)
+                    const int rows = static_cast<int>(s.a1 - s.a0);
+                    const float* tile = slot_ptr(ring, k);
+                    const float scale2 = sh.hp.scale[l] * kLog2e;
+                    const bool valid = lane < rows;
+                    const float4* k4 = reinterpret_cast<const float4*>(lane < cached ? tile + lane * kHeadDim : sh.knew);
+                    float d[kGroup] = {0.0f, 0.0f, 0.0f};
+#pragma unroll 4
+                    for (int j = 0; j < kHeadDim / 4; ++j) {
+                        const int c = (j + lane) & (kHeadDim / 4 - 1);  // rotated: lanes spread over the banks
+                        const float4 kv = k4[c];
+#pragma unroll
+                        for (int h = 0; h < kGroup; ++h) {
+                            const float4 q = reinterpret_cast<const float4*>(sh.qs + h * kHeadDim)[c];
+                            d[h] = fmaf(q.x, kv.x, d[h]);
+                            d[h] = fmaf(q.y, kv.y, d[h]);
+                            d[h] = fmaf(q.z, kv.z, d[h]);
+                            d[h] = fmaf(q.w, kv.w, d[h]);
+                        }
+                    }
+                    float m[kGroup], total[kGroup];
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) {
+                        const float sc = valid ? d[h] * scale2 : -INFINITY;
+                        m[h] = warp_max(sc);  // row 0 is valid: finite
+                        const float p = valid ? exp2f(sc - m[h]) : 0.0f;
+                        total[h] = warp_sum(p);
+                        if (valid) sh.att.p[h][lane] = p;
+                    }
+                    __syncwarp();
+                    float2 o[kGroup];
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) o[h] = make_float2(0.0f, 0.0f);
+                    for (int r = 0; r < rows; ++r) {
+                        const float2 v = reinterpret_cast<const float2*>(
+                            r < cached ? tile + (cached + r) * kHeadDim : sh.vnew)[lane];
+#pragma unroll
+                        for (int h = 0; h < kGroup; ++h) {
+                            const float p = sh.att.p[h][r];
+                            o[h].x = fmaf(p, v.x, o[h].x);
+                            o[h].y = fmaf(p, v.y, o[h].y);
+                        }
+                    }
+                    __syncwarp();  // the warp is done with the tile
+                    if (lane == 0 && s.n_att > 0) {
+                        mbar_arrive(&sh.empty[k % kStepSlots]);
+                        sh.consumed = k + 1;
+                    }
+                    LAYER_MARK(4);
+                    const int nch = sh.hp.nch;
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) {
+                        unsigned long long* pw = sh.hp.x_partial +
+                                                 parity(l) * (static_cast<size_t>(kQHeads) * nch * kStepPartial) +
+                                                 ((static_cast<size_t>(s.g) * kGroup + h) * nch + s.c) * kStepPartial;
+                        st_word(pw + 2 + 2 * lane, tag, o[h].x);
+                        st_word(pw + 3 + 2 * lane, tag, o[h].y);
+                        if (lane == 0) {
+                            st_word(pw, tag, m[h] * kLn2);  // natural-log units
+                            st_word(pw + 1, tag, total[h]);
+                        }
+                    }
+                }
+                k += s.n_att;
+                consumer_sync();
+            } else if (s.has_rows) {
                 const unsigned long long* qkv = sh.hp.x_qkv + (parity(l) * kStepReplicas + cta % kStepReplicas) * kQKV;
                 if (!poll_attention_inputs(a, sh, qkv, s.g, s.owns_new, tag)) goto done;
                 LAYER_MARK(2);
