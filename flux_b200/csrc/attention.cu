@@ -336,7 +336,7 @@ __global__ void __launch_bounds__(kHeadDim) compact_merge_kernel(const __grid_co
 
 }  // namespace
 
-fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream, bool dependent) {
+fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream, bool dependent, bool merge) {
     fx_status st = raise_smem_limit(reinterpret_cast<const void*>(compact_chunk_kernel<128>), chunk_smem<128>(),
                                     "raising attention shared memory");
     if (st == FX_OK)
@@ -355,7 +355,7 @@ fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t strea
                                               "launching compact attention chunks", a)
                            : launch_dependent(compact_chunk_kernel<64>, grid, dim3(kThreads), chunk_smem<64>(), stream,
                                               "launching compact attention chunks", a);
-        if (st != FX_OK || a.counters != nullptr) return st;
+        if (st != FX_OK || a.counters != nullptr || !merge) return st;
         return launch_dependent(compact_merge_kernel, merge_grid, dim3(kHeadDim), 0, stream,
                                 "launching compact attention merge", a);
     }
@@ -364,7 +364,7 @@ fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t strea
     else
         compact_chunk_kernel<64><<<grid, kThreads, chunk_smem<64>(), stream>>>(a);
     FX_CUDA_TRY(cudaGetLastError(), "launching compact attention chunks");
-    if (a.counters != nullptr) return FX_OK;
+    if (a.counters != nullptr || !merge) return FX_OK;
     compact_merge_kernel<<<merge_grid, kHeadDim, 0, stream>>>(a);
     FX_CUDA_TRY(cudaGetLastError(), "launching compact attention merge");
     return FX_OK;

@@ -31,9 +31,10 @@ inline int64_t compact_attention_workspace(int64_t batch, int64_t cap, int rows 
     return batch * kQHeads * ((cap + rows - 1) / rows) * (kHeadDim + 2);
 }
 
-// Enqueue the chunk kernel (and the merge kernel unless `counters` is set)
-// on `stream` (`dependent`: as programmatic dependent launches of the
-// preceding kernel).
-fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream, bool dependent = false);
+// Enqueue the chunk kernel (and the merge kernel unless `counters` is set or
+// `merge` is false: the caller merges the workspace itself) on `stream`
+// (`dependent`: as programmatic dependent launches of the preceding kernel).
+fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream, bool dependent = false,
+                                   bool merge = true);
 
 }  // namespace fx

@@ -22,6 +22,7 @@
 // kernel -- deterministic, FP32, and a row's result does not depend on the
 // other rows of the batch.
 #include "attention.cuh"
+#include "batch_layer.cuh"
 #include "common.cuh"
 #include "tc_gemm.cuh"
 
@@ -353,6 +354,7 @@ struct BatchLane {
     float *norm = nullptr, *attn = nullptr, *act = nullptr;  // 64 rows each (rows >= `rows` stay zero)
     float *partials = nullptr, *attn_ws = nullptr;
     CUtensorMap x_norm, x_attn, x_act;
+    BatchLayerMaps layer_maps;  // the layer kernel's staging maps (layer-kernel step)
 };
 
 struct fx_batch {
@@ -377,6 +379,14 @@ struct fx_batch {
     GemmPlan qkv_plan, o_plan, gu_plan, down_plan, lm_plan;
     // Projections on tcgen05 tensor cores (3xTF32) unless FLUX_B200_BATCH_GEMM=simt.
     bool tensor_cores = true;
+    // FLUX_B200_BATCH_STEP=layers: the work between attention launches as one
+    // cooperative launch per layer (batch_layer.cu, SIMT FP32), 2 launches per
+    // layer; by default the launch chain below (tcgen05 projections, two
+    // lanes), which measured slightly faster (2.92-2.94 vs 2.95-2.98 ms per
+    // 64-sequence step on one B200).
+    bool layer_kernel = false;
+    int layer_grid = 0;
+    unsigned* barriers = nullptr;  // [kLayers + 1][4] grid-barrier counters, cleared at each step
     fx::TcModelWeights tc;
     CUtensorMap x_norm_all;
     size_t layer_stride() const { return static_cast<size_t>(batch) * kKVHeads * capacity * kHeadDim; }
@@ -488,11 +498,84 @@ fx_status run_lane(fx_batch* r, BatchLane& ln, cudaStream_t s) {
     return FX_OK;
 }
 
+// The lane's 30 layers as (layer kernel, attention chunks, merge) x 30 +
+// one layer kernel: the first launch embeds and projects layer 0's QKV,
+// launch l + 1 takes layer l's attention output through o_proj .. down and
+// layer l + 1's QKV (the last one: the final norm rows).
+fx_status run_lane_layers(fx_batch* r, BatchLane& ln, cudaStream_t s) {
+    const fx_model_desc& m = r->model;
+    FX_CUDA_TRY(cudaMemsetAsync(r->barriers, 0, static_cast<size_t>(kLayers + 1) * 4 * sizeof(unsigned), s),
+                "clearing the layer kernels' barriers");
+    BatchLayerArgs a{};
+    a.maps = ln.layer_maps;
+    a.embedding = m.embedding;
+    a.tokens = r->tokens + ln.row0;
+    a.vocab = r->vocab;
+    a.attn = ln.attn;
+    a.h = ln.h;
+    a.h2 = ln.h2;
+    a.act = ln.act;
+    a.q = ln.q;
+    a.positions = r->positions + ln.row0;
+    a.lengths = r->lengths + ln.row0;
+    a.cap = r->capacity;
+    a.rope_cos = m.rope_cos;
+    a.rope_sin = m.rope_sin;
+    a.norm_out = r->norm_all + static_cast<size_t>(ln.row0) * kHidden;
+    a.error = r->error;
+    a.eps = m.epsilon;
+    a.rows = ln.rows;
+    auto cache_of = [&](float* base, int l) { return base + l * r->layer_stride() + ln.row0 * r->sequence_stride(); };
+    a.mode = kLayerFirst;
+    a.next_norm = m.input_norm[0];
+    a.next_qkv = m.packed_qkv[0];
+    a.key_cache = cache_of(r->key_cache, 0);
+    a.value_cache = cache_of(r->value_cache, 0);
+    a.barrier = r->barriers;
+    fx_status st = launch_batch_layer(a, r->layer_grid, s);
+    if (st != FX_OK) return st;
+    for (int l = 0; l < kLayers; ++l) {
+        CompactAttention at{};
+        at.q = ln.q;
+        at.k = cache_of(r->key_cache, l);
+        at.v = cache_of(r->value_cache, l);
+        at.lengths = a.lengths;
+        at.length_stride = 1;
+        at.out = ln.attn;
+        at.ws = ln.attn_ws;
+        at.error = r->error;
+        at.scale = m.attention_scale[l];
+        at.batch = ln.rows;
+        at.cap = r->capacity;
+        at.chunks = (r->capacity + kCompactChunk - 1) / kCompactChunk;
+        at.chunk_rows = kCompactChunk;
+        if ((st = launch_compact_attention(at, s, true, false)) != FX_OK) return st;  // the layer kernel merges
+        const bool last = l + 1 == kLayers;
+        a.attn_ws = ln.attn_ws;
+        a.attn_chunks = at.chunks;
+        a.attn_rows = at.chunk_rows;
+        a.mode = last ? kLayerLast : kLayerMiddle;
+        a.o_proj = m.o_proj[l];
+        a.post_norm = m.post_norm[l];
+        a.gate_up = m.gate_up[l];
+        a.down = m.down[l];
+        a.next_norm = last ? m.final_norm : m.input_norm[l + 1];
+        a.next_qkv = last ? nullptr : m.packed_qkv[l + 1];
+        a.key_cache = last ? nullptr : cache_of(r->key_cache, l + 1);
+        a.value_cache = last ? nullptr : cache_of(r->value_cache, l + 1);
+        a.barrier = r->barriers + 4 * (l + 1);
+        if ((st = launch_batch_layer(a, r->layer_grid, s)) != FX_OK) return st;
+    }
+    return FX_OK;
+}
+
 fx_status run_step(fx_batch* r, cudaStream_t s) {
     const fx_model_desc& m = r->model;
     const int B = static_cast<int>(r->batch);
     fx_status st;
-    if (r->lanes > 1) {
+    if (r->layer_kernel) {
+        if ((st = run_lane_layers(r, r->lane[0], s)) != FX_OK) return st;
+    } else if (r->lanes > 1) {
         // the latency-bound projections and reductions run at high priority,
         // the attention chunks at low (node priorities of the graph)
         LaunchPriorityScope high(r->priority_high);
@@ -541,7 +624,7 @@ void destroy_batch(fx_batch* r) {
     if (r->lane_stream) cudaStreamDestroy(r->lane_stream);
     for (void* p : {static_cast<void*>(r->tokens), static_cast<void*>(r->logits), static_cast<void*>(r->key_cache),
                     static_cast<void*>(r->value_cache), static_cast<void*>(r->activations),
-                    static_cast<void*>(r->partials), static_cast<void*>(r->attn_ws)})
+                    static_cast<void*>(r->partials), static_cast<void*>(r->attn_ws), static_cast<void*>(r->barriers)})
         cudaFree(p);
     tc_weights_release(&r->tc);
     delete r;
@@ -568,8 +651,16 @@ fx_status create_batch(fx_batch* r, cudaStream_t stream) {
     // Lanes (FLUX_B200_BATCH_LANES=1 runs the whole batch as one chain).  The
     // split-K plans depend only on the configured lane count, never on the
     // batch size, so a sequence's result is the same in any batch.
+    const char* step_env = std::getenv("FLUX_B200_BATCH_STEP");
+    r->layer_kernel = step_env != nullptr && std::strcmp(step_env, "layers") == 0;
+    if (r->layer_kernel) {
+        fx_status prep = prepare_batch_layer(&r->layer_grid);
+        if (prep != FX_OK) return prep;
+        FX_CUDA_TRY(cudaMalloc(&r->barriers, static_cast<size_t>(kLayers + 1) * 4 * sizeof(unsigned)),
+                    "allocating the layer kernels' barriers");
+    }
     const char* lanes_env = std::getenv("FLUX_B200_BATCH_LANES");
-    const int lanes_cfg = lanes_env != nullptr && std::strcmp(lanes_env, "1") == 0 ? 1 : 2;
+    const int lanes_cfg = r->layer_kernel || (lanes_env != nullptr && std::strcmp(lanes_env, "1") == 0) ? 1 : 2;
     r->lanes = static_cast<int>(std::min<int64_t>(lanes_cfg, B));
     r->lane[0].row0 = 0;
     r->lane[0].rows = static_cast<int>((B + r->lanes - 1) / r->lanes);
@@ -638,8 +729,17 @@ fx_status create_batch(fx_batch* r, cudaStream_t stream) {
         ln.attn_ws = ws;
         ws += lane_ws(n);
     }
+    if (r->layer_kernel) {
+        BatchLane& ln = r->lane[0];
+        fx_status st0;
+        if ((st0 = tc_encode_map(&ln.layer_maps.attn, ln.attn, 64, kHidden, 64, "the batched attention rows")) != FX_OK ||
+            (st0 = tc_encode_map(&ln.layer_maps.h2, ln.h2, ln.rows, kHidden, 64, "the batched residual rows")) != FX_OK ||
+            (st0 = tc_encode_map(&ln.layer_maps.act, ln.act, 64, kInter, 64, "the batched SwiGLU rows")) != FX_OK ||
+            (st0 = tc_encode_map(&ln.layer_maps.h, ln.h, ln.rows, kHidden, 64, "the batched residual rows")) != FX_OK)
+            return st0;
+    }
     if (tc) {
-        fx_status st0 = tc_weights_create(r->model, true, &r->tc, stream);
+        fx_status st0 = tc_weights_create(r->model, true, &r->tc, stream, !r->layer_kernel);
         if (st0 != FX_OK) return st0;
         if ((st0 = tc_encode_map(&r->x_norm_all, r->norm_all, R, kHidden, 64, "the batched final-norm rows")) != FX_OK)
             return st0;
@@ -714,6 +814,13 @@ extern "C" fx_status fx_batch_create(const fx_model_desc* model, int64_t batch, 
     }
     FX_REQUIRE(reinterpret_cast<uintptr_t>(model->lm_head) % 16 == 0,
                "flux batched decode: LM head must be 16-byte aligned");
+    FX_REQUIRE(reinterpret_cast<uintptr_t>(model->embedding) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(model->final_norm) % 16 == 0,
+               "flux batched decode: embedding and norm weights must be 16-byte aligned");
+    for (int l = 0; l < kLayers; ++l)
+        FX_REQUIRE(reinterpret_cast<uintptr_t>(model->input_norm[l]) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(model->post_norm[l]) % 16 == 0,
+                   "flux batched decode: embedding and norm weights must be 16-byte aligned");
     DeviceScope scope(model->device);
     fx_batch* r = new fx_batch();
     r->model = *model;
@@ -809,6 +916,10 @@ extern "C" fx_status fx_batch_check(fx_batch* r) {
         set_error("flux batched decode: a bounded wait in a tensor-core projection gave up");
         return FX_ERR_DEVICE;
     }
+    if (error & 16u) {
+        set_error("flux batched decode: a bounded wait in the layer kernel gave up");
+        return FX_ERR_DEVICE;
+    }
     return FX_OK;
 }
 
@@ -824,7 +935,8 @@ extern "C" fx_status fx_batch_get_buffers(const fx_batch* r, fx_batch_buffers* o
     out->batch = r->batch;
     out->capacity = r->capacity;
     out->generated_capacity = r->gen_cap;
-    out->kernels_per_step = r->lanes * (1 + kLayers * 10) + 3 + (r->lm_plan.splits > 1 ? 1 : 0);
+    out->kernels_per_step = (r->layer_kernel ? 1 + kLayers * 2 : r->lanes * (1 + kLayers * 10)) + 3 +
+                            (r->lm_plan.splits > 1 ? 1 : 0);
     return FX_OK;
 }
 

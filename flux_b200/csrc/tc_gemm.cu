@@ -357,8 +357,10 @@ fx_status launch_tc_gemm(const TcGemmArgs& args, int bm, int splits, cudaStream_
     return FX_ERR_INVALID;
 }
 
-fx_status tc_weights_create(const fx_model_desc& model, bool lm_head, TcModelWeights* out, cudaStream_t stream) {
-    const size_t per_layer = static_cast<size_t>(kQKV + kHidden + kGateUp) * kHidden + static_cast<size_t>(kHidden) * kInter;
+fx_status tc_weights_create(const fx_model_desc& model, bool lm_head, TcModelWeights* out, cudaStream_t stream,
+                            bool layers) {
+    const size_t per_layer =
+        layers ? static_cast<size_t>(kQKV + kHidden + kGateUp) * kHidden + static_cast<size_t>(kHidden) * kInter : 0;
     const size_t lm = lm_head ? static_cast<size_t>(model.vocab) * kHidden : 0;
     const size_t total = 2 * (per_layer * kLayers + lm);
     FX_CUDA_TRY(cudaMalloc(&out->buffer, total * sizeof(float)), "allocating the split projection weights");
@@ -376,7 +378,7 @@ fx_status tc_weights_create(const fx_model_desc& model, bool lm_head, TcModelWei
         return tc_encode_map(&w.lo, lo, rows, cols, kTcTileN, what);
     };
     fx_status st;
-    for (int l = 0; l < kLayers; ++l) {
+    for (int l = 0; l < (layers ? kLayers : 0); ++l) {
         if ((st = make(out->qkv[l], model.packed_qkv[l], kQKV, kHidden, "packed_qkv")) != FX_OK) return st;
         if ((st = make(out->o[l], model.o_proj[l], kHidden, kHidden, "o_proj")) != FX_OK) return st;
         if ((st = make(out->gate_up[l], model.gate_up[l], kGateUp, kHidden, "gate_up")) != FX_OK) return st;

@@ -62,7 +62,10 @@ struct TcModelWeights {
     bool has_lm_head = false;
 };
 
-fx_status tc_weights_create(const fx_model_desc& model, bool lm_head, TcModelWeights* out, cudaStream_t stream);
+// `layers` false: the LM head only (the persistent batched layers multiply
+// FP32 weights on the SIMT cores).
+fx_status tc_weights_create(const fx_model_desc& model, bool lm_head, TcModelWeights* out, cudaStream_t stream,
+                            bool layers = true);
 void tc_weights_release(TcModelWeights* w);
 
 // Arguments of C = X . W^T (+ residual) with K split in `k_per_split` slices.

@@ -34,8 +34,12 @@ def _load(runtime, index, length, seed, token):
     return keys, values
 
 
-def test_batched_greedy_steps_match_oracle(model_gpu, smollm2_model):
+@pytest.mark.parametrize("step", ["kernels", "layers"])
+def test_batched_greedy_steps_match_oracle(model_gpu, smollm2_model, monkeypatch, step):
+    """Both batched steps: the launch chain (default) and the cooperative
+    layer kernel (FLUX_B200_BATCH_STEP=layers)."""
     from flux_b200.runtime import NativeSmolLM2BatchedDecode
+    monkeypatch.setenv("FLUX_B200_BATCH_STEP", step)
     lengths = [0, 5, 130, 300]
     capacity = 304
     runtime = NativeSmolLM2BatchedDecode(model_gpu, len(lengths), capacity)
@@ -84,10 +88,12 @@ def test_batched_matches_batch_one_runtime(model_gpu):
                                single.key_cache[:, 0, :, length:length + 4].cpu().numpy(), rtol=1e-4, atol=1e-5)
 
 
-def test_batch_of_64_equals_each_sequence_alone(model_gpu):
+@pytest.mark.parametrize("step", ["kernels", "layers"])
+def test_batch_of_64_equals_each_sequence_alone(model_gpu, monkeypatch, step):
     """Rows never interact: a sequence's logits in a batch of 64 ragged
     contexts are bitwise those of the same sequence run alone."""
     from flux_b200.runtime import NativeSmolLM2BatchedDecode
+    monkeypatch.setenv("FLUX_B200_BATCH_STEP", step)
     rng = np.random.default_rng(11)
     lengths = [int(x) for x in rng.integers(1, 600, size=64)]
     capacity = 608
@@ -124,6 +130,7 @@ def test_two_lanes_match_one_lane(model_gpu, monkeypatch):
     differ, so the logits agree to rounding; each run's tokens are the argmax
     of its own logits."""
     from flux_b200.runtime import NativeSmolLM2BatchedDecode
+    monkeypatch.setenv("FLUX_B200_BATCH_STEP", "kernels")  # lanes belong to the launch-chain step
     rng = np.random.default_rng(5)
     lengths = [int(x) for x in rng.integers(1, 500, size=7)]
     capacity = 512
@@ -146,3 +153,34 @@ def test_two_lanes_match_one_lane(model_gpu, monkeypatch):
         for step, row in enumerate(logits):
             assert torch.equal(gen[:, step], row.argmax(dim=-1).to(gen.dtype))
     assert k_two == k_one + 1 + 30 * 10
+
+
+def test_layer_kernel_matches_launch_chain(model_gpu, monkeypatch):
+    """The cooperative layer-kernel step (FLUX_B200_BATCH_STEP=layers: the
+    attention merge, projections, norms, SwiGLU and RoPE between attention
+    launches in one launch, SIMT FP32) against the default launch chain
+    (tensor-core 3xTF32 split-K projections and separate reduction kernels):
+    the same math in other summation orders, so the logits agree to rounding;
+    2 launches per layer instead of 10."""
+    from flux_b200.runtime import NativeSmolLM2BatchedDecode
+    rng = np.random.default_rng(8)
+    lengths = [int(x) for x in rng.integers(1, 700, size=9)]
+    capacity = 712
+    config = hf.smollm2_config()
+    caches = [hf.synthetic_cache(config, n, seed=3000 + i, std=0.5) for i, n in enumerate(lengths)]
+    runs = {}
+    for mode in ("kernels", "layers"):
+        monkeypatch.setenv("FLUX_B200_BATCH_STEP", mode)
+        monkeypatch.setenv("FLUX_B200_BATCH_LANES", "1")
+        runtime = NativeSmolLM2BatchedDecode(model_gpu, len(lengths), capacity)
+        for i, n in enumerate(lengths):
+            keys, values = caches[i]
+            runtime.load(i, (211 * i + 5) % 49152, [k.cuda() for k in keys], [v.cuda() for v in values], n)
+        logits = [runtime.step(1).clone() for _ in range(3)]
+        runtime.check()
+        runs[mode] = (logits, runtime.key_cache().clone(), runtime.kernels_per_step)
+    (chain, chain_k, k_chain), (layers, layers_k, k_layers) = runs["kernels"], runs["layers"]
+    for a, b in zip(chain, layers):
+        torch.testing.assert_close(b, a, rtol=2e-5, atol=2e-5)
+    torch.testing.assert_close(layers_k, chain_k, rtol=1e-5, atol=1e-5)
+    assert k_chain == k_layers + 30 * 8
