@@ -6,6 +6,10 @@ Code written against the reference package imports from ``flux.ops``,
 alias of the flux_b200 module that implements it (``_ALIASES``), so an
 unmodified caller runs on the B200 library.
 
+``torch.classes.flux.NativeSmolLM2Decode`` and ``NativeSmolLM2Prefill`` are
+registered (``libfluxb200_torch.so``) with the reference's constructor
+argument lists and methods, for code that builds the runtime objects directly.
+
 Differences a caller can see:
 * the plain operator functions the reference ships as PyTorch formulas
   (``flux.ops.rms_norm``, ``residual_rmsnorm``, ``rope``, ``softmax``,
@@ -22,9 +26,15 @@ from __future__ import annotations
 import sys
 import types
 
+from flux_b200 import _native
 from flux_b200 import integration as _integration
 from flux_b200 import operators as _operators
 from flux_b200 import runtime as _runtime
+
+# torch.classes.flux.NativeSmolLM2Decode / NativeSmolLM2Prefill, the custom
+# classes the reference's runtime module constructs (registered when the
+# library is built; the probes in flux.runtime load it as well).
+_native.load_torch_classes()
 
 # The reference's plain (PyTorch-formula) operators, same signatures, on the
 # native kernels (flux/ops/{rmsnorm,residual_rmsnorm,rope,softmax,

@@ -206,6 +206,29 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     return lib
 
 
+TORCH_CLASSES_PATH = LIBRARY_PATH.with_name("libfluxb200_torch.so")
+_TORCH_CLASSES: bool | None = None
+
+
+def load_torch_classes() -> bool:
+    """Register ``torch.classes.flux.NativeSmolLM2Decode`` / ``NativeSmolLM2Prefill``
+    (``libfluxb200_torch.so``, the reference's custom-class surface over this
+    library); False when that library is not built or does not load.  The C
+    library loads first so both share one copy of it."""
+    global _TORCH_CLASSES
+    if _TORCH_CLASSES is None:
+        _TORCH_CLASSES = False
+        if TORCH_CLASSES_PATH.exists():
+            try:
+                load()
+                import torch
+                torch.classes.load_library(str(TORCH_CLASSES_PATH))
+                _TORCH_CLASSES = True
+            except (OSError, RuntimeError, NativeLibraryUnavailable):
+                _TORCH_CLASSES = False
+    return _TORCH_CLASSES
+
+
 def is_available() -> bool:
     try:
         load()

@@ -68,11 +68,17 @@ class NativePrefillRuntimeMemory:
 
 
 def native_smollm2_runtime_is_available() -> bool:
-    return _native.is_available()
+    available = _native.is_available()
+    if available:
+        _native.load_torch_classes()  # torch.classes.flux.* for callers that build the objects directly
+    return available
 
 
 def native_smollm2_prefill_is_available() -> bool:
-    return _native.is_available()
+    available = _native.is_available()
+    if available:
+        _native.load_torch_classes()
+    return available
 
 
 # ------------------------------------------------------- device buffer views
