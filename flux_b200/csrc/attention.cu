@@ -85,7 +85,10 @@ __device__ __forceinline__ int64_t sequence_length(const CompactAttention& a, in
 }
 
 template <int kRows>
-__global__ void __launch_bounds__(kThreads) compact_chunk_kernel(const __grid_constant__ CompactAttention a) {
+// Three CTAs per SM (shared memory allows three 128-row CTAs); the bound
+// also steers register allocation: 2.885 vs 2.919 ms per batched step
+// against the unbounded build on one B200.
+__global__ void __launch_bounds__(kThreads, 3) compact_chunk_kernel(const __grid_constant__ CompactAttention a) {
     grid_dependency_wait();
 
     extern __shared__ __align__(128) unsigned char smem[];
@@ -336,35 +339,36 @@ __global__ void __launch_bounds__(kHeadDim) compact_merge_kernel(const __grid_co
 
 }  // namespace
 
-fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream, bool dependent, bool merge) {
-    fx_status st = raise_smem_limit(reinterpret_cast<const void*>(compact_chunk_kernel<128>), chunk_smem<128>(),
-                                    "raising attention shared memory");
-    if (st == FX_OK)
-        st = raise_smem_limit(reinterpret_cast<const void*>(compact_chunk_kernel<64>), chunk_smem<64>(),
-                              "raising attention shared memory");
+namespace {
+
+template <int kRows>
+fx_status launch_chunks(const CompactAttention& a, dim3 grid, cudaStream_t stream, bool dependent) {
+    const fx_status st = raise_smem_limit(reinterpret_cast<const void*>(compact_chunk_kernel<kRows>), chunk_smem<kRows>(),
+                                          "raising attention shared memory");
     if (st != FX_OK) return st;
+    if (dependent)
+        return launch_dependent(compact_chunk_kernel<kRows>, grid, dim3(kThreads), chunk_smem<kRows>(), stream,
+                                "launching compact attention chunks", a);
+    compact_chunk_kernel<kRows><<<grid, kThreads, chunk_smem<kRows>(), stream>>>(a);
+    FX_CUDA_TRY(cudaGetLastError(), "launching compact attention chunks");
+    return FX_OK;
+}
+
+}  // namespace
+
+fx_status launch_compact_attention(const CompactAttention& a, cudaStream_t stream, bool dependent, bool merge) {
     FX_REQUIRE(a.chunk_rows == 64 || a.chunk_rows == 128, "flux attention: chunks are 64 or 128 rows");
     FX_REQUIRE(a.batch >= 1 && a.batch <= 65535 && a.chunks >= 1 && a.chunks <= kMergeMaxChunks &&
                    a.chunks * a.chunk_rows >= a.cap,
                "flux attention: batch or capacity out of range");
     const dim3 grid(static_cast<unsigned>(a.chunks), kKVHeads, static_cast<unsigned>(a.batch));
     const dim3 merge_grid(static_cast<unsigned>(a.batch * kQHeads));
-    if (dependent) {
-        fx_status st = a.chunk_rows == 128
-                           ? launch_dependent(compact_chunk_kernel<128>, grid, dim3(kThreads), chunk_smem<128>(), stream,
-                                              "launching compact attention chunks", a)
-                           : launch_dependent(compact_chunk_kernel<64>, grid, dim3(kThreads), chunk_smem<64>(), stream,
-                                              "launching compact attention chunks", a);
-        if (st != FX_OK || a.counters != nullptr || !merge) return st;
+    const fx_status st = a.chunk_rows == 128 ? launch_chunks<128>(a, grid, stream, dependent)
+                                             : launch_chunks<64>(a, grid, stream, dependent);
+    if (st != FX_OK || a.counters != nullptr || !merge) return st;
+    if (dependent)
         return launch_dependent(compact_merge_kernel, merge_grid, dim3(kHeadDim), 0, stream,
                                 "launching compact attention merge", a);
-    }
-    if (a.chunk_rows == 128)
-        compact_chunk_kernel<128><<<grid, kThreads, chunk_smem<128>(), stream>>>(a);
-    else
-        compact_chunk_kernel<64><<<grid, kThreads, chunk_smem<64>(), stream>>>(a);
-    FX_CUDA_TRY(cudaGetLastError(), "launching compact attention chunks");
-    if (a.counters != nullptr || !merge) return FX_OK;
     compact_merge_kernel<<<merge_grid, kHeadDim, 0, stream>>>(a);
     FX_CUDA_TRY(cudaGetLastError(), "launching compact attention merge");
     return FX_OK;
