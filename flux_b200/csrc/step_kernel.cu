@@ -1,12 +1,14 @@
 // The whole batch-1 decode step as ONE persistent cooperative launch.
 //
 // One CTA per SM, 512 threads: 15 consumer warps do the math, one producer
-// warp streams weights and cache rows into a ring of 7 x 27 KB shared-memory
-// slots with TMA (1-D cp.async.bulk for rows, 2-D cp.async.bulk.tensor for
-// column strips; never multicast) completing on full/empty mbarrier pairs.
-// The producer walks the CTA's tiles in consumption order and runs up to 7
-// tiles ahead, so HBM keeps streaming while the consumers wait for values
-// from other CTAs.
+// warp streams weights and cache rows into a 189 KB shared-memory ring with
+// TMA (1-D cp.async.bulk for rows, 2-D cp.async.bulk.tensor for column
+// strips; never multicast) completing on full/empty mbarrier pairs.  Each
+// tile takes its own size (128-byte aligned, <= 27 KB) of the ring, not a
+// fixed slot, so short tiles (a chunk's last few cache rows) do not hold a
+// whole slot: the producer walks the CTA's tiles in consumption order and
+// runs as far ahead as the bytes allow, so HBM keeps streaming while the
+// consumers wait for values from other CTAs.
 //
 // Each CTA owns a fixed slice of every projection and one (kv head, chunk)
 // of the attention.  Per layer four dependent steps (no grid barrier):
@@ -44,6 +46,15 @@ namespace {
 constexpr unsigned long long kWaitNs = 2000000000ull;    // 2 s per wait
 constexpr unsigned long long kPeerCheckNs = 1000000ull;  // look at the error word after 1 ms
 constexpr int kConsumerWarps = kStepConsumers / 32;      // 15
+constexpr int64_t kRingBytes = static_cast<int64_t>(kStepSlots) * kStepSlotBytes;  // 193,536
+constexpr int kTileBars = 12;  // full / empty barrier pairs, tile k on pair k % 12 (more than the tiles in flight)
+// Tiles in flight at most: as many as the bytes allow (<= 12) when the CTA's
+// attention chunk spans two or more cache tiles, else 7 (the streaming then
+// stays out of the way of the exchanges).  Measured on B200 (ms/token, fixed
+// 7 x 27 KB slots -> this ring): 0.425 -> 0.403 at 8192, 0.403 -> 0.389 at
+// 4096, 0.344 -> 0.342 at 128; 12 tiles at short contexts: 0.348 at 128.
+constexpr int kRingAheadLong = kTileBars;
+constexpr int kRingAheadShort = 7;
 constexpr int kProducerWarp = kConsumerWarps;            // warp 15
 constexpr int kRowBytes = kHidden * 4;                   // one 576-float row
 constexpr int kStripBytes = kStepBlock * kStepStripRows * 4;  // one 2-D box (3072 B)
@@ -251,8 +262,10 @@ struct HotParams {
 struct Shared {
     HotParams hp;
     Sched s;
-    uint64_t full[kStepSlots];
-    uint64_t empty[kStepSlots];
+    uint64_t full[kTileBars];
+    uint64_t empty[kTileBars];
+    uint32_t toff[kTileBars];   // ring byte offset of tile k at k % kTileBars (producer -> consumers)
+    int64_t tend[kTileBars];    // producer bookkeeping: end of tile k in the ring's byte stream
     alignas(16) float hraw[kHidden];          // layer input h
     alignas(16) float mid[kHidden];           // h' (kept for the next layer's h)
     alignas(16) float xs[kHidden];            // normalised vector
@@ -450,13 +463,21 @@ __device__ bool producer_wait(const StepArgs& a, Shared& sh, uint64_t* bar, uint
     return true;
 }
 
+__device__ __forceinline__ uint64_t* tile_full(Shared& sh, int k) { return &sh.full[k % kTileBars]; }
+__device__ __forceinline__ uint64_t* tile_empty(Shared& sh, int k) { return &sh.empty[k % kTileBars]; }
+__device__ __forceinline__ uint32_t tile_parity(int k) { return static_cast<uint32_t>(k / kTileBars) & 1u; }
+
+// Tile k in the ring (its offset is published before its full barrier's arrival).
+__device__ __forceinline__ const float* slot_ptr(const Shared& sh, unsigned char* ring, int k) {
+    return reinterpret_cast<const float*>(ring + sh.toff[k % kTileBars]);
+}
+
 // Consumer side of tile k: wait until it landed; nullptr (uniformly) on abort.
 __device__ const float* acquire(const StepArgs& a, Shared& sh, unsigned char* ring, int k) {
-    const int slot = k % kStepSlots;
-    wait_bar(a, sh, &sh.full[slot], static_cast<uint32_t>(k / kStepSlots) & 1u);
+    wait_bar(a, sh, tile_full(sh, k), tile_parity(k));
     consumer_sync();
     if (sh.abort) return nullptr;
-    return reinterpret_cast<const float*>(ring + static_cast<size_t>(slot) * kStepSlotBytes);
+    return slot_ptr(sh, ring, k);
 }
 
 // Every consumer thread waits (bounded) until tiles k .. k + n - 1 landed,
@@ -464,17 +485,13 @@ __device__ const float* acquire(const StepArgs& a, Shared& sh, unsigned char* ri
 // visible (sh.abort), and the caller reads sh.abort after it.
 __device__ void wait_tiles(const StepArgs& a, Shared& sh, int k, int n) {
     for (int b = 0; b < n; ++b)
-        if (!wait_bar(a, sh, &sh.full[(k + b) % kStepSlots], static_cast<uint32_t>((k + b) / kStepSlots) & 1u)) break;
-}
-
-__device__ __forceinline__ const float* slot_ptr(unsigned char* ring, int k) {
-    return reinterpret_cast<const float*>(ring + static_cast<size_t>(k % kStepSlots) * kStepSlotBytes);
+        if (!wait_bar(a, sh, tile_full(sh, k + b), tile_parity(k + b))) break;
 }
 
 // Tiles k .. k + n - 1 (one attention batch): wait until all landed; false (uniformly) on abort.
 __device__ bool acquire_batch(const StepArgs& a, Shared& sh, int k, int n) {
     for (int b = 0; b < n; ++b)
-        if (!wait_bar(a, sh, &sh.full[(k + b) % kStepSlots], static_cast<uint32_t>((k + b) / kStepSlots) & 1u)) break;
+        if (!wait_bar(a, sh, tile_full(sh, k + b), tile_parity(k + b))) break;
     consumer_sync();
     return !sh.abort;
 }
@@ -482,7 +499,7 @@ __device__ bool acquire_batch(const StepArgs& a, Shared& sh, int k, int n) {
 __device__ void release_batch(Shared& sh, int k, int n) {
     consumer_sync();
     if (threadIdx.x == 0) {
-        for (int b = 0; b < n; ++b) mbar_arrive(&sh.empty[(k + b) % kStepSlots]);
+        for (int b = 0; b < n; ++b) mbar_arrive(tile_empty(sh, k + b));
         sh.consumed = k + n;
     }
 }
@@ -490,7 +507,7 @@ __device__ void release_batch(Shared& sh, int k, int n) {
 __device__ void release(Shared& sh, int k) {
     consumer_sync();
     if (threadIdx.x == 0) {
-        mbar_arrive(&sh.empty[k % kStepSlots]);
+        mbar_arrive(tile_empty(sh, k));
         sh.consumed = k + 1;
     }
 }
@@ -746,7 +763,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         sh.hp.nch = a.nch;
     }
     if (tid == 0) {
-        for (int i = 0; i < kStepSlots; ++i) {
+        for (int i = 0; i < kTileBars; ++i) {
             mbar_init(&sh.full[i], 1);
             mbar_init(&sh.empty[i], 1);
         }
@@ -767,14 +784,37 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     if (warp == kProducerWarp) {
         // ---------------------------------------------------------- producer
         if (lane == 0) {
-            for (int k = 0; k < s.total; ++k) {
-                const int slot = k % kStepSlots;
-                if (!producer_wait(a, sh, &sh.empty[slot], (static_cast<uint32_t>(k / kStepSlots) & 1u) ^ 1u)) break;
-                unsigned char* dst = ring + static_cast<size_t>(slot) * kStepSlotBytes;
-                const uint32_t bytes = issue_tile(a, sh.hp, s, k, dst, &sh.full[slot], TileOp::kCount);
+            // The ring as a byte stream: tile k occupies [start, end) with
+            // start = the stream position (moved to the next lap when the
+            // tile would straddle the ring's end).  It may be written once the
+            // tiles whose bytes it reuses (those ending after end - ring size)
+            // are released, in order, and at most `ahead` tiles are in flight
+            // (which also frees its barrier pair: tile k - kTileBars released).
+            int64_t pos = 0, freed = 0;
+            int next = 0;  // oldest tile whose release the producer has not yet seen
+            const int ahead = s.n_att >= 2 ? kRingAheadLong : kRingAheadShort;
+            bool ok = true;
+            for (int k = 0; ok && k < s.total; ++k) {
+                const uint32_t bytes = issue_tile(a, sh.hp, s, k, nullptr, nullptr, TileOp::kCount);
+                const int64_t size = (static_cast<int64_t>(bytes) + 127) / 128 * 128;
+                if (pos % kRingBytes + size > kRingBytes) pos += kRingBytes - pos % kRingBytes;
+                const int64_t end = pos + size;
+                while (next < k && (freed < end - kRingBytes || next <= k - ahead)) {
+                    if (!producer_wait(a, sh, tile_empty(sh, next), tile_parity(next))) {
+                        ok = false;
+                        break;
+                    }
+                    freed = sh.tend[next % kTileBars];
+                    ++next;
+                }
+                if (!ok) break;
+                sh.toff[k % kTileBars] = static_cast<uint32_t>(pos % kRingBytes);
+                sh.tend[k % kTileBars] = end;
+                unsigned char* dst = ring + pos % kRingBytes;
+                pos = end;
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive_expect_tx(&sh.full[slot], bytes);
-                issue_tile(a, sh.hp, s, k, dst, &sh.full[slot], TileOp::kLoad);
+                mbar_arrive_expect_tx(tile_full(sh, k), bytes);
+                issue_tile(a, sh.hp, s, k, dst, tile_full(sh, k), TileOp::kLoad);
                 sh.issued = k + 1;
             }
         }
@@ -824,7 +864,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             // barrier of the h read below also publishes this wait.  xs gets
             // h * norm weight, and the dot products take the 1 / rms factor.
             wait_tiles(a, sh, k, 1);
-            const float* t = slot_ptr(ring, k);
+            const float* t = slot_ptr(sh, ring, k);
             if (l == 0) {
                 const bool valid = s.tok >= 0 && s.tok < a.vocab;
                 float ss = 0.0f;
@@ -943,11 +983,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     }
                     __syncwarp();
                     LAYER_MARK(2);
-                    if (s.n_att > 0) wait_bar(a, sh, &sh.full[k % kStepSlots], static_cast<uint32_t>(k / kStepSlots) & 1u);
+                    if (s.n_att > 0) wait_bar(a, sh, tile_full(sh, k), tile_parity(k));
                     LAYER_MARK(3);
                     const int cached = static_cast<int>(s.cached_end - s.a0);  // rows in the tile (K, then V)
                     const int rows = static_cast<int>(s.a1 - s.a0);
-                    const float* tile = slot_ptr(ring, k);
+                    const float* tile = slot_ptr(sh, ring, k);
                     const float scale2 = sh.hp.scale[l] * kLog2e;
                     const bool valid = lane < rows;
                     const float4* k4 = reinterpret_cast<const float4*>(lane < cached ? tile + lane * kHeadDim : sh.knew);
@@ -990,7 +1030,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                     }
                     __syncwarp();  // the warp is done with the tile
                     if (lane == 0 && s.n_att > 0) {
-                        mbar_arrive(&sh.empty[k % kStepSlots]);
+                        mbar_arrive(tile_empty(sh, k));
                         sh.consumed = k + 1;
                     }
                     LAYER_MARK(4);
@@ -1059,8 +1099,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                         goto done;
                     }
                     auto tile_base = [&](int gi) {
-                        return reinterpret_cast<const float*>(
-                            ring + static_cast<size_t>((k + gi / kStepAttnRows) % kStepSlots) * kStepSlotBytes);
+                        return slot_ptr(sh, ring, k + gi / kStepAttnRows);
                     };
                     auto key_row = [&](int gi) -> const float* {
                         if (gi >= cached) return sh.knew;
@@ -1153,9 +1192,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                         for (int b = 0; b < nb; ++b) {
                             const int base = b * kStepAttnRows;
                             const int n = min(kStepAttnRows, cached - base);
-                            const float* vb = reinterpret_cast<const float*>(
-                                                  ring + static_cast<size_t>((k + b) % kStepSlots) * kStepSlotBytes) +
-                                              n * kHeadDim + pq * 4;
+                            const float* vb = slot_ptr(sh, ring, k + b) + n * kHeadDim + pq * 4;
                             int rr = psplit - base % kPvSplits;
                             if (rr < 0) rr += kPvSplits;
                             for (; rr + kPvSplits < n; rr += 2 * kPvSplits) {  // two rows per trip
@@ -1199,7 +1236,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 }
                 consumer_sync();  // every thread is done with the last batch's tiles
                 if (tid == 0) {
-                    for (int b = 0; b < last_batch; ++b) mbar_arrive(&sh.empty[(k + b) % kStepSlots]);
+                    for (int b = 0; b < last_batch; ++b) mbar_arrive(tile_empty(sh, k + b));
                     sh.consumed = k + last_batch;
                 }
                 k += last_batch;
@@ -1300,13 +1337,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 const float inv = norm_inverse(sh, sh.hp.eps);
                 // warp f: gate row f on lanes 0-15, up row f on lanes 16-31, SwiGLU on lane 0.
                 if (warp < nf) {
-                    const float y = row_dot(slot_ptr(ring, k + half) + warp * kHidden, sh.xs, l16) * inv;
+                    const float y = row_dot(slot_ptr(sh, ring, k + half) + warp * kHidden, sh.xs, l16) * inv;
                     const float up = __shfl_sync(0xffffffffu, y, 16);
                     if (lane == 0) sh.act[warp] = swiglu(y, up);
                 }
                 consumer_sync();
                 LAYER_MARK(10);
-                tally_products(slot_ptr(ring, k + 2), sh.act, s.f1 - s.f0, down_tally(l) + s.replica, down_overflow(l));
+                tally_products(slot_ptr(sh, ring, k + 2), sh.act, s.f1 - s.f0, down_tally(l) + s.replica, down_overflow(l));
                 release_batch(sh, k, 3);
                 k += 3;
             }
@@ -1321,7 +1358,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             if (s.n_lm > 0) {
                 if (!tally_read(a, sh, down_tally(kLayers - 1), down_overflow(kLayers - 1), sh.mid, sh.hraw, G)) goto done;
                 wait_tiles(a, sh, k, 1);
-                const float* t = slot_ptr(ring, k);
+                const float* t = slot_ptr(sh, ring, k);
                 normalise(sh, sh.hraw, t, sh.hp.eps);
                 if (sh.abort) goto done;
                 if (s.v0 == 0)
@@ -1392,7 +1429,7 @@ done:
         // After an abort: wait (bounded) for copies the consumers never released.
         for (int kk = sh.consumed; kk < sh.issued; ++kk) {
             const unsigned long long t0 = global_timer();
-            while (!mbar_try_wait(&sh.full[kk % kStepSlots], static_cast<uint32_t>(kk / kStepSlots) & 1u))
+            while (!mbar_try_wait(tile_full(sh, kk), tile_parity(kk)))
                 if (global_timer() - t0 > kWaitNs) break;
         }
     }
