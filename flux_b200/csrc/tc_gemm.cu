@@ -255,6 +255,284 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     }
 }
 
+// Persistent form for large M (the prefill's projections, 128-row tiles, no
+// K split): one CTA per SM walks the tiles t = blockIdx.x + u * gridDim.x
+// (weight block fastest), so the TMA ring, TMEM and the barriers persist
+// across tiles and a tile's first loads are issued while the previous tile
+// still multiplies.  448 threads:
+//   warp 0, lane 0  TMA producer over every (tile, stage) in order: W_hi,
+//                   W_lo and raw X boxes into a 4-stage ring (48 KB each);
+//   warp 1          512 TMEM columns: [0, 128) the tile's cross terms,
+//                   [128, 512) three hi.hi group buffers; lane 0 issues the
+//                   MMAs, commits each stage to empty[stage], each group to
+//                   acc_full and each tile's last stage to tile_full;
+//   warps 2-5       split each staged X tile into hi (in place) and lo (one
+//                   of two 16 KB buffers, reused once empty[] shows the MMAs
+//                   of the stage two back done);
+//   warps 6-13      promote the hi.hi groups into FP32 registers, then take
+//                   the tile's cross terms, free them for the next tile and
+//                   store C while the next tile multiplies (three group
+//                   buffers let the MMAs run six stages ahead of the store).
+// Each tile's sums are formed as in tc_gemm_kernel<128, *>: the same
+// products, the same groups of kTcPromote stages and the same order of the
+// FP32 adds.  Every mbarrier operation and tcgen05.commit of the MMA thread
+// costs ~110-170 cycles that do not overlap the queued MMAs (measured on
+// B200), so the MMA thread commits once per stage plus once per group.
+constexpr int kPtThreads = 448;
+constexpr int kPtSplit = 128;
+constexpr int kPtEpi = 256;
+constexpr int kPtStages = 4;
+constexpr uint32_t kPtX = 128 * kTcTileK * 4;    // 16 KB
+constexpr uint32_t kPtStage = 2 * kWBox + kPtX;  // W_hi, W_lo, X (-> X_hi)
+constexpr size_t kPtSmem = static_cast<size_t>(kPtStages) * kPtStage + 2 * kPtX + 1024 + 256;
+static_assert(kPtSmem <= 232448, "the persistent GEMM's shared memory exceeds one CTA's limit");
+
+__global__ void __launch_bounds__(kPtThreads, 1) tc_gemm_persistent_kernel(const __grid_constant__ TcGemmArgs a) {
+    constexpr int S = kPtStages;
+    extern __shared__ unsigned char tc_raw[];
+    unsigned char* smem = tc_raw + ((1024u - (smem_addr(tc_raw) & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kPtStage + 2 * kPtX);
+    uint64_t* conv = full + S;
+    uint64_t* empty = conv + S;
+    uint64_t* acc_full = empty + S;     // [3] a group's hi.hi products are in TMEM
+    uint64_t* acc_empty = acc_full + 3; // [3] the epilogue has taken them
+    uint64_t* tile_full = acc_empty + 3;   // a tile's cross terms are complete
+    uint64_t* tile_empty = tile_full + 1;  // the epilogue has taken them
+    uint64_t* done = tile_empty + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int nblocks = (a.n + kTcTileN - 1) / kTcTileN;
+    const int tiles = nblocks * ((a.m + 127) / 128);
+    const int mine = static_cast<int>(blockIdx.x) < tiles ? (tiles - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
+    const int nk = a.k / kTcTileK;
+    auto tile_n0 = [&](int u) { return (static_cast<int>(blockIdx.x) + u * static_cast<int>(gridDim.x)) % nblocks * kTcTileN; };
+    auto tile_m0 = [&](int u) { return (static_cast<int>(blockIdx.x) + u * static_cast<int>(gridDim.x)) / nblocks * 128; };
+    auto w_hi = [&](int s) { return smem + s * kPtStage; };
+    auto w_lo = [&](int s) { return smem + s * kPtStage + kWBox; };
+    auto x_hi = [&](int s) { return smem + s * kPtStage + 2 * kWBox; };
+    auto x_lo = [&](int b) { return smem + S * kPtStage + b * kPtX; };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            bar_init(&full[s], 1);
+            bar_init(&conv[s], kPtSplit);
+            bar_init(&empty[s], 1);
+        }
+        for (int j = 0; j < 3; ++j) {
+            bar_init(&acc_full[j], 1);
+            bar_init(&acc_empty[j], kPtEpi);
+        }
+        bar_init(tile_full, 1);
+        bar_init(tile_empty, kPtEpi);
+        bar_init(done, 1);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            bool ok = true;
+            for (int u = 0; ok && u < mine; ++u) {
+                const int n0 = tile_n0(u), m0 = tile_m0(u);
+                for (int j = 0; j < nk; ++j) {
+                    const int i = u * nk + j, s = i % S;
+                    if (i >= S && !bar_wait(&empty[s], static_cast<uint32_t>(i / S - 1) & 1u, abort, a.error)) {
+                        ok = false;
+                        break;
+                    }
+                    if (*abort) {
+                        ok = false;
+                        break;
+                    }
+                    bar_expect(&full[s], kPtStage);
+                    tma_box(w_hi(s), &a.w_hi, j * kTcTileK, n0, &full[s]);
+                    tma_box(w_lo(s), &a.w_lo, j * kTcTileK, n0, &full[s]);
+                    if (i == 0) grid_dependency_wait();  // X comes from the previous kernel
+                    tma_box(x_hi(s), &a.x, j * kTcTileK, m0, &full[s]);
+                    issued = i + 1;
+                }
+            }
+            if (issued == 0) grid_dependency_wait();
+            // Copies still in flight land before the CTA leaves (a no-op
+            // unless a consumer gave up early).
+            for (int i = max(0, issued - S); i < issued; ++i) {
+                const unsigned long long t0 = now_ns();
+                while (!bar_test(&full[i % S], static_cast<uint32_t>(i / S) & 1u))
+                    if (now_ns() - t0 > kTcWaitNs) break;
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = tf32_idesc(128);
+            bool ok = true;
+            int group = 0;
+            for (int u = 0; ok && u < mine; ++u) {
+                for (int j = 0; j < nk; ++j) {
+                    const int i = u * nk + j, s = i % S, b = i & 1;
+                    const bool first = j % kTcPromote == 0, last = j % kTcPromote == kTcPromote - 1 || j == nk - 1;
+                    if (!bar_wait(&conv[s], static_cast<uint32_t>(i / S) & 1u, abort, a.error) ||
+                        (j == 0 && u >= 1 &&
+                         !bar_wait(tile_empty, static_cast<uint32_t>(u - 1) & 1u, abort, a.error)) ||
+                        (first && group >= 3 &&
+                         !bar_wait(&acc_empty[group % 3], static_cast<uint32_t>(group / 3 - 1) & 1u, abort,
+                                   a.error))) {
+                        ok = false;
+                        break;
+                    }
+                    fence_after_sync();
+                    const uint64_t ah = sw128_desc(smem_addr(w_hi(s))), al = sw128_desc(smem_addr(w_lo(s)));
+                    const uint64_t bh = sw128_desc(smem_addr(x_hi(s))), bl = sw128_desc(smem_addr(x_lo(b)));
+                    const uint32_t cross = tmem, main_acc = tmem + static_cast<uint32_t>(128 + group % 3 * 128);
+#pragma unroll
+                    for (int kk = 0; kk < kTcTileK / 8; ++kk) {
+                        const uint64_t step = static_cast<uint64_t>(kk * 32 >> 4);  // 8 TF32 = 32 bytes
+                        mma_tf32(cross, ah + step, bl + step, idesc, (j | kk) != 0 ? 1u : 0u);
+                        mma_tf32(cross, al + step, bh + step, idesc, 1u);
+                        mma_tf32(main_acc, ah + step, bh + step, idesc, (!first || kk != 0) ? 1u : 0u);
+                    }
+                    mma_commit(&empty[s]);
+                    if (last) mma_commit(&acc_full[group++ % 3]);
+                    if (j == nk - 1) mma_commit(tile_full);
+                }
+            }
+            // every MMA issued above completes before TMEM is freed
+            mma_commit(done);
+            const unsigned long long t0 = now_ns();
+            while (!bar_test(done, 0))
+                if (now_ns() - t0 > kTcWaitNs) break;
+        }
+        __syncwarp();
+    } else if (warp < 6) {
+        const int t = threadIdx.x - 64;  // 0..127
+        bool ok = true;
+        for (int u = 0; ok && u < mine; ++u) {
+            for (int j = 0; j < nk; ++j) {
+                const int i = u * nk + j, s = i % S, b = i & 1;
+                // X_lo buffer b was last read by the MMAs of stage i - 2; empty[(i - 2) % S]
+                // cannot run a phase past them, since stage i + 2 needs this split first.
+                if (!bar_wait(&full[s], static_cast<uint32_t>(i / S) & 1u, abort, a.error) ||
+                    (i >= 2 && !bar_wait(&empty[(i - 2) % S], static_cast<uint32_t>((i - 2) / S) & 1u, abort,
+                                         a.error))) {
+                    ok = false;
+                    break;
+                }
+                float4* xh = reinterpret_cast<float4*>(x_hi(s)) + t;
+                float4* xl = reinterpret_cast<float4*>(x_lo(b)) + t;
+                // a fixed trip count, so that all eight loads are in flight at once
+                constexpr int kPer = 128 * kTcTileK / 4 / kPtSplit;
+                float4 v[kPer];
+#pragma unroll
+                for (int r = 0; r < kPer; ++r) v[r] = xh[r * kPtSplit];
+#pragma unroll
+                for (int r = 0; r < kPer; ++r) {
+                    // integer-ALU rounding (the conversion pipe is quarter rate)
+                    float4 h, l;
+                    h.x = tf32_round_int(v[r].x);
+                    h.y = tf32_round_int(v[r].y);
+                    h.z = tf32_round_int(v[r].z);
+                    h.w = tf32_round_int(v[r].w);
+                    l.x = tf32_round_int(v[r].x - h.x);
+                    l.y = tf32_round_int(v[r].y - h.y);
+                    l.z = tf32_round_int(v[r].z - h.z);
+                    l.w = tf32_round_int(v[r].w - h.w);
+                    xh[r * kPtSplit] = h;
+                    xl[r * kPtSplit] = l;
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                bar_arrive(&conv[s]);
+            }
+        }
+    } else {
+        // Warps w and w + 4 share TMEM lane quarter w % 4 and take one half
+        // of the 128 columns each (see tc_gemm_kernel for the promotion).
+        const int quarter = warp & 3;
+        const int c0 = (warp - 6) / 4 * 64;
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        const int groups = (nk + kTcPromote - 1) / kTcPromote;
+        bool ok = true;
+        int group = 0;
+        bool waited = false;
+        for (int u = 0; ok && u < mine; ++u) {
+            float acc[64];
+#pragma unroll
+            for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
+            for (int g = 0; g < groups; ++g, ++group) {
+                const int j = group % 3;
+                if (!bar_wait(&acc_full[j], static_cast<uint32_t>(group / 3) & 1u, abort, a.error)) {
+                    ok = false;
+                    break;
+                }
+                __syncwarp();
+                fence_after_sync();
+#pragma unroll
+                for (int col = 0; col < 64; col += 32) {
+                    float v[32];
+                    tmem_load32(tmem + lane_base + static_cast<uint32_t>(128 + j * 128 + c0 + col), v);
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) acc[col + c] += v[c];
+                }
+                fence_before_sync();
+                bar_arrive(&acc_empty[j]);
+            }
+            if (!ok || !bar_wait(tile_full, static_cast<uint32_t>(u) & 1u, abort, a.error)) {
+                ok = false;
+                break;
+            }
+            __syncwarp();
+            fence_after_sync();
+            float out[64];
+#pragma unroll
+            for (int col = 0; col < 64; col += 32) {
+                float v[32];
+                tmem_load32(tmem + lane_base + static_cast<uint32_t>(c0 + col), v);
+#pragma unroll
+                for (int c = 0; c < 32; ++c) out[col + c] = acc[col + c] + v[c];
+            }
+            fence_before_sync();
+            bar_arrive(tile_empty);
+            if (!waited) {
+                grid_dependency_wait();  // the residual and C belong to earlier kernels too
+                waited = true;
+            }
+            if (*abort) {
+                ok = false;
+                break;
+            }
+            const int n = tile_n0(u) + quarter * 32 + lane, m0 = tile_m0(u) + c0;
+            if (n < a.n) {
+#pragma unroll
+                for (int q = 0; q < 64; ++q) {
+                    const int m = m0 + q;
+                    if (m < a.m) {
+                        const long long at = static_cast<long long>(m) * a.ldc + n;
+                        a.c[at] = a.residual != nullptr ? out[q] + a.residual[at] : out[q];
+                    }
+                }
+            }
+        }
+        if (!waited) grid_dependency_wait();
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after_sync();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+    }
+}
+
 __global__ void tf32_split_kernel(const float4* __restrict__ w, float4* __restrict__ hi, float4* __restrict__ lo,
                                   size_t n4) {
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
@@ -289,6 +567,20 @@ fx_status launch_variant(const TcGemmArgs& args, dim3 grid, cudaStream_t stream,
                                 "launching the tensor-core GEMM", args);
     tc_gemm_kernel<BM, STAGES><<<grid, kTcThreads, smem, stream>>>(args);
     FX_CUDA_TRY(cudaGetLastError(), "launching the tensor-core GEMM");
+    return FX_OK;
+}
+
+fx_status launch_persistent(const TcGemmArgs& args, cudaStream_t stream) {
+    const fx_status raised = raise_smem_limit(reinterpret_cast<const void*>(tc_gemm_persistent_kernel), kPtSmem,
+                                              "raising the persistent tensor-core GEMM's shared memory");
+    if (raised != FX_OK) return raised;
+    int device = 0, sms = 0;
+    FX_CUDA_TRY(cudaGetDevice(&device), "querying the current device");
+    FX_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "querying the SM count");
+    const long long tiles = static_cast<long long>((args.n + kTcTileN - 1) / kTcTileN) * ((args.m + 127) / 128);
+    const unsigned grid = static_cast<unsigned>(std::min<long long>(tiles, sms));
+    tc_gemm_persistent_kernel<<<grid, kPtThreads, kPtSmem, stream>>>(args);
+    FX_CUDA_TRY(cudaGetLastError(), "launching the persistent tensor-core GEMM");
     return FX_OK;
 }
 
@@ -349,6 +641,10 @@ fx_status launch_tc_gemm(const TcGemmArgs& args, int bm, int splits, cudaStream_
                "tensor-core GEMM: K and its slices must be multiples of 32, M, N > 0");
     const dim3 grid(static_cast<unsigned>((args.n + kTcTileN - 1) / kTcTileN),
                     static_cast<unsigned>((args.m + bm - 1) / bm), static_cast<unsigned>(splits));
+    // 128-row tiles without a K split (the prefill's projections): one
+    // persistent CTA per SM.
+    if (bm == 128 && splits == 1 && stages == 0 && !dependent && args.k_per_split == args.k)
+        return launch_persistent(args, stream);
     if (stages == 0) stages = tc_default_stages(bm);
     if (bm == 64 && stages == 4) return launch_variant<64, 4>(args, grid, stream, dependent);
     if (bm == 64 && stages == 3) return launch_variant<64, 3>(args, grid, stream, dependent);
