@@ -27,6 +27,8 @@
 #include "tc_gemm.cuh"
 #include "tcgen05.cuh"
 
+#include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -533,6 +535,318 @@ __global__ void __launch_bounds__(kPtThreads, 1) tc_gemm_persistent_kernel(const
     }
 }
 
+// Paired form for large M (the prefill's projections; N a multiple of 192,
+// no K split): a cluster of two CTAs on two SMs walks tiles of 256 X rows x
+// 192 W rows, t = pair + u * pairs (W block fastest).  The pair's MMAs
+// (tcgen05 cta_group::2, M = 256, N = 192) take A = X (128 rows from each
+// CTA) and B = W (96 rows from each), so one instruction does twice the
+// per-SM work of a 128 x 128 MMA for the same issue, wait and commit cost on
+// the MMA thread -- those cost ~110-170 cycles each and do not overlap the
+// queued MMAs.  D in each CTA's TMEM: its 128 X rows x the 192 outputs.
+// 384 threads per CTA:
+//   warp 0, lane 0  TMA producer (each CTA): per 32-column stage the CTA's
+//                   raw X box (32 x 128) and W_hi / W_lo boxes (32 x 96)
+//                   into a 4-stage ring, refilled when the leader's commit
+//                   reaches empty[stage] in both CTAs;
+//   warp 1          allocates 512 TMEM columns for the pair; on the leader
+//                   (rank 0) lane 0 waits for both CTAs' split stage
+//                   (conv[stage], 2 arrivals) and issues 12 MMAs per
+//                   stage into one of two 192-column group accumulators
+//                   (every product of 2 stages: Xhi.Wlo + Xlo.Whi + Xhi.Whi
+//                   per K step), committing to both CTAs' empty[stage] and,
+//                   per group, acc_full[group % 2];
+//                   on the peer lane 0 forwards each split stage: it waits
+//                   for the peer's sdone[stage] and arrives on the leader's
+//                   conv[stage] (a cluster-scope release takes ~0.5 us, so
+//                   the split warps do not make it themselves);
+//   warps 2-5       split each staged X tile into hi (in place) and lo (one
+//                   of three 16 KB buffers), then one thread arrives on
+//                   conv[stage] (leader) or sdone[stage] (peer);
+//   warps 6-13      add each group into FP32 registers (warp w: TMEM lane
+//                   quarter w % 4, 96 of the 192 columns), release the group
+//                   on the leader's acc_empty, and after a tile's last group
+//                   store its rows (float4 stores, + residual).
+// The tensor core's accumulation truncates, so each group of 2 stages (8
+// hi.hi products) starts a fresh accumulator and is added in FP32 with
+// round-to-nearest, as in the other forms.
+constexpr int kPrThreads = 448;
+constexpr int kPrSplit = 128;
+constexpr int kPrEpiWarps = 8;
+constexpr int kPrStages = 4;
+constexpr int kPrXlo = 3;
+constexpr uint32_t kPrX = 128 * kTcTileK * 4;            // 16 KB
+constexpr uint32_t kPrW = (kTcPairN / 2) * kTcTileK * 4;  // 12 KB
+constexpr uint32_t kPrStage = kPrX + 2 * kPrW;            // X (-> X_hi), W_hi, W_lo
+constexpr size_t kPrSmem = static_cast<size_t>(kPrStages) * kPrStage + kPrXlo * kPrX + 1024 + 256;
+static_assert(kPrSmem <= 232448, "the paired GEMM's shared memory exceeds one CTA's limit");
+static_assert(kPrW % 1024 == 0 && kPrStage % 1024 == 0, "operand tiles keep the 1024-byte swizzle alignment");
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPrThreads, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ TcGemmArgs a) {
+    constexpr int S = kPrStages;
+    extern __shared__ unsigned char tc_raw[];
+    unsigned char* smem = tc_raw + ((1024u - (smem_addr(tc_raw) & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kPrStage + kPrXlo * kPrX);
+    uint64_t* empty = full + S;         // the leader's MMAs of a stage are done (both CTAs)
+    uint64_t* conv = empty + S;         // leader: both CTAs split the stage
+    uint64_t* acc_full = conv + S;      // [2] a group is in TMEM (both CTAs)
+    uint64_t* acc_empty = acc_full + 2; // [2] leader: both CTAs' epilogues took it
+    uint64_t* sdone = acc_empty + 2;    // peer: its split of a stage is done (for the forwarder)
+    uint64_t* done = sdone + S;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t rank = cluster_rank();
+    const int pair = static_cast<int>(blockIdx.x) / 2, pairs = static_cast<int>(gridDim.x) / 2;
+    const int nblocks = a.n / kTcPairN;
+    const int tiles = nblocks * ((a.m + 255) / 256);
+    const int mine = pair < tiles ? (tiles - 1 - pair) / pairs + 1 : 0;
+    const int nk = a.k / kTcTileK;
+    auto tile_n0 = [&](int u) { return (pair + u * pairs) % nblocks * kTcPairN; };
+    auto tile_m0 = [&](int u) { return (pair + u * pairs) / nblocks * 256 + static_cast<int>(rank) * 128; };
+    auto x_hi = [&](int s) { return smem + s * kPrStage; };
+    auto w_hi = [&](int s) { return smem + s * kPrStage + kPrX; };
+    auto w_lo = [&](int s) { return smem + s * kPrStage + kPrX + kPrW; };
+    auto x_lo = [&](int b) { return smem + S * kPrStage + b * kPrX; };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            bar_init(&full[s], 1);
+            bar_init(&empty[s], 1);
+            bar_init(&conv[s], 2);
+            bar_init(&sdone[s], 1);
+        }
+        for (int j = 0; j < 2; ++j) {
+            bar_init(&acc_full[j], 1);
+            bar_init(&acc_empty[j], 2 * kPrEpiWarps);
+        }
+        bar_init(done, 1);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    cluster_sync();  // both CTAs' barriers exist before either arrives on the other's
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            bool ok = true;
+            const int w0 = static_cast<int>(rank) * (kTcPairN / 2);
+            for (int u = 0; ok && u < mine; ++u) {
+                const int n0 = tile_n0(u) + w0, m0 = tile_m0(u);
+                for (int j = 0; j < nk; ++j) {
+                    const int i = u * nk + j, s = i % S;
+                    if (i >= S && !bar_wait(&empty[s], static_cast<uint32_t>(i / S - 1) & 1u, abort, a.error)) {
+                        ok = false;
+                        break;
+                    }
+                    if (*abort) {
+                        ok = false;
+                        break;
+                    }
+                    bar_expect(&full[s], kPrStage);
+                    tma_box(w_hi(s), &a.w_hi96, j * kTcTileK, n0, &full[s]);
+                    tma_box(w_lo(s), &a.w_lo96, j * kTcTileK, n0, &full[s]);
+                    if (i == 0) grid_dependency_wait();  // X comes from the previous kernel
+                    tma_box(x_hi(s), &a.x, j * kTcTileK, m0, &full[s]);
+                    issued = i + 1;
+                }
+            }
+            if (issued == 0) grid_dependency_wait();
+            // Copies still in flight land before the CTA leaves (a no-op
+            // unless a consumer gave up early).
+            for (int i = max(0, issued - S); i < issued; ++i) {
+                const unsigned long long t0 = now_ns();
+                while (!bar_test(&full[i % S], static_cast<uint32_t>(i / S) & 1u))
+                    if (now_ns() - t0 > kTcWaitNs) break;
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = tf32_idesc_pair(kTcPairN);
+            bool ok = true;
+            int group = 0;
+            for (int u = 0; ok && u < mine; ++u) {
+                for (int j = 0; j < nk; ++j) {
+                    const int i = u * nk + j, s = i % S;
+                    const bool first = j % kTcPromote == 0, last = j % kTcPromote == kTcPromote - 1 || j == nk - 1;
+                    if (!bar_wait_cluster(&conv[s], static_cast<uint32_t>(i / S) & 1u, abort, a.error) ||
+                        (first && group >= 2 &&
+                         !bar_wait_cluster(&acc_empty[group & 1], static_cast<uint32_t>(group / 2 - 1) & 1u, abort,
+                                           a.error))) {
+                        ok = false;
+                        break;
+                    }
+                    fence_after_sync();
+                    const uint64_t ah = sw128_desc(smem_addr(x_hi(s))), al = sw128_desc(smem_addr(x_lo(i % kPrXlo)));
+                    const uint64_t bh = sw128_desc(smem_addr(w_hi(s))), bl = sw128_desc(smem_addr(w_lo(s)));
+                    const uint32_t acc = tmem + static_cast<uint32_t>((group & 1) * 256);
+#pragma unroll
+                    for (int kk = 0; kk < kTcTileK / 8; ++kk) {
+                        const uint64_t step = static_cast<uint64_t>(kk * 32 >> 4);  // 8 TF32 = 32 bytes
+                        mma_tf32_pair(acc, ah + step, bl + step, idesc, (!first || kk != 0) ? 1u : 0u);
+                        mma_tf32_pair(acc, al + step, bh + step, idesc, 1u);
+                        mma_tf32_pair(acc, ah + step, bh + step, idesc, 1u);
+                    }
+                    mma_commit_pair(&empty[s]);
+                    if (last) mma_commit_pair(&acc_full[group++ & 1]);
+                }
+            }
+            // every MMA issued above completes before TMEM is freed
+            mma_commit_pair(done);
+        }
+        if (lane == 0 && rank != 0) {
+            // the peer's forwarder: its split stages to the leader's conv[]
+            for (int i = 0; i < mine * nk; ++i) {
+                if (!bar_wait(&sdone[i % S], static_cast<uint32_t>(i / S) & 1u, abort, a.error)) break;
+                bar_arrive_rank(&conv[i % S], 0);
+            }
+        }
+        if (lane == 0) {
+            const unsigned long long t0 = now_ns();
+            while (!bar_test(done, 0))
+                if (now_ns() - t0 > kTcWaitNs) break;
+        }
+        __syncwarp();
+    } else if (warp < 2 + kPrSplit / 32) {
+        const int t = threadIdx.x - 64;  // 0..127
+        bool stop = false;
+        for (int u = 0; !stop && u < mine; ++u) {
+            for (int j = 0; j < nk; ++j) {
+                const int i = u * nk + j, s = i % S;
+                // X_lo buffer i % 3 was last read by the MMAs of stage i - 3;
+                // empty[(i - 3) % S] cannot run a phase past them, since stage
+                // i + 1 needs this split first.
+                const bool ready =
+                    bar_wait(&full[s], static_cast<uint32_t>(i / S) & 1u, abort, a.error) &&
+                    (i < kPrXlo ||
+                     bar_wait(&empty[(i - kPrXlo) % S], static_cast<uint32_t>((i - kPrXlo) / S) & 1u, abort, a.error));
+                if (ready) {
+                    float4* xh = reinterpret_cast<float4*>(x_hi(s)) + t;
+                    float4* xl = reinterpret_cast<float4*>(x_lo(i % kPrXlo)) + t;
+                    constexpr int kHalf = 128 * kTcTileK / 4 / kPrSplit / 2;  // 4 float4 per pass
+#pragma unroll
+                    for (int pass = 0; pass < 2; ++pass) {
+                        float4 v[kHalf];
+#pragma unroll
+                        for (int r = 0; r < kHalf; ++r) v[r] = xh[(pass * kHalf + r) * kPrSplit];
+#pragma unroll
+                        for (int r = 0; r < kHalf; ++r) {
+                            // integer-ALU rounding (the conversion pipe is quarter rate)
+                            float4 h, l;
+                            h.x = tf32_round_int(v[r].x);
+                            h.y = tf32_round_int(v[r].y);
+                            h.z = tf32_round_int(v[r].z);
+                            h.w = tf32_round_int(v[r].w);
+                            l.x = tf32_round_int(v[r].x - h.x);
+                            l.y = tf32_round_int(v[r].y - h.y);
+                            l.z = tf32_round_int(v[r].z - h.z);
+                            l.w = tf32_round_int(v[r].w - h.w);
+                            xh[(pass * kHalf + r) * kPrSplit] = h;
+                            xl[(pass * kHalf + r) * kPrSplit] = l;
+                        }
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                }
+                // One arrival per CTA and stage: the split threads meet on a
+                // named barrier that also ORs their stop flags, so every one
+                // of them leaves the loop at the same stage and none waits
+                // there alone.
+                uint32_t any_stop;
+                asm volatile(
+                    "{\n\t.reg .pred q, r;\n\t"
+                    "setp.ne.u32 q, %1, 0;\n\t"
+                    "bar.red.or.pred r, 1, %2, q;\n\t"
+                    "selp.u32 %0, 1, 0, r;\n\t}"
+                    : "=r"(any_stop)
+                    : "r"(ready && !*abort ? 0u : 1u), "n"(kPrSplit)
+                    : "memory");
+                if (any_stop != 0) {
+                    stop = true;
+                    break;
+                }
+                if (t == 0) bar_arrive(rank == 0 ? &conv[s] : &sdone[s]);
+            }
+        }
+    } else {
+        const int quarter = warp & 3;
+        const int c0 = (warp - 6) / 4 * (kTcPairN / 2);  // 0 or 96
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        const int groups = (nk + kTcPromote - 1) / kTcPromote;
+        bool ok = true;
+        int group = 0;
+        bool waited = false;
+        for (int u = 0; ok && u < mine; ++u) {
+            float acc[kTcPairN / 2];
+#pragma unroll
+            for (int c = 0; c < kTcPairN / 2; ++c) acc[c] = 0.0f;
+            for (int g = 0; g < groups; ++g, ++group) {
+                const int j = group & 1;
+                if (!bar_wait(&acc_full[j], static_cast<uint32_t>(group / 2) & 1u, abort, a.error)) {
+                    ok = false;
+                    break;
+                }
+                __syncwarp();
+                fence_after_sync();
+#pragma unroll
+                for (int col = 0; col < kTcPairN / 2; col += 16) {
+                    float v[16];
+                    tmem_load16(tmem + lane_base + static_cast<uint32_t>(j * 256 + c0 + col), v);
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) acc[col + c] += v[c];
+                }
+                fence_before_sync();
+                __syncwarp();
+                if (lane == 0) bar_arrive_rank(&acc_empty[j], 0);
+            }
+            if (!ok) break;
+            if (!waited) {
+                grid_dependency_wait();  // the residual and C belong to earlier kernels too
+                waited = true;
+            }
+            if (*abort) {
+                ok = false;
+                break;
+            }
+            const int m = tile_m0(u) + quarter * 32 + lane, n0 = tile_n0(u) + c0;
+            if (m < a.m) {
+                float* crow = a.c + static_cast<long long>(m) * a.ldc + n0;
+                const float* rrow = a.residual != nullptr ? a.residual + static_cast<long long>(m) * a.ldc + n0 : nullptr;
+#pragma unroll
+                for (int q = 0; q < kTcPairN / 2; q += 4) {
+                    float4 o = make_float4(acc[q], acc[q + 1], acc[q + 2], acc[q + 3]);
+                    if (rrow != nullptr) {
+                        const float4 r = *reinterpret_cast<const float4*>(rrow + q);
+                        o.x += r.x;
+                        o.y += r.y;
+                        o.z += r.z;
+                        o.w += r.w;
+                    }
+                    *reinterpret_cast<float4*>(crow + q) = o;
+                }
+            }
+        }
+        if (!waited) grid_dependency_wait();
+    }
+    fence_before_sync();
+    __syncthreads();
+    cluster_sync();  // neither CTA frees TMEM or leaves while the pair may still use it
+    if (warp == 1) {
+        fence_after_sync();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+    }
+}
+
 __global__ void tf32_split_kernel(const float4* __restrict__ w, float4* __restrict__ hi, float4* __restrict__ lo,
                                   size_t n4) {
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
@@ -581,6 +895,44 @@ fx_status launch_persistent(const TcGemmArgs& args, cudaStream_t stream) {
     const unsigned grid = static_cast<unsigned>(std::min<long long>(tiles, sms));
     tc_gemm_persistent_kernel<<<grid, kPtThreads, kPtSmem, stream>>>(args);
     FX_CUDA_TRY(cudaGetLastError(), "launching the persistent tensor-core GEMM");
+    return FX_OK;
+}
+
+fx_status launch_pair(const TcGemmArgs& args, cudaStream_t stream) {
+    const fx_status raised = raise_smem_limit(reinterpret_cast<const void*>(tc_gemm_pair_kernel), kPrSmem,
+                                              "raising the paired tensor-core GEMM's shared memory");
+    if (raised != FX_OK) return raised;
+    // every pair of a persistent grid must be resident at once
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(2, 1, 1);
+    config.blockDim = dim3(kPrThreads, 1, 1);
+    config.dynamicSmemBytes = kPrSmem;
+    config.stream = stream;
+    cudaLaunchAttribute cluster{};
+    cluster.id = cudaLaunchAttributeClusterDimension;
+    cluster.val.clusterDim.x = 2;
+    cluster.val.clusterDim.y = 1;
+    cluster.val.clusterDim.z = 1;
+    config.attrs = &cluster;
+    config.numAttrs = 1;
+    // resident pairs per device, queried once (the query costs host time on every launch otherwise)
+    static std::atomic<int> resident[64];
+    int device = 0;
+    FX_CUDA_TRY(cudaGetDevice(&device), "querying the current device");
+    int clusters = device >= 0 && device < 64 ? resident[device].load(std::memory_order_relaxed) : 0;
+    if (clusters <= 0) {
+        FX_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, tc_gemm_pair_kernel, &config),
+                    "querying the resident CTA pairs of the paired GEMM");
+        if (device >= 0 && device < 64) resident[device].store(clusters, std::memory_order_relaxed);
+    }
+    if (clusters <= 0) {
+        set_error("paired tensor-core GEMM: no CTA pair fits on this device");
+        return FX_ERR_CUDA;
+    }
+    const long long tiles = static_cast<long long>(args.n / kTcPairN) * ((args.m + 255) / 256);
+    const unsigned grid = static_cast<unsigned>(2 * std::min<long long>(tiles, clusters));
+    tc_gemm_pair_kernel<<<grid, kPrThreads, kPrSmem, stream>>>(args);
+    FX_CUDA_TRY(cudaGetLastError(), "launching the paired tensor-core GEMM");
     return FX_OK;
 }
 
@@ -641,8 +993,12 @@ fx_status launch_tc_gemm(const TcGemmArgs& args, int bm, int splits, cudaStream_
                "tensor-core GEMM: K and its slices must be multiples of 32, M, N > 0");
     const dim3 grid(static_cast<unsigned>((args.n + kTcTileN - 1) / kTcTileN),
                     static_cast<unsigned>((args.m + bm - 1) / bm), static_cast<unsigned>(splits));
-    // 128-row tiles without a K split (the prefill's projections): one
-    // persistent CTA per SM.
+    // 128-row tiles without a K split (the prefill's projections): CTA pairs
+    // when N is a multiple of 192, else one persistent CTA per SM.
+    if (bm == 128 && splits == 1 && stages == 0 && !dependent && args.k_per_split == args.k && args.has_pair &&
+        args.n % kTcPairN == 0 && args.ldc % 4 == 0 && reinterpret_cast<uintptr_t>(args.c) % 16 == 0 &&
+        (args.residual == nullptr || reinterpret_cast<uintptr_t>(args.residual) % 16 == 0))
+        return launch_pair(args, stream);
     if (bm == 128 && splits == 1 && stages == 0 && !dependent && args.k_per_split == args.k)
         return launch_persistent(args, stream);
     if (stages == 0) stages = tc_default_stages(bm);
@@ -670,8 +1026,11 @@ fx_status tc_weights_create(const fx_model_desc& model, bool lm_head, TcModelWei
         w.cols = cols;
         fx_status st = tc_split(src, hi, lo, n, stream);
         if (st != FX_OK) return st;
-        if ((st = tc_encode_map(&w.hi, hi, rows, cols, kTcTileN, what)) != FX_OK) return st;
-        return tc_encode_map(&w.lo, lo, rows, cols, kTcTileN, what);
+        if ((st = tc_encode_map(&w.hi, hi, rows, cols, kTcTileN, what)) != FX_OK ||
+            (st = tc_encode_map(&w.lo, lo, rows, cols, kTcTileN, what)) != FX_OK ||
+            (st = tc_encode_map(&w.hi96, hi, rows, cols, kTcPairN / 2, what)) != FX_OK)
+            return st;
+        return tc_encode_map(&w.lo96, lo, rows, cols, kTcPairN / 2, what);
     };
     fx_status st;
     for (int l = 0; l < (layers ? kLayers : 0); ++l) {
@@ -707,6 +1066,9 @@ TcGemmArgs tc_args(const TcWeight& w, const CUtensorMap& x, float* c, const floa
     a.ldc = w.rows;
     a.k_per_split = k_per_split;
     a.split_stride = static_cast<long long>(m) * w.rows;
+    a.w_hi96 = w.hi96;
+    a.w_lo96 = w.lo96;
+    a.has_pair = true;
     return a;
 }
 
@@ -732,6 +1094,12 @@ extern "C" fx_status fx_linear_3xtf32_f32(const float* input, const float* weigh
     if ((st = tc_encode_map(&args.w_hi, weight_hi, n, k, kTcTileN, "weight_hi")) != FX_OK) return st;
     if ((st = tc_encode_map(&args.w_lo, weight_lo, n, k, kTcTileN, "weight_lo")) != FX_OK) return st;
     if ((st = tc_encode_map(&args.x, input, m, k, bm, "input")) != FX_OK) return st;
+    if (bm == 128 && n % kTcPairN == 0) {
+        if ((st = tc_encode_map(&args.w_hi96, weight_hi, n, k, kTcPairN / 2, "weight_hi")) != FX_OK ||
+            (st = tc_encode_map(&args.w_lo96, weight_lo, n, k, kTcPairN / 2, "weight_lo")) != FX_OK)
+            return st;
+        args.has_pair = true;
+    }
     args.c = output;
     args.residual = residual;
     args.error = error;

@@ -17,6 +17,7 @@ namespace fx {
 
 constexpr int kTcTileN = 128;  // weight rows per CTA (the MMA's M)
 constexpr int kTcTileK = 32;   // K columns per stage: one 128-byte swizzle row
+constexpr int kTcPairN = 192;  // weight rows per CTA pair in the paired form (96 per CTA)
 
 // C[m][n] (+ R[m][n]) = sum_k X[m][k] W[n][k] over k in split blockIdx.z's
 // slice; C points at split 0 and later splits follow at `split_stride`.
@@ -24,6 +25,10 @@ struct alignas(64) TcGemmArgs {
     CUtensorMap w_hi;  // [N][K], box 32 x 128, 128-byte swizzle
     CUtensorMap w_lo;
     CUtensorMap x;     // [M][K], box 32 x BM, 128-byte swizzle
+    // W with boxes of 96 rows, for the paired form (128-row X tiles, no K
+    // split, N a multiple of 192); `has_pair` says they are set.
+    CUtensorMap w_hi96, w_lo96;
+    bool has_pair;
     float* c;
     const float* residual;  // null, or [M][ldc] added in the epilogue
     int* error;             // bit 8: a wait gave up
@@ -47,9 +52,10 @@ fx_status tc_split(const float* w, float* hi, float* lo, size_t n, cudaStream_t 
 fx_status launch_tc_gemm(const TcGemmArgs& args, int bm, int splits, cudaStream_t stream, bool dependent,
                          int stages = 0);
 
-// The hi / lo halves of one projection weight and their tensor maps.
+// The hi / lo halves of one projection weight and their tensor maps (boxes
+// of 128 rows, and of 96 rows for the paired form).
 struct TcWeight {
-    CUtensorMap hi, lo;
+    CUtensorMap hi, lo, hi96, lo96;
     int rows = 0, cols = 0;
 };
 

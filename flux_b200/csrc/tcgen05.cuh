@@ -189,6 +189,84 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, ui
         : "memory");
 }
 
+// ---- CTA pairs (a cluster of two; rank 0 issues the pair's MMAs) --------
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Every thread of both CTAs; orders barrier initialisation and the end of
+// the pair's work across the two CTAs.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on the mbarrier at the same shared-memory offset in CTA `rank` of
+// the cluster (release at cluster scope).
+__device__ __forceinline__ void bar_arrive_rank(uint64_t* bar, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(bar)), "r"(rank));
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+
+__device__ __forceinline__ bool bar_test_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait with cluster-scope acquire, for barriers the peer CTA arrives on.
+__device__ inline bool bar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort, int* error) {
+    if (bar_test_cluster(bar, parity)) return true;
+    const unsigned long long t0 = now_ns();
+    while (!bar_test_cluster(bar, parity)) {
+        if (*abort) return false;
+        if (now_ns() - t0 > kTcWaitNs) {
+            *abort = 1;
+            atomicOr(error, 256);
+            return false;
+        }
+    }
+    return true;
+}
+
+// One MMA over both CTAs of the pair: A rows [0, M/2) from this CTA's shared
+// memory and [M/2, M) from the peer's at the same offsets, B likewise split
+// by its N rows, D in each CTA's TMEM (its M/2 lanes x N columns).
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrives on the mbarrier at this offset in both CTAs once the pair's MMAs
+// issued so far are done.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_addr(bar)),
+        "h"(static_cast<uint16_t>(3))
+        : "memory");
+}
+
+// Instruction descriptor for the pair: FP32 accumulate, TF32 A and B, both
+// K-major, M = 256, N = n.
+__host__ __device__ constexpr uint32_t tf32_idesc_pair(int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | (256u >> 4 << 24);
+}
+
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)), "r"(cols)
                  : "memory");

@@ -54,7 +54,10 @@ def test_split_is_exact_tf32_pair():
 
 
 @pytest.mark.parametrize("m,k,n", [(1, 576, 960), (64, 576, 576), (5, 1536, 576), (37, 576, 3072),
-                                   (64, 576, 49152), (300, 576, 960), (1000, 1536, 576), (4096, 576, 3072)])
+                                   (64, 576, 49152), (300, 576, 960), (1000, 1536, 576), (4096, 576, 3072),
+                                   # CTA pairs (N a multiple of 192) at the prefill's size, one weight block,
+                                   # and the persistent single-CTA form (N not a multiple of 192)
+                                   (8192, 576, 576), (1000, 576, 192), (300, 576, 1000)])
 def test_linear_3xtf32_matches_fp32(m, k, n):
     g = torch.Generator().manual_seed(m * 7 + n)
     x = torch.randn(m, k, generator=g).cuda()
