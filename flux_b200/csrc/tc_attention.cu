@@ -65,8 +65,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
     uint64_t* k_full = bars + 1;
     uint64_t* k_empty = k_full + kKStages;
     uint64_t* v_full = k_empty + kKStages;
-    uint64_t* v_empty = v_full + kVStages;
-    uint64_t* s_full = v_empty + kVStages;
+    uint64_t* s_full = v_full + kVStages;
     uint64_t* p_full = s_full + 2;
     uint64_t* o_full = p_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
@@ -86,10 +85,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
             bar_init(&k_full[s], 1);
             bar_init(&k_empty[s], 1);
         }
-        for (int s = 0; s < kVStages; ++s) {
-            bar_init(&v_full[s], 1);
-            bar_init(&v_empty[s], 1);
-        }
+        for (int s = 0; s < kVStages; ++s) bar_init(&v_full[s], 1);
         for (int x = 0; x < 2; ++x) {
             bar_init(&s_full[x], 1);
             bar_init(&p_full[x], 128);
@@ -106,12 +102,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
 
     // One producer lane per ring: warp 0 loads Q and the K tiles, warp 9 the
     // V^T tiles.
-    auto produce = [&](int stages, uint64_t* full, uint64_t* empty, auto&& load) {
+    // `freed(t)` waits until the stage of tile t - stages may be refilled.
+    auto produce = [&](int stages, uint64_t* full, auto&& freed, auto&& load) {
         int issued = 0;
         for (int t = 0; t < nt; ++t) {
             const int s = t % stages;
-            if (t >= stages && !bar_wait(&empty[s], static_cast<uint32_t>(t / stages - 1) & 1u, abort, a.error))
-                break;
+            if (t >= stages && !freed(t)) break;
             bar_expect(&full[s], kHalfStage);
             load(t, s, &full[s]);
             issued = t + 1;
@@ -132,7 +128,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
             tma_box(qs + 1 * kQBox, &a.q_hi, 32, qy, q_full);
             tma_box(qs + 2 * kQBox, &a.q_lo, 0, qy, q_full);
             tma_box(qs + 3 * kQBox, &a.q_lo, 32, qy, q_full);
-            produce(kKStages, k_full, k_empty, [&](int t, int s, uint64_t* bar) {
+            auto k_freed = [&](int t) {
+                return bar_wait(&k_empty[t % kKStages], static_cast<uint32_t>(t / kKStages - 1) & 1u, abort, a.error);
+            };
+            produce(kKStages, k_full, k_freed, [&](int t, int s, uint64_t* bar) {
                 unsigned char* st = kstage(s);
                 const int ky = g * a.padded + t * kTcAttnKeys;
                 tma_box(st + 0 * kKBox, &a.k_hi, 0, ky, bar);
@@ -146,7 +145,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
         }
     } else if (warp == kAttnThreads / 32 - 1) {
         if (lane == 0) {
-            produce(kVStages, v_full, v_empty, [&](int t, int s, uint64_t* bar) {
+            // V^T stage t % 2 is free once the P V products of tile t - 2 are
+            // done: o_full[t % 2] of that tile (its next phase needs this very
+            // tile, so the parity cannot alias), one commit fewer per tile.
+            auto v_freed = [&](int t) {
+                return bar_wait(&o_full[t & 1], static_cast<uint32_t>((t - kVStages) >> 1) & 1u, abort, a.error);
+            };
+            produce(kVStages, v_full, v_freed, [&](int t, int s, uint64_t* bar) {
                 unsigned char* st = vstage(s);
                 const int vx = t * kTcAttnKeys;
                 tma_box(st + 0 * kKBox, &a.vt_hi, vx, g * kHeadDim, bar);
@@ -208,7 +213,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
                     mma_tf32_ts(o, ph + col, vh, idesc, 1u);
                 }
                 mma_commit(&o_full[x]);
-                mma_commit(&v_empty[s]);
             }
         }
         __syncwarp();

@@ -569,6 +569,11 @@ __global__ void __launch_bounds__(kPtThreads, 1) tc_gemm_persistent_kernel(const
 // The tensor core's accumulation truncates, so each group of 2 stages (8
 // hi.hi products) starts a fresh accumulator and is added in FP32 with
 // round-to-nearest, as in the other forms.
+// Below this many X rows the pairs' 256-row tiles are too few to fill the
+// GPU (a 128-token prompt: 16 pairs, half of each tile padding), so smaller
+// M takes the single-CTA forms.  Measured prefills (ms, pairs / per-tile):
+// 128 tokens 5.70 / 4.90, 1024: 6.96 / 6.81, 2048: 8.92 / 9.48.
+constexpr int kPairMinRows = 2048;
 constexpr int kPrThreads = 448;
 constexpr int kPrSplit = 128;
 constexpr int kPrEpiWarps = 8;
@@ -994,8 +999,10 @@ fx_status launch_tc_gemm(const TcGemmArgs& args, int bm, int splits, cudaStream_
     const dim3 grid(static_cast<unsigned>((args.n + kTcTileN - 1) / kTcTileN),
                     static_cast<unsigned>((args.m + bm - 1) / bm), static_cast<unsigned>(splits));
     // 128-row tiles without a K split (the prefill's projections): CTA pairs
-    // when N is a multiple of 192, else one persistent CTA per SM.
+    // when M fills them (at least kPairMinRows rows) and N is a multiple of
+    // 192, else one persistent CTA per SM.
     if (bm == 128 && splits == 1 && stages == 0 && !dependent && args.k_per_split == args.k && args.has_pair &&
+        args.m >= kPairMinRows &&
         args.n % kTcPairN == 0 && args.ldc % 4 == 0 && reinterpret_cast<uintptr_t>(args.c) % 16 == 0 &&
         (args.residual == nullptr || reinterpret_cast<uintptr_t>(args.residual) % 16 == 0))
         return launch_pair(args, stream);
