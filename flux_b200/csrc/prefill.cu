@@ -376,6 +376,9 @@ struct fx_prefill {
     fx::TcModelWeights tc;                  // split projection weights
     CUtensorMap x_norm, x_attn, x_swiglu;   // activation maps of the projections
     int bm = 128;                           // activation rows per tensor-core tile
+    // From kTcPairMinRows rows the gate/up projection runs on CTA pairs with
+    // SwiGLU in its epilogue (gate/up weights split in the fused row order).
+    bool fused_swiglu = false;
     // Tensor-core attention (unless FLUX_B200_PREFILL_ATTENTION=simt): split
     // q / K / V^T planes and their maps.
     bool tc_attention = true;
@@ -437,8 +440,17 @@ fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
         // residual = attn . Wo^T + in; norm = rmsnorm(residual)
         if ((st = project(p->tc.o[l], p->x_attn, p->residual, in)) != FX_OK) return st;
         if ((st = fx_rmsnorm_f32(p->residual, m.post_norm[l], p->norm, S, kHidden, m.epsilon, s)) != FX_OK) return st;
-        if ((st = project(p->tc.gate_up[l], p->x_norm, p->gate_up, nullptr)) != FX_OK) return st;
-        if ((st = fx_packed_swiglu_f32(p->gate_up, p->swiglu_out, S, kInter, s)) != FX_OK) return st;
+        if (p->fused_swiglu) {
+            TcGemmArgs a = tc_args(p->tc.gate_up[l], p->x_norm, nullptr, nullptr, error, static_cast<int>(S),
+                                   kHidden);
+            a.swiglu = true;
+            a.act = p->swiglu_out;
+            a.act_ld = kInter;
+            if ((st = launch_tc_gemm(a, p->bm, 1, s, false)) != FX_OK) return st;
+        } else {
+            if ((st = project(p->tc.gate_up[l], p->x_norm, p->gate_up, nullptr)) != FX_OK) return st;
+            if ((st = fx_packed_swiglu_f32(p->gate_up, p->swiglu_out, S, kInter, s)) != FX_OK) return st;
+        }
         if ((st = project(p->tc.down[l], p->x_swiglu, out, p->residual)) != FX_OK) return st;
     }
     const float* last = p->h_a + (S - 1) * kHidden;  // 30 layers end in h_a
@@ -488,7 +500,8 @@ fx_status prefill_create_impl(fx_prefill* p, const int64_t* ids, cudaStream_t s)
         cursor += (counts[i] + 63) / 64 * 64;
     }
     FX_CUDA_TRY(cudaMemsetAsync(p->buffer, 0, p->buffer_bytes, s), "clearing the prefill workspace");
-    fx_status st0 = tc_weights_create(p->model, false, &p->tc, s);
+    p->fused_swiglu = p->bm == 128 && S >= kTcPairMinRows;
+    fx_status st0 = tc_weights_create(p->model, false, &p->tc, s, true, p->fused_swiglu);
     if (st0 != FX_OK) return st0;
     const char* attention_mode = std::getenv("FLUX_B200_PREFILL_ATTENTION");
     p->tc_attention = !(attention_mode != nullptr && std::strcmp(attention_mode, "simt") == 0);

@@ -565,15 +565,12 @@ __global__ void __launch_bounds__(kPtThreads, 1) tc_gemm_persistent_kernel(const
 //   warps 6-13      add each group into FP32 registers (warp w: TMEM lane
 //                   quarter w % 4, 96 of the 192 columns), release the group
 //                   on the leader's acc_empty, and after a tile's last group
-//                   store its rows (float4 stores, + residual).
+//                   store its rows (float4 stores, + residual), or with the
+//                   fused SwiGLU silu(gate) * up of its 48 gate / up column
+//                   pairs.
 // The tensor core's accumulation truncates, so each group of 2 stages (8
 // hi.hi products) starts a fresh accumulator and is added in FP32 with
 // round-to-nearest, as in the other forms.
-// Below this many X rows the pairs' 256-row tiles are too few to fill the
-// GPU (a 128-token prompt: 16 pairs, half of each tile padding), so smaller
-// M takes the single-CTA forms.  Measured prefills (ms, pairs / per-tile):
-// 128 tokens 5.70 / 4.90, 1024: 6.96 / 6.81, 2048: 8.92 / 9.48.
-constexpr int kPairMinRows = 2048;
 constexpr int kPrThreads = 448;
 constexpr int kPrSplit = 128;
 constexpr int kPrEpiWarps = 8;
@@ -824,7 +821,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPrThreads, 1)
                 break;
             }
             const int m = tile_m0(u) + quarter * 32 + lane, n0 = tile_n0(u) + c0;
-            if (m < a.m) {
+            if (a.swiglu) {
+                // columns [0, 48) are gates and [48, 96) their ups: features
+                // (tile_n0 + c0) / 2 + [0, 48)
+                if (m < a.m) {
+                    float* arow = a.act + static_cast<long long>(m) * a.act_ld + n0 / 2;
+#pragma unroll
+                    for (int q = 0; q < kTcPairN / 4; q += 4)
+                        *reinterpret_cast<float4*>(arow + q) =
+                            make_float4(swiglu(acc[q], acc[kTcPairN / 4 + q]), swiglu(acc[q + 1], acc[kTcPairN / 4 + q + 1]),
+                                        swiglu(acc[q + 2], acc[kTcPairN / 4 + q + 2]),
+                                        swiglu(acc[q + 3], acc[kTcPairN / 4 + q + 3]));
+                }
+            } else if (m < a.m) {
                 float* crow = a.c + static_cast<long long>(m) * a.ldc + n0;
                 const float* rrow = a.residual != nullptr ? a.residual + static_cast<long long>(m) * a.ldc + n0 : nullptr;
 #pragma unroll
@@ -868,6 +877,34 @@ __global__ void tf32_split_kernel(const float4* __restrict__ w, float4* __restri
         r.w = tf32_rna(v.w - h.w);
         hi[i] = h;
         lo[i] = r;
+    }
+}
+
+// The packed gate/up weight split with its rows in the fused-SwiGLU order:
+// destination row r of block b = r / 192, c = r % 192 takes feature
+// f = 96 b + 48 (c / 96) + c % 48, its gate row f when c % 96 < 48, else its
+// up row inter + f.
+__global__ void tf32_split_swiglu_rows_kernel(const float4* __restrict__ w, float4* __restrict__ hi,
+                                              float4* __restrict__ lo, int rows, int cols4, int inter) {
+    const size_t n4 = static_cast<size_t>(rows) * cols4;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int r = static_cast<int>(i / cols4), col = static_cast<int>(i % cols4);
+        const int b = r / kTcPairN, c = r % kTcPairN;
+        const int f = (kTcPairN / 2) * b + (kTcPairN / 4) * (c / (kTcPairN / 2)) + c % (kTcPairN / 4);
+        const int src = c % (kTcPairN / 2) < kTcPairN / 4 ? f : inter + f;
+        const float4 v = w[static_cast<size_t>(src) * cols4 + col];
+        float4 h, l;
+        h.x = tf32_rna(v.x);
+        h.y = tf32_rna(v.y);
+        h.z = tf32_rna(v.z);
+        h.w = tf32_rna(v.w);
+        l.x = tf32_rna(v.x - h.x);
+        l.y = tf32_rna(v.y - h.y);
+        l.z = tf32_rna(v.z - h.z);
+        l.w = tf32_rna(v.w - h.w);
+        hi[i] = h;
+        lo[i] = l;
     }
 }
 
@@ -999,13 +1036,18 @@ fx_status launch_tc_gemm(const TcGemmArgs& args, int bm, int splits, cudaStream_
     const dim3 grid(static_cast<unsigned>((args.n + kTcTileN - 1) / kTcTileN),
                     static_cast<unsigned>((args.m + bm - 1) / bm), static_cast<unsigned>(splits));
     // 128-row tiles without a K split (the prefill's projections): CTA pairs
-    // when M fills them (at least kPairMinRows rows) and N is a multiple of
+    // when M fills them (at least kTcPairMinRows rows) and N is a multiple of
     // 192, else one persistent CTA per SM.
     if (bm == 128 && splits == 1 && stages == 0 && !dependent && args.k_per_split == args.k && args.has_pair &&
-        args.m >= kPairMinRows &&
+        args.m >= kTcPairMinRows &&
         args.n % kTcPairN == 0 && args.ldc % 4 == 0 && reinterpret_cast<uintptr_t>(args.c) % 16 == 0 &&
-        (args.residual == nullptr || reinterpret_cast<uintptr_t>(args.residual) % 16 == 0))
+        (args.residual == nullptr || reinterpret_cast<uintptr_t>(args.residual) % 16 == 0) &&
+        (!args.swiglu || (args.act != nullptr && args.act_ld % 4 == 0 && reinterpret_cast<uintptr_t>(args.act) % 16 == 0)))
         return launch_pair(args, stream);
+    if (args.swiglu) {
+        set_error("tensor-core GEMM: the fused SwiGLU runs only in the paired form (M >= 2048, N % 192 == 0, bm 128)");
+        return FX_ERR_INVALID;
+    }
     if (bm == 128 && splits == 1 && stages == 0 && !dependent && args.k_per_split == args.k)
         return launch_persistent(args, stream);
     if (stages == 0) stages = tc_default_stages(bm);
@@ -1017,21 +1059,35 @@ fx_status launch_tc_gemm(const TcGemmArgs& args, int bm, int splits, cudaStream_
 }
 
 fx_status tc_weights_create(const fx_model_desc& model, bool lm_head, TcModelWeights* out, cudaStream_t stream,
-                            bool layers) {
+                            bool layers, bool swiglu_rows) {
+    static_assert(kInter % (kTcPairN / 2) == 0, "the gate/up features fill whole 192-row blocks");
     const size_t per_layer =
         layers ? static_cast<size_t>(kQKV + kHidden + kGateUp) * kHidden + static_cast<size_t>(kHidden) * kInter : 0;
     const size_t lm = lm_head ? static_cast<size_t>(model.vocab) * kHidden : 0;
     const size_t total = 2 * (per_layer * kLayers + lm);
     FX_CUDA_TRY(cudaMalloc(&out->buffer, total * sizeof(float)), "allocating the split projection weights");
     float* cursor = out->buffer;
-    auto make = [&](TcWeight& w, const float* src, int rows, int cols, const char* what) -> fx_status {
+    auto make = [&](TcWeight& w, const float* src, int rows, int cols, const char* what,
+                    bool reorder = false) -> fx_status {
         const size_t n = static_cast<size_t>(rows) * cols;
         float* hi = cursor;
         float* lo = cursor + n;
         cursor += 2 * n;
         w.rows = rows;
         w.cols = cols;
-        fx_status st = tc_split(src, hi, lo, n, stream);
+        fx_status st = FX_OK;
+        if (reorder) {
+            FX_REQUIRE(reinterpret_cast<uintptr_t>(src) % 16 == 0 && cols % 4 == 0,
+                       "tf32 split: the gate/up weight must be 16-byte aligned rows of a multiple of 4 floats");
+            const size_t n4 = n / 4;
+            const unsigned blocks = static_cast<unsigned>(std::min<size_t>((n4 + 255) / 256, 148 * 16));
+            tf32_split_swiglu_rows_kernel<<<blocks, 256, 0, stream>>>(
+                reinterpret_cast<const float4*>(src), reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lo),
+                rows, cols / 4, kInter);
+            FX_CUDA_TRY(cudaGetLastError(), "launching the reordered tf32 split");
+        } else {
+            st = tc_split(src, hi, lo, n, stream);
+        }
         if (st != FX_OK) return st;
         if ((st = tc_encode_map(&w.hi, hi, rows, cols, kTcTileN, what)) != FX_OK ||
             (st = tc_encode_map(&w.lo, lo, rows, cols, kTcTileN, what)) != FX_OK ||
@@ -1043,7 +1099,8 @@ fx_status tc_weights_create(const fx_model_desc& model, bool lm_head, TcModelWei
     for (int l = 0; l < (layers ? kLayers : 0); ++l) {
         if ((st = make(out->qkv[l], model.packed_qkv[l], kQKV, kHidden, "packed_qkv")) != FX_OK) return st;
         if ((st = make(out->o[l], model.o_proj[l], kHidden, kHidden, "o_proj")) != FX_OK) return st;
-        if ((st = make(out->gate_up[l], model.gate_up[l], kGateUp, kHidden, "gate_up")) != FX_OK) return st;
+        if ((st = make(out->gate_up[l], model.gate_up[l], kGateUp, kHidden, "gate_up", swiglu_rows)) != FX_OK)
+            return st;
         if ((st = make(out->down[l], model.down[l], kHidden, kInter, "down")) != FX_OK) return st;
     }
     out->has_lm_head = lm_head;

@@ -18,6 +18,11 @@ namespace fx {
 constexpr int kTcTileN = 128;  // weight rows per CTA (the MMA's M)
 constexpr int kTcTileK = 32;   // K columns per stage: one 128-byte swizzle row
 constexpr int kTcPairN = 192;  // weight rows per CTA pair in the paired form (96 per CTA)
+// The paired form runs from this many X rows; below it the pairs' 256-row
+// tiles are too few to fill the GPU (a 128-token prompt: 16 pairs, half of
+// each tile padding).  Measured prefills (ms, pairs / per-tile): 128 tokens
+// 5.70 / 4.90, 1024: 6.96 / 6.81, 2048: 8.92 / 9.48.
+constexpr int kTcPairMinRows = 2048;
 
 // C[m][n] (+ R[m][n]) = sum_k X[m][k] W[n][k] over k in split blockIdx.z's
 // slice; C points at split 0 and later splits follow at `split_stride`.
@@ -29,6 +34,12 @@ struct alignas(64) TcGemmArgs {
     // split, N a multiple of 192); `has_pair` says they are set.
     CUtensorMap w_hi96, w_lo96;
     bool has_pair;
+    // Fused SwiGLU (paired form only): W is the packed gate/up weight split
+    // with rows in the order tc_weights_create(..., swiglu_rows) gives, and
+    // act[m][f] = silu(gate) * up is written instead of C (row stride act_ld).
+    bool swiglu;
+    float* act;
+    int act_ld;
     float* c;
     const float* residual;  // null, or [M][ldc] added in the epilogue
     int* error;             // bit 8: a wait gave up
@@ -69,9 +80,12 @@ struct TcModelWeights {
 };
 
 // `layers` false: the LM head only (the persistent batched layers multiply
-// FP32 weights on the SIMT cores).
+// FP32 weights on the SIMT cores).  `swiglu_rows`: the packed gate/up
+// weights are split with their rows reordered for the paired form's fused
+// SwiGLU -- in each block of 192 rows, features 96 b + 48 h + [0, 48) as 48
+// gate rows then their 48 up rows (h = 0, 1) -- and serve only that form.
 fx_status tc_weights_create(const fx_model_desc& model, bool lm_head, TcModelWeights* out, cudaStream_t stream,
-                            bool layers = true);
+                            bool layers = true, bool swiglu_rows = false);
 void tc_weights_release(TcModelWeights* w);
 
 // Arguments of C = X . W^T (+ residual) with K split in `k_per_split` slices.
