@@ -129,6 +129,45 @@ __global__ void gemm_nt_simple_kernel(const float* __restrict__ A, const float* 
     C[t] = R != nullptr ? acc + R[t] : acc;
 }
 
+// The prefill's RMSNorm: one warp per row of kHidden floats (float4 loads,
+// shuffle reduction), out = v * rsqrt(mean(v^2) + eps) * w.  The op-level
+// kernel (ops.cu) keeps the reference's summation order with a block per
+// row; the prefill, whose products are 3xTF32 anyway, only needs FP32
+// accuracy, and a block per 576-float row reached ~1.5 TB/s.
+constexpr int kNormRowsPerBlock = 8;
+__global__ void __launch_bounds__(32 * kNormRowsPerBlock) prefill_rmsnorm_kernel(const float* __restrict__ in,
+                                                                                const float* __restrict__ weight,
+                                                                                float* __restrict__ out, int64_t rows,
+                                                                                float eps) {
+    constexpr int kVec = kHidden / 4;                   // 144 float4 per row
+    constexpr int kPer = (kVec + 31) / 32;              // 5 per lane (the last partly)
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * kNormRowsPerBlock + threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    if (row >= rows) return;
+    const float4* x = reinterpret_cast<const float4*>(in + row * kHidden);
+    float4 v[kPer];
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int i = lane + 32 * j;
+        v[j] = i < kVec ? x[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float inv = rsqrtf(ss / static_cast<float>(kHidden) + eps);
+    const float4* w = reinterpret_cast<const float4*>(weight);
+    float4* y = reinterpret_cast<float4*>(out + row * kHidden);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int i = lane + 32 * j;
+        if (i < kVec) {
+            const float4 g = w[i];
+            y[i] = make_float4(v[j].x * inv * g.x, v[j].y * inv * g.y, v[j].z * inv * g.z, v[j].w * inv * g.w);
+        }
+    }
+}
+
 __global__ void embedding_gather_kernel(const int64_t* __restrict__ ids, const float* __restrict__ embedding,
                                         float* __restrict__ out, int64_t rows, int64_t vocab) {
     const int64_t total = rows * kHidden;
@@ -163,15 +202,28 @@ struct PrefillSplit {
     int64_t padded;
 };
 
-__global__ void prefill_rope_cache_kernel(const float* __restrict__ packed, const float* __restrict__ cos,
-                                          const float* __restrict__ sin, float* __restrict__ q,
-                                          float* __restrict__ key_cache, float* __restrict__ value_cache,
-                                          int64_t rows, int64_t capacity, PrefillSplit split) {
-    const int64_t total = rows * kQKV;
-    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
-         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t r = t / kQKV;
-        const int col = static_cast<int>(t % kQKV);
+// One block per kRopeRows rows x one chunk of three heads (blockIdx.y: q
+// heads 0-2, 3-5, 6-8, k heads, v heads): every store is coalesced along the
+// columns, and the V^T planes (one row per value column) go through a
+// shared-memory tile so that each of their rows is written as kRopeRows
+// consecutive floats (a store per element at a stride of `padded` floats
+// took ~2x the kernel's traffic time).
+constexpr int kRopeRows = 16;
+constexpr int kRopeChunk = kKVHeads * kHeadDim;  // 192 columns
+static_assert(kQKV == 5 * kRopeChunk, "packed QKV is five chunks of three heads");
+__global__ void __launch_bounds__(256) prefill_rope_cache_kernel(const float* __restrict__ packed,
+                                                                 const float* __restrict__ cos,
+                                                                 const float* __restrict__ sin, float* __restrict__ q,
+                                                                 float* __restrict__ key_cache,
+                                                                 float* __restrict__ value_cache, int64_t rows,
+                                                                 int64_t capacity, PrefillSplit split) {
+    __shared__ float vt_tile[kKVHeads * kHeadDim][kRopeRows + 1];
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kRopeRows;
+    const int nrows = static_cast<int>(min(static_cast<int64_t>(kRopeRows), rows - r0));
+    const int chunk = static_cast<int>(blockIdx.y);
+    for (int e = threadIdx.x; e < nrows * kRopeChunk; e += blockDim.x) {
+        const int rr = e / kRopeChunk, col = chunk * kRopeChunk + e % kRopeChunk;
+        const int64_t r = r0 + rr;
         const float* prow = packed + r * kQKV;
         if (col < kHidden + kKVHeads * kHeadDim) {
             const int base = (col / kHeadDim) * kHeadDim, d = col % kHeadDim;
@@ -191,8 +243,15 @@ __global__ void prefill_rope_cache_kernel(const float* __restrict__ packed, cons
         } else {
             const int u = col - kHidden - kKVHeads * kHeadDim;
             value_cache[(static_cast<int64_t>(u / kHeadDim) * capacity + r) * kHeadDim + u % kHeadDim] = prow[col];
-            if (split.vt_hi != nullptr)
-                store_split(split.vt_hi, split.vt_lo, static_cast<size_t>(u) * split.padded + r, prow[col]);
+            vt_tile[u][rr] = prow[col];
+        }
+    }
+    if (split.vt_hi != nullptr && chunk == 4) {  // uniform over the block
+        __syncthreads();
+        for (int e = threadIdx.x; e < kKVHeads * kHeadDim * kRopeRows; e += blockDim.x) {
+            const int u = e / kRopeRows, rr = e % kRopeRows;
+            if (rr < nrows) store_split(split.vt_hi, split.vt_lo, static_cast<size_t>(u) * split.padded + r0 + rr,
+                                        vt_tile[u][rr]);
         }
     }
 }
@@ -407,6 +466,14 @@ fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
     auto project = [&](const TcWeight& w, const CUtensorMap& x, float* c, const float* residual) {
         return launch_tc_gemm(tc_args(w, x, c, residual, error, static_cast<int>(S), w.cols), p->bm, 1, s, false);
     };
+    auto prefill_norm = [&](const float* in, const float* weight) -> fx_status {
+        if (reinterpret_cast<uintptr_t>(in) % 16 != 0 || reinterpret_cast<uintptr_t>(weight) % 16 != 0)
+            return fx_rmsnorm_f32(in, weight, p->norm, S, kHidden, m.epsilon, s);  // float4 loads need 16 bytes
+        prefill_rmsnorm_kernel<<<static_cast<unsigned>((S + kNormRowsPerBlock - 1) / kNormRowsPerBlock),
+                                 32 * kNormRowsPerBlock, 0, s>>>(in, weight, p->norm, S, m.epsilon);
+        FX_CUDA_TRY(cudaGetLastError(), "launching the prefill RMSNorm");
+        return FX_OK;
+    };
     const size_t layer_stride = static_cast<size_t>(kKVHeads) * cap * kHeadDim;
     embedding_gather_kernel<<<blocks_for(S * kHidden), 256, 0, s>>>(ids, m.embedding, p->h_a, S, m.vocab);
     FX_CUDA_TRY(cudaGetLastError(), "launching embedding gather");
@@ -415,7 +482,7 @@ fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
         float* out = l % 2 == 0 ? p->h_b : p->h_a;
         float* kc = db.key_cache + l * layer_stride;
         float* vc = db.value_cache + l * layer_stride;
-        if ((st = fx_rmsnorm_f32(in, m.input_norm[l], p->norm, S, kHidden, m.epsilon, s)) != FX_OK) return st;
+        if ((st = prefill_norm(in, m.input_norm[l])) != FX_OK) return st;
         if ((st = project(p->tc.qkv[l], p->x_norm, p->qkv, nullptr)) != FX_OK) return st;
         PrefillSplit split{};
         if (p->tc_attention) {
@@ -425,8 +492,8 @@ fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
                      b + 2 * S * kHidden + 2 * kKVHeads * P * kHeadDim,
                      b + 2 * S * kHidden + 3 * kKVHeads * P * kHeadDim, P};
         }
-        prefill_rope_cache_kernel<<<blocks_for(S * kQKV), 256, 0, s>>>(p->qkv, m.rope_cos, m.rope_sin, p->q, kc, vc,
-                                                                       S, cap, split);
+        prefill_rope_cache_kernel<<<dim3(static_cast<unsigned>((S + kRopeRows - 1) / kRopeRows), 5), 256, 0, s>>>(
+            p->qkv, m.rope_cos, m.rope_sin, p->q, kc, vc, S, cap, split);
         FX_CUDA_TRY(cudaGetLastError(), "launching prefill RoPE/cache fill");
         if (p->tc_attention) {
             TcAttentionArgs args = p->attn_args;
@@ -439,7 +506,7 @@ fx_status prefill_run(fx_prefill* p, const int64_t* ids, cudaStream_t s) {
         }
         // residual = attn . Wo^T + in; norm = rmsnorm(residual)
         if ((st = project(p->tc.o[l], p->x_attn, p->residual, in)) != FX_OK) return st;
-        if ((st = fx_rmsnorm_f32(p->residual, m.post_norm[l], p->norm, S, kHidden, m.epsilon, s)) != FX_OK) return st;
+        if ((st = prefill_norm(p->residual, m.post_norm[l])) != FX_OK) return st;
         if (p->fused_swiglu) {
             TcGemmArgs a = tc_args(p->tc.gate_up[l], p->x_norm, nullptr, nullptr, error, static_cast<int>(S),
                                    kHidden);
