@@ -3,9 +3,12 @@
 // One CTA per (128 queries, q head); key tiles of 64 rows up to the causal
 // limit.  Q, K and V^T arrive already split into TF32 hi / lo planes (the
 // RoPE / cache-fill kernel writes them), so no operand is converted here.
-// 320 threads:
+// 352 threads:
 //   warp 0, lane 0   TMA: Q (hi, lo; two 32-column boxes each) once, then per
-//                    key tile K (hi, lo) and V^T (hi, lo) into a 2-stage ring;
+//                    key tile K (hi, lo) into a 2-stage ring, a stage freed
+//                    by the commit of that tile's scores (s_full);
+//   warp 10, lane 0  TMA: V^T (hi, lo) per key tile into a 2-stage ring, a
+//                    stage freed by the commit of that tile's P V (o_full);
 //   warp 1           owns TMEM (512 columns); lane 0 issues the MMAs:
 //                    S = Q K^T as two accumulators (head dims 0-31 and 32-63,
 //                    12 MMAs each: Qhi.Klo + Qlo.Khi + Qhi.Khi per K step),
@@ -36,7 +39,7 @@ namespace {
 using namespace tc;
 
 constexpr int kAttnThreads = 352;  // K producer, MMA, 8 softmax warps, V producer
-constexpr int kKStages = 3;         // K is free once the scores are done ...
+constexpr int kKStages = 2;         // K is free once the scores are done ...
 constexpr int kVStages = 2;         // ... V^T only after P V
 constexpr uint32_t kQBox = kTcAttnQ * 128;              // 128 rows x 32 floats (16 KB)
 constexpr uint32_t kKBox = kTcAttnKeys * 128;           // 64 rows x 32 floats (8 KB)
@@ -63,8 +66,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kQBytes + kRingBytes);
     uint64_t* q_full = bars;
     uint64_t* k_full = bars + 1;
-    uint64_t* k_empty = k_full + kKStages;
-    uint64_t* v_full = k_empty + kKStages;
+    uint64_t* v_full = k_full + kKStages;
     uint64_t* s_full = v_full + kVStages;
     uint64_t* p_full = s_full + 2;
     uint64_t* o_full = p_full + 2;
@@ -83,7 +85,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
         bar_init(q_full, 1);
         for (int s = 0; s < kKStages; ++s) {
             bar_init(&k_full[s], 1);
-            bar_init(&k_empty[s], 1);
         }
         for (int s = 0; s < kVStages; ++s) bar_init(&v_full[s], 1);
         for (int x = 0; x < 2; ++x) {
@@ -129,7 +130,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
             tma_box(qs + 2 * kQBox, &a.q_lo, 0, qy, q_full);
             tma_box(qs + 3 * kQBox, &a.q_lo, 32, qy, q_full);
             auto k_freed = [&](int t) {
-                return bar_wait(&k_empty[t % kKStages], static_cast<uint32_t>(t / kKStages - 1) & 1u, abort, a.error);
+                // K stage t % 2 is free once the scores of tile t - 2 are
+                // done: s_full[t % 2] of that tile (its next phase needs this
+                // very tile, so the parity cannot alias).
+                return bar_wait(&s_full[t & 1], static_cast<uint32_t>((t - kKStages) >> 1) & 1u, abort, a.error);
             };
             produce(kKStages, k_full, k_freed, [&](int t, int s, uint64_t* bar) {
                 unsigned char* st = kstage(s);
@@ -188,7 +192,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tc_prefill_attention_kernel(c
                     }
                 }
                 mma_commit(&s_full[x]);
-                mma_commit(&k_empty[s]);
                 return true;
             };
             ok = ok && nt > 0 && issue_scores(0);
