@@ -171,7 +171,10 @@ FX_API fx_status fx_tf32_split_f32(const float* input, float* hi, float* lo, int
  * accumulation; K % 32 == 0, 16-byte aligned rows.  `error` is a device int
  * that gets bit 8 if an internal wait gave up (never expected).  Same
  * contract as fx_linear_f32 (csrc/cublaslt_linear/cublaslt_linear_cuda.h:20-33),
- * used by the batched and prefill projections. */
+ * used by the batched and prefill projections.  M <= 64: one CTA per
+ * 128 x 64 tile; M >= 2048 with N % 192 == 0: persistent CTA pairs (a
+ * cluster launch of tcgen05 cta_group::2 MMAs); otherwise one persistent CTA
+ * per SM over 128 x 128 tiles. */
 FX_API fx_status fx_linear_3xtf32_f32(const float* input, const float* weight_hi, const float* weight_lo,
                                const float* residual, float* output, int64_t m, int64_t k, int64_t n,
                                int* error, void* stream);
