@@ -539,11 +539,12 @@ __global__ void __launch_bounds__(kPtThreads, 1) tc_gemm_persistent_kernel(const
 // no K split): a cluster of two CTAs on two SMs walks tiles of 256 X rows x
 // 192 W rows, t = pair + u * pairs (W block fastest).  The pair's MMAs
 // (tcgen05 cta_group::2, M = 256, N = 192) take A = X (128 rows from each
-// CTA) and B = W (96 rows from each), so one instruction does twice the
-// per-SM work of a 128 x 128 MMA for the same issue, wait and commit cost on
-// the MMA thread -- those cost ~110-170 cycles each and do not overlap the
-// queued MMAs.  D in each CTA's TMEM: its 128 X rows x the 192 outputs.
-// 384 threads per CTA:
+// CTA) and B = W (96 rows from each), so one instruction does 1.5 times the
+// per-SM work of a 128 x 128 MMA (128 x 192 on each SM) while each CTA
+// stages only 96 W rows, for the same issue, wait and commit cost on the MMA
+// thread -- those cost ~110-170 cycles each and do not overlap the queued
+// MMAs.  D in each CTA's TMEM: its 128 X rows x the 192 outputs.
+// 448 threads per CTA:
 //   warp 0, lane 0  TMA producer (each CTA): per 32-column stage the CTA's
 //                   raw X box (32 x 128) and W_hi / W_lo boxes (32 x 96)
 //                   into a 4-stage ring, refilled when the leader's commit
