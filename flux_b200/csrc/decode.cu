@@ -516,7 +516,10 @@ struct fx_decode {
     cudaEvent_t done = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
-    int64_t* host_io = nullptr;   // page-locked [0] token in, [1] token out (fx_decode_replay_host)
+    int64_t* host_io = nullptr;   // page-locked, mapped [0] token in, [1] token out (fx_decode_replay_host)
+    int64_t* host_io_dev = nullptr;  // the same words as the device sees them
+    cudaGraph_t graph_host = nullptr;      // persistent step: the step also writing host_io[1]
+    cudaGraphExec_t exec_host = nullptr;
     // owned device memory
     int64_t* state = nullptr;     // token, position, length, step, generated[capacity]
     float* logits = nullptr;
@@ -649,10 +652,11 @@ fx_status initialize_state(fx_decode* r, const int64_t* token, const float* cons
 }
 
 // Enqueue one decode step on `stream`: one cooperative launch, or 151 kernels.
-fx_status run_body(fx_decode* r, cudaStream_t stream) {
+fx_status run_body(fx_decode* r, cudaStream_t stream, bool host_io = false) {
     const fx_model_desc& m = r->model;
     if (r->persistent) {
         StepArgs a{};
+        if (host_io) a.host_out = r->host_io_dev + 1;
         for (int l = 0; l < kLayers; ++l) a.layer[l] = r->step_layers[l];
         a.embedding = m.embedding;
         a.final_norm = m.final_norm;
@@ -749,6 +753,8 @@ void release(fx_decode* r) {
     }
     if (r->pending && r->done != nullptr) cudaEventSynchronize(r->done);
     if (r->exec) cudaGraphExecDestroy(r->exec);
+    if (r->exec_host) cudaGraphExecDestroy(r->exec_host);
+    if (r->graph_host) cudaGraphDestroy(r->graph_host);
     if (r->graph) cudaGraphDestroy(r->graph);
     if (r->done) cudaEventDestroy(r->done);
     if (r->capture_stream) {
@@ -818,8 +824,10 @@ fx_status create_impl(fx_decode* r, const int64_t* token, const float* const* ks
     if (st != FX_OK) return st;
     FX_CUDA_TRY(cudaStreamCreateWithFlags(&r->capture_stream, cudaStreamNonBlocking), "creating capture stream");
     FX_CUDA_TRY(cudaEventCreateWithFlags(&r->done, cudaEventDisableTiming), "creating completion event");
-    FX_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&r->host_io), 2 * sizeof(int64_t), cudaHostAllocDefault),
+    FX_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&r->host_io), 2 * sizeof(int64_t), cudaHostAllocMapped),
                 "allocating page-locked token words");
+    FX_CUDA_TRY(cudaHostGetDevicePointer(reinterpret_cast<void**>(&r->host_io_dev), r->host_io, 0),
+                "mapping the page-locked token words");
     st = initialize_state(r, token, ks, vs, rows, position, stream);
     if (st != FX_OK) return st;
     FX_CUDA_TRY(cudaEventRecord(r->done, stream), "recording setup");
@@ -849,6 +857,23 @@ fx_status create_impl(fx_decode* r, const int64_t* token, const float* const* ks
     FX_CUDA_TRY(end, "ending CUDA graph capture");
     r->graph = graph;
     FX_CUDA_TRY(cudaGraphInstantiate(&r->exec, r->graph, 0), "instantiating the decode graph");
+    if (r->persistent) {
+        // the same step also writing its token to the mapped host word
+        FX_CUDA_TRY(cudaStreamBeginCapture(r->capture_stream, cudaStreamCaptureModeThreadLocal),
+                    "beginning the host-word graph capture");
+        r->capture_active = true;
+        st = run_body(r, r->capture_stream, true);
+        cudaGraph_t host_graph = nullptr;
+        const cudaError_t host_end = cudaStreamEndCapture(r->capture_stream, &host_graph);
+        r->capture_active = false;
+        if (st != FX_OK) {
+            if (host_graph) cudaGraphDestroy(host_graph);
+            return st;
+        }
+        FX_CUDA_TRY(host_end, "ending the host-word graph capture");
+        r->graph_host = host_graph;
+        FX_CUDA_TRY(cudaGraphInstantiate(&r->exec_host, r->graph_host, 0), "instantiating the host-word graph");
+    }
     FX_CUDA_TRY(cudaStreamSynchronize(r->capture_stream), "finalizing capture");
     r->start_position = position;
     return FX_OK;
@@ -921,20 +946,25 @@ extern "C" fx_status fx_decode_replay_host(fx_decode* r, const int64_t* host_tok
     DeviceGuard guard(r->model.device);
     cudaStream_t s = as_stream(stream);
     if (r->pending) FX_CUDA_TRY(cudaStreamWaitEvent(s, r->done, 0), "ordering consecutive replays");
-    // The staging words are free: the previous call returned after its copies.
+    // The staging words are free: the previous call returned after its step.
     if (host_token != nullptr) {
         r->host_io[0] = *host_token;
         FX_CUDA_TRY(cudaMemcpyAsync(r->token(), r->host_io, sizeof(int64_t), cudaMemcpyHostToDevice, s),
                     "copying the host replay token");
     }
-    FX_CUDA_TRY(cudaGraphLaunch(r->exec, s), "launching the decode graph");
-    FX_CUDA_TRY(cudaMemcpyAsync(r->host_io + 1, r->token(), sizeof(int64_t), cudaMemcpyDeviceToHost, s),
-                "copying the sampled token to the host");
+    if (r->exec_host != nullptr) {
+        // the step stores its token to the mapped host word itself
+        FX_CUDA_TRY(cudaGraphLaunch(r->exec_host, s), "launching the decode graph");
+    } else {
+        FX_CUDA_TRY(cudaGraphLaunch(r->exec, s), "launching the decode graph");
+        FX_CUDA_TRY(cudaMemcpyAsync(r->host_io + 1, r->token(), sizeof(int64_t), cudaMemcpyDeviceToHost, s),
+                    "copying the sampled token to the host");
+    }
     FX_CUDA_TRY(cudaEventRecord(r->done, s), "recording replay completion");
     r->pending = true;
     ++r->replay_count;
     FX_CUDA_TRY(cudaEventSynchronize(r->done), "waiting for the replay");
-    *host_next = r->host_io[1];
+    *host_next = reinterpret_cast<volatile int64_t*>(r->host_io)[1];
     return FX_OK;
 }
 

@@ -730,6 +730,14 @@ __device__ __forceinline__ void argmax_take(float& bv, long long& bi, float v, l
 
 __device__ __forceinline__ size_t parity(int l) { return static_cast<size_t>(l & 1); }
 
+// The step's output token to the host-mapped word of fx_decode_replay_host
+// (system scope; the host reads it after the step has completed).
+__device__ __forceinline__ void publish_host_token(const StepArgs& a, int64_t token) {
+    if (a.host_out != nullptr)
+        asm volatile("st.relaxed.sys.global.s64 [%0], %1;" ::"l"(a.host_out), "l"(static_cast<long long>(token))
+                     : "memory");
+}
+
 // ------------------------------------------------------------------ kernel
 
 __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __grid_constant__ StepArgs a) {
@@ -739,7 +747,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = gridDim.x, cta = blockIdx.x;
 
-    if (*reinterpret_cast<volatile int*>(a.stop) != 0) return;  // generation already ended on EOS (uniform)
+    if (*reinterpret_cast<volatile int*>(a.stop) != 0) {  // generation already ended on EOS (uniform)
+        if (cta == 0 && tid == 0) publish_host_token(a, *a.token);  // the token a copy would return
+        return;
+    }
     // The schedule is uniform over the CTA and read throughout the step: it
     // lives in shared memory (as a per-thread struct it was spilled to local
     // memory, 64 KB per CTA, more than the L1 left beside the ring).
@@ -775,7 +786,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     __syncthreads();
     const Sched& s = sh.s;
     if (s.pos < 0 || s.pos >= a.capacity) {  // uniform
-        if (cta == 0 && tid == 0) atomicOr(a.error, 1);
+        if (cta == 0 && tid == 0) {
+            atomicOr(a.error, 1);
+            publish_host_token(a, *a.token);
+        }
         return;
     }
     if (cta == 0 && tid == 0) *a.length = s.pos + 1;
@@ -1412,6 +1426,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 if (lane == 0) {
                     const int64_t selected = bi < 0 ? 0 : bi;
                     *a.token = selected;
+                    publish_host_token(a, selected);
                     const int64_t st = *a.step;
                     if (st >= 0 && st < cap) a.generated[st] = selected;
                     if (a.stop[1] != 0 && selected == static_cast<int64_t>(a.stop[1]) - 1) a.stop[0] = 1;

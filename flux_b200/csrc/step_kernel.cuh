@@ -68,6 +68,11 @@ struct StepArgs {
     float* key_cache;         // [30, 3, capacity, 64]
     float* value_cache;
     int64_t* token;
+    // Host-mapped page-locked word of fx_decode_replay_host (null in the
+    // device-resident graph): the step also stores the sampled token there,
+    // so no device-to-host copy node follows it.  (Its input token still
+    // arrives by a copy: 148 CTAs reading one mapped word cost ~0.1 ms.)
+    int64_t* host_out;
     int64_t* position;
     int64_t* length;
     int64_t* step;
